@@ -1,0 +1,427 @@
+// The MoE block handle (artlite_moe_create / set_weights / forward / sync / debug / destroy): raw GGUF expert blocks
+// resident in HBM, per-handle workspaces sized for max_tokens, and the forward's kernel sequence on one stream:
+//   router (x W_r^T, fp32) -> route (ids, w) -> dispatch (offsets, perm, slot) -> experts -> combine (y).
+// The experts run on one of two paths:
+//   gemv  (path 1; decode batches): CUDA-core dequant-GEMVs, fp32 dequant and accumulation (gemv.cu);
+//   tc    (path 2; prefill): the token rows gathered into dispatch order (bf16), then tcgen05 grouped GEMMs over the
+//         raw quantised blocks dequantised in shared memory (tc_gemm.cu), h and y in bf16.
+// The order of the stages is MoEPrefill.items (src/artlite/moe/prefill.py:102-125) minus the NPU's host round trip:
+// routing and dispatch run on the GPU between the router and the experts.
+#include <cuda_runtime.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <chrono>
+#include <memory>
+#include <thread>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "tc_gemm.cuh"
+
+struct artlite_moe {
+  artlite_moe_desc d{};
+  int dev = 0;
+  cudaStream_t st = nullptr;
+  int E_local = 0, e0 = 0;  // this rank's experts [e0, e0 + E_local)
+  struct Layer {
+    artlite::DevBuf gate, up, down, router, bias;
+    bool has_bias = false;
+    int qtype = -1, down_qtype = -1, router_qtype = -1;
+    int64_t rb_gu = 0, rb_dn = 0;
+  };
+  std::vector<Layer> layers;
+  // workspaces
+  artlite::DevBuf xin, yout, logits, ids, w, offsets, perm, slot, counts, blk, unit_gu, unit_dn, status;
+  artlite::DevBuf h, y, xp, tiles;
+  int64_t last_T = 0;
+  int last_path = 0;
+  bool timing = false;
+  std::vector<cudaEvent_t> ev;  // [n_layers][kStages]: the last forward of each layer, read without a sync
+  std::vector<int> n_stages;    // per layer
+  std::vector<int> paths;       // per layer: the expert path of its last forward
+};
+
+namespace artlite {
+constexpr int kStages = 8;
+}
+
+namespace artlite {
+namespace {
+
+int choose_path(const artlite_moe& h, int64_t T, int qtype) {
+  if (h.d.path == 1 || h.d.path == 2) return h.d.path;
+  // tcgen05 for prefill-sized batches of the formats its loader reads, the GEMVs otherwise
+  if (T * h.d.top_k >= 4 * h.d.n_experts && tc_supported(qtype, h.d.hidden, h.d.expert_ffn)) return 2;
+  return 1;
+}
+
+int status_error(const DevStatus& s, int E) {
+  if (s.code == ARTLITE_EDEVICE) {
+    set_error("moe: expert id %d of %d from the routing", s.a, E);
+    return ARTLITE_EDEVICE;
+  }
+  if (s.code) {
+    set_error("moe: device status %d (%d %d %d)", s.code, s.a, s.b, s.c);
+    return s.code;
+  }
+  return ARTLITE_OK;
+}
+
+int wait(cudaStream_t st, int timeout_ms) {
+  if (timeout_ms <= 0) timeout_ms = 60000;
+  cudaEvent_t e;
+  AL_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  AL_CUDA(cudaEventRecord(e, st));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(e);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) {
+      cudaEventDestroy(e);
+      set_error("moe: %s", cudaGetErrorString(q));
+      return ARTLITE_ECUDA;
+    }
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+      cudaEventDestroy(e);
+      set_error("moe: no completion within %d ms", timeout_ms);
+      return ARTLITE_ETIMEOUT;
+    }
+    std::this_thread::yield();
+  }
+  cudaEventDestroy(e);
+  return ARTLITE_OK;
+}
+
+}  // namespace
+}  // namespace artlite
+
+using namespace artlite;
+
+extern "C" {
+#pragma GCC visibility push(default)
+
+int artlite_moe_create(const artlite_moe_desc* desc, artlite_moe** out) {
+  AL_CHECK(desc && out, ARTLITE_EINVAL, "moe_create: null argument");
+  const artlite_moe_desc& d = *desc;
+  AL_CHECK(d.hidden > 0 && d.n_experts > 0 && d.top_k >= 1 && d.top_k <= d.n_experts && d.expert_ffn > 0 &&
+               d.n_layers >= 1 && d.max_tokens >= 0 && (d.gating == 0 || d.gating == 1),
+           ARTLITE_EINVAL, "moe_create: H %d E %d K %d F %d layers %d max_tokens %d gating %d", d.hidden,
+           d.n_experts, d.top_k, d.expert_ffn, d.n_layers, d.max_tokens, d.gating);
+  AL_CHECK(d.act_dtype == ARTLITE_F32 || d.act_dtype == ARTLITE_BF16, ARTLITE_EINVAL,
+           "moe_create: act_dtype %d (F32 or BF16)", d.act_dtype);
+  AL_CHECK(d.n_experts <= 1024 && d.top_k <= 32 && d.hidden % 256 == 0 && d.expert_ffn % 256 == 0,
+           ARTLITE_EUNSUPPORTED, "moe_create: E %d K %d H %d F %d (this build: E <= 1024, K <= 32, H and F "
+           "multiples of 256)", d.n_experts, d.top_k, d.hidden, d.expert_ffn);
+  const int world = d.ep_world > 0 ? d.ep_world : 1;
+  AL_CHECK(d.ep_rank >= 0 && d.ep_rank < world && d.n_experts % world == 0, ARTLITE_EINVAL,
+           "moe_create: rank %d of %d with %d experts", d.ep_rank, world, d.n_experts);
+  AL_CHECK(world == 1, ARTLITE_EUNSUPPORTED, "moe_create: expert parallelism goes through artlite_moe_ep_* (world %d)",
+           world);
+  std::unique_ptr<artlite_moe> h(new artlite_moe);
+  h->d = d;
+  if (d.device >= 0) AL_CUDA(cudaSetDevice(d.device));
+  AL_CUDA(cudaGetDevice(&h->dev));
+  AL_CUDA(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking));
+  h->E_local = d.n_experts / world;
+  h->e0 = d.ep_rank * h->E_local;
+  h->layers.resize(d.n_layers);
+  const char* tm = getenv("ARTLITE_MOE_TIMING");
+  h->timing = tm && tm[0] == '1';
+  h->n_stages.assign(d.n_layers, 0);
+  h->paths.assign(d.n_layers, 0);
+  if (h->timing) {
+    h->ev.assign((size_t)d.n_layers * kStages, nullptr);
+    for (cudaEvent_t& e : h->ev) AL_CUDA(cudaEventCreate(&e));
+  }
+  const int64_t T = d.max_tokens > 0 ? d.max_tokens : 1, P = T * d.top_k;
+  const int H = d.hidden, E = d.n_experts, F = d.expert_ffn;
+  AL_TRY(h->logits.reserve(sizeof(float) * T * E));
+  AL_TRY(h->ids.reserve(sizeof(int32_t) * P));
+  AL_TRY(h->w.reserve(sizeof(float) * P));
+  AL_TRY(h->offsets.reserve(sizeof(int64_t) * (E + 1)));
+  AL_TRY(h->perm.reserve(sizeof(int32_t) * P));
+  AL_TRY(h->slot.reserve(sizeof(int32_t) * P));
+  AL_TRY(h->counts.reserve(sizeof(int32_t) * E));
+  AL_TRY(h->blk.reserve(dispatch_scratch_bytes(P, E)));
+  AL_TRY(h->unit_gu.reserve(sizeof(int32_t) * (E + 1)));
+  AL_TRY(h->unit_dn.reserve(sizeof(int32_t) * (E + 1)));
+  AL_TRY(h->status.reserve(sizeof(DevStatus)));
+  AL_TRY(h->tiles.reserve(tc_sched_bytes(E)));
+  // h and y hold fp32 rows (gemv) or bf16 rows (tc: at least P + 256 of them, whole 256-row token boxes)
+  AL_TRY(h->h.reserve(std::max(sizeof(float) * P * F, sizeof(uint16_t) * (P + 256) * F)));
+  AL_TRY(h->y.reserve(sizeof(float) * P * H));
+  AL_TRY(h->xp.reserve(sizeof(uint16_t) * (P + 256) * H));
+  const size_t act = d.act_dtype == ARTLITE_BF16 ? 2 : 4;
+  AL_TRY(h->xin.reserve(act * T * H));
+  AL_TRY(h->yout.reserve(act * T * H));
+  AL_CUDA(cudaMemsetAsync(h->status.ptr, 0, sizeof(DevStatus), h->st));
+  AL_CUDA(cudaStreamSynchronize(h->st));
+  *out = h.release();
+  return ARTLITE_OK;
+}
+
+int artlite_moe_set_weights(artlite_moe* h, int layer, int qtype, const void* gate, const void* up, int down_qtype,
+                            const void* down, const void* router, int router_qtype) {
+  AL_CHECK(h, ARTLITE_EINVAL, "moe_set_weights: null handle");
+  AL_CHECK(layer >= 0 && layer < (int)h->layers.size(), ARTLITE_EINVAL, "moe_set_weights: layer %d of %d", layer,
+           (int)h->layers.size());
+  AL_CHECK(gate && up && down && router, ARTLITE_EINVAL, "moe_set_weights: null tensor");
+  AL_CHECK(router_qtype == ARTLITE_F32 || router_qtype == ARTLITE_BF16, ARTLITE_EINVAL,
+           "moe_set_weights: router type %d (F32 or BF16)", router_qtype);
+  int per, bytes, per_d, bytes_d;
+  AL_TRY(qtype_block(qtype, &per, &bytes));
+  AL_TRY(qtype_block(down_qtype, &per_d, &bytes_d));
+  const artlite_moe_desc& d = h->d;
+  AL_CHECK(d.hidden % per == 0 && d.expert_ffn % per_d == 0, ARTLITE_EINVAL, "moe_set_weights: H %d / F %d and blocks "
+           "of %d / %d", d.hidden, d.expert_ffn, per, per_d);
+  AL_CUDA(cudaSetDevice(h->dev));
+  artlite_moe::Layer& L = h->layers[layer];
+  L.qtype = qtype;
+  L.down_qtype = down_qtype;
+  L.router_qtype = router_qtype;
+  L.rb_gu = (int64_t)d.hidden / per * bytes;
+  L.rb_dn = (int64_t)d.expert_ffn / per_d * bytes_d;
+  const int64_t F = d.expert_ffn, H = d.hidden;
+  const size_t gu_bytes = (size_t)(h->E_local * F * L.rb_gu), dn_bytes = (size_t)(h->E_local * H * L.rb_dn);
+  const size_t r_bytes = (size_t)d.n_experts * H * (router_qtype == ARTLITE_F32 ? 4 : 2);
+  // (64 bytes of slack past each tensor: the loaders read whole 16-byte words)
+  AL_TRY(L.gate.reserve(gu_bytes + 64));
+  AL_TRY(L.up.reserve(gu_bytes + 64));
+  AL_TRY(L.down.reserve(dn_bytes + 64));
+  AL_TRY(L.router.reserve(r_bytes));
+  const uint8_t* g8 = static_cast<const uint8_t*>(gate) + (size_t)(h->e0 * F * L.rb_gu);
+  const uint8_t* u8 = static_cast<const uint8_t*>(up) + (size_t)(h->e0 * F * L.rb_gu);
+  const uint8_t* d8 = static_cast<const uint8_t*>(down) + (size_t)(h->e0 * H * L.rb_dn);
+  AL_CUDA(cudaMemcpyAsync(L.gate.ptr, g8, gu_bytes, cudaMemcpyDefault, h->st));
+  AL_CUDA(cudaMemcpyAsync(L.up.ptr, u8, gu_bytes, cudaMemcpyDefault, h->st));
+  AL_CUDA(cudaMemcpyAsync(L.down.ptr, d8, dn_bytes, cudaMemcpyDefault, h->st));
+  AL_CUDA(cudaMemcpyAsync(L.router.ptr, router, r_bytes, cudaMemcpyDefault, h->st));
+  AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.gate.ptr) + gu_bytes, 0, 64, h->st));
+  AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.up.ptr) + gu_bytes, 0, 64, h->st));
+  AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.down.ptr) + dn_bytes, 0, 64, h->st));
+  return wait(h->st, 0);
+}
+
+int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64_t T, void* stream) {
+  AL_CHECK(h, ARTLITE_EINVAL, "moe_forward: null handle");
+  AL_CHECK(layer >= 0 && layer < (int)h->layers.size() && h->layers[layer].qtype >= 0, ARTLITE_EINVAL,
+           "moe_forward: layer %d has no weights", layer);
+  AL_CHECK(T >= 0 && T <= (h->d.max_tokens > 0 ? h->d.max_tokens : 1), ARTLITE_EINVAL,
+           "moe_forward: T %lld (max_tokens %d)", (long long)T, h->d.max_tokens);
+  AL_CHECK(T == 0 || (x && y), ARTLITE_EINVAL, "moe_forward: null x / y");
+  const artlite_moe_desc& d = h->d;
+  const artlite_moe::Layer& L = h->layers[layer];
+  const int H = d.hidden, E = d.n_experts, K = d.top_k, F = d.expert_ffn;
+  const int64_t P = T * K;
+  const size_t act = d.act_dtype == ARTLITE_BF16 ? 2 : 4;
+  AL_CUDA(cudaSetDevice(h->dev));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->st;
+  h->last_T = T;
+  if (T == 0) return ARTLITE_OK;
+  const bool x_dev = is_device_ptr(x) && ((uintptr_t)x % 16) == 0;
+  const bool y_dev = is_device_ptr(y) && ((uintptr_t)y % 16) == 0;
+  const void* xd = x;
+  if (!x_dev) {
+    AL_CUDA(cudaMemcpyAsync(h->xin.ptr, x, act * T * H, cudaMemcpyDefault, st));
+    xd = h->xin.ptr;
+  }
+  void* yd = y_dev ? y : h->yout.ptr;
+  int ns = 0;
+  auto mark = [&]() -> int {
+    if (h->timing && ns < kStages) AL_CUDA(cudaEventRecord(h->ev[(size_t)layer * kStages + ns++], st));
+    return ARTLITE_OK;
+  };
+  AL_TRY(mark());
+  // 1. router logits
+  // (kernels of this forward: router, route, 3 dispatch, then 4 (gemv) or 6 (tc), then the combine)
+  AL_TRY(launch_router(xd, d.act_dtype, L.router.ptr, L.router_qtype, L.has_bias ? L.bias.as<float>() : nullptr, T, H,
+                       E, h->logits.as<float>(), st));
+  AL_TRY(mark());
+  // 2. routing
+  RouteArgs ra{h->logits.as<float>(), T, E, E, 0, E, K, d.gating, K <= 16 && E % 16 == 0 && E <= 512,
+               h->ids.as<int32_t>(), h->w.as<float>()};
+  AL_TRY(launch_route(ra, st));
+  // 3. dispatch
+  DispatchArgs da{};
+  da.ids = h->ids.as<int32_t>();
+  da.P = P;
+  da.E = E;
+  da.blk_counts = h->blk.as<int32_t>();
+  da.offsets = h->offsets.as<int64_t>();
+  da.perm = h->perm.as<int32_t>();
+  da.slot = h->slot.as<int32_t>();
+  da.counts = h->counts.as<int32_t>();
+  da.status = h->status.as<DevStatus>();
+  AL_TRY(launch_dispatch(da, st));
+  AL_TRY(mark());
+  const int path = choose_path(*h, T, L.qtype) == 2 && tc_supported(L.down_qtype, F, H) ? 2 : 1;
+  h->last_path = path;
+  h->paths[layer] = path;
+  if (path == 1) {
+    const int rt_gu = gemv_row_tile(F), rt_dn = gemv_row_tile(H);
+    AL_TRY(launch_unit_scan(h->counts.as<int32_t>(), E, kGemvTokens, F / rt_gu, h->unit_gu.as<int32_t>(), st));
+    AL_TRY(launch_unit_scan(h->counts.as<int32_t>(), E, kGemvTokens, H / rt_dn, h->unit_dn.as<int32_t>(), st));
+    ExpertGemvArgs g{};
+    g.qtype = L.qtype;
+    g.w0 = L.gate.as<uint8_t>();
+    g.w1 = L.up.as<uint8_t>();
+    g.row_bytes = L.rb_gu;
+    g.K = H;
+    g.N = F;
+    g.E = E;
+    g.x = xd;
+    g.x_dtype = d.act_dtype;
+    g.perm = h->perm.as<int32_t>();
+    g.offsets = h->offsets.as<int64_t>();
+    g.unit_off = h->unit_gu.as<int32_t>();
+    g.rt = rt_gu;
+    g.k = K;
+    g.out = h->h.as<float>();
+    AL_TRY(launch_gemv_gu(g, st));
+    AL_TRY(mark());
+    ExpertGemvArgs dn = g;
+    dn.qtype = L.down_qtype;
+    dn.w0 = L.down.as<uint8_t>();
+    dn.w1 = nullptr;
+    dn.row_bytes = L.rb_dn;
+    dn.K = F;
+    dn.N = H;
+    dn.x = h->h.ptr;
+    dn.x_dtype = ARTLITE_F32;
+    dn.unit_off = h->unit_dn.as<int32_t>();
+    dn.rt = rt_dn;
+    dn.out = h->y.as<float>();
+    AL_TRY(launch_gemv_down(dn, st));
+    AL_TRY(mark());
+    AL_TRY(launch_combine(h->y.ptr, ARTLITE_F32, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype,
+                          st));
+  } else {
+    AL_TRY(launch_gather(xd, d.act_dtype, h->perm.as<int32_t>(), P, K, H, h->xp.as<uint16_t>(), st));
+    TcGemmArgs g{};
+    g.qtype = L.qtype;
+    g.w0 = L.gate.as<uint8_t>();
+    g.w1 = L.up.as<uint8_t>();
+    g.row_bytes = L.rb_gu;
+    g.K = H;
+    g.N = F;
+    g.E = E;
+    g.x = h->xp.as<uint16_t>();
+    g.x_rows = (int64_t)(h->xp.bytes / (sizeof(uint16_t) * H));
+    g.status = h->status.as<DevStatus>();
+    g.P = P;
+    g.offsets = h->offsets.as<int64_t>();
+    g.counts = h->counts.as<int32_t>();
+    g.sched = h->tiles.ptr;
+    g.out = h->h.as<uint16_t>();
+    AL_TRY(launch_tc_gemm(g, /*gu=*/true, st));
+    AL_TRY(mark());
+    TcGemmArgs dn = g;
+    dn.qtype = L.down_qtype;
+    dn.w0 = L.down.as<uint8_t>();
+    dn.w1 = nullptr;
+    dn.row_bytes = L.rb_dn;
+    dn.K = F;
+    dn.N = H;
+    dn.x = h->h.as<uint16_t>();
+    dn.x_rows = (int64_t)(h->h.bytes / (sizeof(uint16_t) * F));
+    dn.out = h->y.as<uint16_t>();
+    AL_TRY(launch_tc_gemm(dn, /*gu=*/false, st));
+    AL_TRY(mark());
+    AL_TRY(launch_combine(h->y.ptr, ARTLITE_BF16, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype,
+                          st));
+  }
+  AL_TRY(mark());
+  h->n_stages[layer] = ns;
+  if (!y_dev) {
+    AL_CUDA(cudaMemcpyAsync(y, yd, act * T * H, cudaMemcpyDefault, st));
+    AL_TRY(wait(st, 0));
+    DevStatus s;
+    AL_CUDA(cudaMemcpy(&s, h->status.ptr, sizeof s, cudaMemcpyDeviceToHost));
+    if (s.code) {
+      AL_CUDA(cudaMemset(h->status.ptr, 0, sizeof s));
+      return status_error(s, E);
+    }
+  }
+  return ARTLITE_OK;
+}
+
+int artlite_moe_set_router_bias(artlite_moe* h, int layer, const float* bias) {
+  AL_CHECK(h, ARTLITE_EINVAL, "moe_set_router_bias: null handle");
+  AL_CHECK(layer >= 0 && layer < (int)h->layers.size(), ARTLITE_EINVAL, "moe_set_router_bias: layer %d of %d", layer,
+           (int)h->layers.size());
+  AL_CUDA(cudaSetDevice(h->dev));
+  artlite_moe::Layer& L = h->layers[layer];
+  if (!bias) {
+    L.has_bias = false;
+    return ARTLITE_OK;
+  }
+  AL_TRY(L.bias.reserve(sizeof(float) * h->d.n_experts));
+  AL_CUDA(cudaMemcpyAsync(L.bias.ptr, bias, sizeof(float) * h->d.n_experts, cudaMemcpyDefault, h->st));
+  L.has_bias = true;
+  return wait(h->st, 0);
+}
+
+int artlite_moe_sync(artlite_moe* h, int timeout_ms) {
+  AL_CHECK(h, ARTLITE_EINVAL, "moe_sync: null handle");
+  AL_CUDA(cudaSetDevice(h->dev));
+  AL_TRY(wait(h->st, timeout_ms));
+  AL_CUDA(cudaDeviceSynchronize());
+  DevStatus s;
+  AL_CUDA(cudaMemcpy(&s, h->status.ptr, sizeof s, cudaMemcpyDeviceToHost));
+  if (s.code) {
+    AL_CUDA(cudaMemset(h->status.ptr, 0, sizeof s));
+    return status_error(s, h->d.n_experts);
+  }
+  return ARTLITE_OK;
+}
+
+int artlite_moe_debug(artlite_moe* h, float* logits, int32_t* ids, float* weights, int64_t* offsets, int32_t* perm) {
+  AL_CHECK(h, ARTLITE_EINVAL, "moe_debug: null handle");
+  AL_TRY(artlite_moe_sync(h, 0));
+  const int64_t T = h->last_T, P = T * h->d.top_k;
+  const int E = h->d.n_experts;
+  if (logits) AL_CUDA(cudaMemcpy(logits, h->logits.ptr, sizeof(float) * T * E, cudaMemcpyDefault));
+  if (ids) AL_CUDA(cudaMemcpy(ids, h->ids.ptr, sizeof(int32_t) * P, cudaMemcpyDefault));
+  if (weights) AL_CUDA(cudaMemcpy(weights, h->w.ptr, sizeof(float) * P, cudaMemcpyDefault));
+  if (offsets) AL_CUDA(cudaMemcpy(offsets, h->offsets.ptr, sizeof(int64_t) * (E + 1), cudaMemcpyDefault));
+  if (perm) AL_CUDA(cudaMemcpy(perm, h->perm.ptr, sizeof(int32_t) * P, cudaMemcpyDefault));
+  return ARTLITE_OK;
+}
+
+int artlite_moe_stage_times(artlite_moe* h, int layer, float* ms, int* n_out) {
+  AL_CHECK(h && ms && n_out, ARTLITE_EINVAL, "moe_stage_times: null argument");
+  AL_CHECK(layer >= 0 && layer < (int)h->layers.size(), ARTLITE_EINVAL, "moe_stage_times: layer %d", layer);
+  *n_out = 0;
+  const int ns = h->n_stages[layer];
+  if (!h->timing || ns < 2) return ARTLITE_OK;
+  AL_CUDA(cudaSetDevice(h->dev));
+  const cudaEvent_t* e = &h->ev[(size_t)layer * kStages];
+  AL_CUDA(cudaEventSynchronize(e[ns - 1]));
+  for (int i = 0; i + 1 < ns; i++) AL_CUDA(cudaEventElapsedTime(&ms[i], e[i], e[i + 1]));
+  *n_out = ns - 1;
+  return ARTLITE_OK;
+}
+
+int artlite_moe_path(artlite_moe* h, int layer) {
+  if (!h || layer < 0 || layer >= (int)h->layers.size()) return 0;
+  return h->paths[layer];
+}
+
+int64_t artlite_moe_launch_count(void) { return artlite::launch_count(); }
+
+int artlite_moe_destroy(artlite_moe* h) {
+  if (!h) return ARTLITE_OK;
+  cudaSetDevice(h->dev);
+  cudaStreamSynchronize(h->st);
+  for (cudaEvent_t e : h->ev)
+    if (e) cudaEventDestroy(e);
+  cudaStreamDestroy(h->st);
+  delete h;
+  return ARTLITE_OK;
+}
+
+}  // extern "C"

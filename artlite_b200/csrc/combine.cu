@@ -1,0 +1,98 @@
+// The weighted combine (CombineOperator, src/artlite/moe/gather.py:11-17,295-384): per token t,
+// out_t = sum_i w[t, i] y[slot[t k + i]] with an fp32 accumulator in slot order i = 0 .. k - 1 (deterministic), one
+// rounding to the output type; and the dispatch-order gather of the token rows for the grouped GEMM.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace artlite {
+
+namespace {
+
+__device__ __forceinline__ void load8(const void* base, int dtype, int64_t i, float* v) {
+  if (dtype == ARTLITE_BF16) {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i);
+    const float4 a = p[0], b = p[1];
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  }
+}
+
+__device__ __forceinline__ void store8(void* base, int dtype, int64_t i, const float* v) {
+  if (dtype == ARTLITE_BF16) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      w[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(base) + i) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + i);
+    p[0] = make_float4(v[0], v[1], v[2], v[3]);
+    p[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+
+}  // namespace
+
+// one CTA per token row, 8 values per thread (H % 8 == 0)
+__global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype, const int32_t* slot, const float* w,
+                                                      int64_t T, int k, int H, void* out, int out_dtype) {
+  const int64_t t = blockIdx.x;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = 0; i < k; i++) {
+      const float wi = w[t * k + i];
+      float v[8];
+      load8(y, y_dtype, (int64_t)slot[t * k + i] * H + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] = fmaf(wi, v[j], acc[j]);
+    }
+    store8(out, out_dtype, t * H + c, acc);
+  }
+}
+
+int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float* w, int64_t T, int k, int H, void* out,
+                   int out_dtype, cudaStream_t st) {
+  AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "combine: H %d (a multiple of 8)", H);
+  if (T == 0) return ARTLITE_OK;
+  combine_kernel<<<(unsigned)T, 256, 0, st>>>(y, y_dtype, slot, w, T, k, H, out, out_dtype);
+  AL_LAUNCHED();
+  return ARTLITE_OK;
+}
+
+__global__ void __launch_bounds__(256) gather_kernel(const void* x, int x_dtype, const int32_t* perm, int64_t P, int k,
+                                                     int H, uint16_t* xp) {
+  const int64_t i = blockIdx.x;
+  const int64_t t = perm[i] / k;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    if (x_dtype == ARTLITE_BF16) {
+      *reinterpret_cast<uint4*>(xp + i * H + c) =
+          *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + t * H + c);
+    } else {
+      float v[8];
+      load8(x, ARTLITE_F32, t * H + c, v);
+      store8(xp, ARTLITE_BF16, i * H + c, v);
+    }
+  }
+}
+
+int launch_gather(const void* x, int x_dtype, const int32_t* perm, int64_t P, int k, int H, uint16_t* xp,
+                  cudaStream_t st) {
+  AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "gather: H %d (a multiple of 8)", H);
+  if (P == 0) return ARTLITE_OK;
+  gather_kernel<<<(unsigned)P, 256, 0, st>>>(x, x_dtype, perm, P, k, H, xp);
+  AL_LAUNCHED();
+  return ARTLITE_OK;
+}
+
+}  // namespace artlite

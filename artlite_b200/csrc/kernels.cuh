@@ -1,0 +1,111 @@
+// Kernel argument blocks and launchers of libartlite_moe_cuda.so (one definition per .cu file).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace artlite {
+
+// ---------------------------------------------------------------- route.cu
+struct RouteArgs {
+  const float* logits;
+  int64_t n, row;
+  int per_col;
+  int64_t pitch;
+  int E, k, sigmoid, vector_shape;
+  int32_t* ids;
+  float* w;
+};
+int check_route_args(int64_t n, int per_col, int E, int k);
+int launch_route(const RouteArgs& a, cudaStream_t st);
+
+// ---------------------------------------------------------------- dispatch.cu
+// Pairs p = t k + i (P = n k) grouped by expert, stable in p. Work buffers sized by dispatch_scratch_bytes.
+struct DispatchArgs {
+  const int32_t* ids;
+  int64_t P;
+  int E;
+  // scratch (device)
+  int32_t* blk_counts;  // [nblk][E]
+  // outputs (device)
+  int64_t* offsets;     // [E + 1]
+  int32_t* perm;        // [P]
+  int32_t* slot;        // [P]
+  int32_t* counts;      // [E] pairs per expert
+  // work units per expert: ceil(count / unit_rows) * unit_mult, their exclusive scan (int32 [E + 1]); unit_rows 0: none
+  int unit_rows, unit_mult;
+  int32_t* unit_off;
+  // the compacted list of experts with pairs (int32 [E]) and their number (int32 [1]); may be null
+  int32_t* active;
+  int32_t* n_active;
+  DevStatus* status;
+};
+constexpr int kDispatchBlockPairs = 4096;
+size_t dispatch_scratch_bytes(int64_t P, int E);
+int launch_dispatch(const DispatchArgs& a, cudaStream_t st);
+
+// The reference plan's chunk deal (moe_host.cpp:256-274) from a dispatch: experts / counts / sizes / rows / pos.
+struct ChunkPlanArgs {
+  const int32_t* ids;
+  const int32_t* slot;
+  const int32_t* perm;
+  const int64_t* offsets;
+  const int32_t* chunk_off;  // [E + 1] exclusive scan of ceil(count / chunk) (a dispatch with unit_rows = chunk)
+  int64_t P;
+  int k, E, cols, cap, chunk;
+  int32_t *experts, *counts, *sizes, *rows;
+  int64_t* pos;
+  DevStatus* status;
+};
+int launch_chunk_plan(const ChunkPlanArgs& a, cudaStream_t st);
+
+// ---------------------------------------------------------------- dequant.cu
+int qtype_from_name(const char* name);
+const char* qtype_name(int qtype);
+int qtype_block(int qtype, int* per, int* bytes);  // values and bytes per block; ARTLITE_EUNSUPPORTED if unknown
+int launch_dequant_rows(int qtype, const uint8_t* raw, int64_t n, int64_t row_bytes, int64_t cols, float* out,
+                        cudaStream_t st);
+
+// ---------------------------------------------------------------- router.cu
+// logits (T x E fp32) = x (T x H, f32 or bf16) . W_r^T (E x H, f32 or bf16) (+ bias (E), if not null)
+int launch_router(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H, int E,
+                  float* logits, cudaStream_t st);
+
+// ---------------------------------------------------------------- gemv.cu (CUDA-core dequant path)
+struct ExpertGemvArgs {
+  int qtype;          // weights' GGUF type
+  const uint8_t* w0;  // gate rows (E F x rb_h) or down rows (E H x rb_f)
+  const uint8_t* w1;  // up rows (gu only)
+  int64_t row_bytes;  // bytes per weight row
+  int K;              // reduction length (H for gu, F for down)
+  int N;              // output rows per expert (F for gu, H for down)
+  int E;
+  const void* x;      // gu: the token rows (T x H, act dtype); down: h rows (P x F fp32, in dispatch order)
+  int x_dtype;
+  const int32_t* perm;     // dispatch order -> pair (gu: token = pair / k)
+  const int64_t* offsets;  // [E + 1]
+  const int32_t* unit_off; // [E + 1] items per expert, ceil(n_e / 8) * (N / rt), scanned (launch_unit_scan)
+  int rt;                  // weight rows per item (gemv_row_tile(N))
+  int k;
+  float* out;        // gu: h (P x F fp32, dispatch order); down: y (P x H fp32, dispatch order)
+};
+constexpr int kGemvTokens = 8;  // pairs per item
+int gemv_row_tile(int N);
+int launch_gemv_gu(const ExpertGemvArgs& a, cudaStream_t st);
+int launch_gemv_down(const ExpertGemvArgs& a, cudaStream_t st);
+
+// out[E + 1] = exclusive scan over experts of ceil(counts[e] / unit_rows) * mult (one CTA)
+int launch_unit_scan(const int32_t* counts, int E, int unit_rows, int mult, int32_t* out, cudaStream_t st);
+
+// ---------------------------------------------------------------- combine.cu
+// out[t] = sum_i w[t, i] y[slot[t k + i]] in slot order, fp32; out f32 or bf16. y rows are f32 (y_dtype F32) or bf16.
+int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float* w, int64_t T, int k, int H, void* out,
+                   int out_dtype, cudaStream_t st);
+
+// gather x rows into dispatch order: xp[i] = x[perm[i] / k] (bf16 out; x f32 or bf16)
+int launch_gather(const void* x, int x_dtype, const int32_t* perm, int64_t P, int k, int H, uint16_t* xp,
+                  cudaStream_t st);
+
+}  // namespace artlite

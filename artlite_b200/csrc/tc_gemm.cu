@@ -1,0 +1,501 @@
+// The prefill expert GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), reading the raw GGUF blocks.
+//
+// Per tile: 128 weight rows of one expert (the MMA's A operand, M = 128) x up to 256 of the expert's (token, slot)
+// rows in dispatch order (B, N <= 256), K in stages of 64, an fp32 accumulator in TMEM (two of 256 columns: the
+// epilogue of tile i overlaps the MMAs of tile i + 1). D = A . B^T, so the output rows are weight rows and its
+// columns tokens; the epilogue transposes on the way out.
+//   gu    A = 64 gate rows and the 64 up rows of the same features, arranged so that every epilogue warp holds 16 gate
+//         and the matching 16 up rows (TMEM lanes 32q + l: l < 16 gate feature 16q + l, l >= 16 up feature 16q + l - 16);
+//         out h[(token), f] = silu(g) u in bf16 (ref.swiglu, tests/moe/ref.py:21-24).
+//   down  A = 128 down rows; out y[(token), n] in bf16.
+// Warp roles (320 threads, one CTA per SM, persistent over a static round-robin of tiles):
+//   warp 0      TMA producer: raw weight bytes (2D tensor map over the GGUF rows, 16-bit elements, 256 K-values
+//               per stage: 144 B a row for Q4_0 / Q4_K, 272 B for Q8_0) and the token rows (bf16, 128-byte swizzle);
+//               it also allocates and frees the 512 TMEM columns.
+//   warp 1      MMA issuer: tcgen05.mma kind::f16 (bf16 x bf16 -> fp32), one thread; tcgen05.commit frees stages.
+//   warps 2-5   dequant: a thread per weight row; the row's raw bytes (one stage) into registers, then per 64 values
+//               the reference's exact fp32 decode (quant.cuh's arithmetic), rounded once to bf16, written into the A
+//               stage in the UMMA K-major 128-byte-swizzle layout; fence.proxy.async, then an mbarrier arrive.
+//   warps 6-9   epilogue: tcgen05.ld of 32 columns at a time, SwiGLU (gu) or the plain rows (down), bf16 stores.
+// Every mbarrier wait is bounded (kWaitCycles): on expiry the CTA records ARTLITE_ETIMEOUT in the status word, stops
+// issuing, lets copies and MMAs already issued land, frees its TMEM and exits.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "kernels.cuh"
+#include "quant.cuh"
+#include "tc_gemm.cuh"
+
+namespace artlite {
+namespace tc {
+
+constexpr int BM = 128, BNMAX = 256, BK = 64, KC = 256, S = 3, R = 2;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BNMAX * BK * 2;
+constexpr int kThreads = 320;
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at the B200's clocks
+
+__host__ __device__ constexpr int chunk_bytes(int qt) {  // raw bytes of 256 values of a row
+  return qt == ARTLITE_Q8_0 ? 272 : (qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_K) ? 144 : 0;
+}
+
+struct Params {
+  CUtensorMap map_w0, map_w1, map_x;
+  const int64_t* offsets;
+  const int32_t* toff;  // [E + 1] tiles per expert (ceil(n_e / 256) * MT), scanned
+  uint16_t* out;
+  DevStatus* status;
+  int E, K, N, MT;
+};
+
+struct Smem {
+  uint64_t full_a[S], full_b[S], empty[S], raw_full[R], raw_empty[R], tfull[2], tempty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// a bounded wait: false once the CTA aborted (this wait ran out, or another role's did)
+__device__ __forceinline__ bool wait(Smem* sm, uint64_t* bar, uint32_t parity, DevStatus* st, int where) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*(volatile int*)&sm->abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *(volatile int*)&sm->abort = 1;
+      report(st, ARTLITE_ETIMEOUT, where, (int)blockIdx.x, 0);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart (SBO), version 1
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major, M x N
+__device__ __forceinline__ uint32_t idesc(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct Tile {
+  int e, m;
+  int64_t row0;  // dispatch row of the tile's first token
+  int valid;     // tokens in the tile
+  int n_mma;     // MMA N: valid rounded up to 16
+};
+
+__device__ __forceinline__ Tile tile_of(const Params& p, int t) {
+  int lo = 0, hi = p.E;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (p.toff[mid] <= t) lo = mid; else hi = mid;
+  }
+  const int local = t - p.toff[lo];
+  const int j = local / p.MT;
+  Tile T;
+  T.e = lo;
+  T.m = local % p.MT;
+  const int64_t o = p.offsets[lo];
+  const int n_e = (int)(p.offsets[lo + 1] - o);
+  const int ntile = (n_e + BNMAX - 1) / BNMAX;
+  const int tile_n = (((n_e + ntile - 1) / ntile) + 15) & ~15;
+  const int start = j * tile_n;
+  T.row0 = o + start;
+  T.valid = min(n_e - start, tile_n);
+  T.n_mma = (T.valid + 15) & ~15;
+  return T;
+}
+
+// ---------------------------------------------------------------- dequant of one 64-value step into bf16 pairs
+
+__device__ __forceinline__ uint32_t byte_at(const uint32_t* w, int b) { return (w[b >> 2] >> ((b & 3) * 8)) & 0xFFu; }
+__device__ __forceinline__ float half_at(const uint32_t* w, int b) {
+  return __half2float(__ushort_as_half((unsigned short)(byte_at(w, b) | (byte_at(w, b + 1) << 8))));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// w: a row's raw bytes of one 256-value stage; o: 32 words = values 64 sub .. 64 sub + 63 as bf16 pairs
+template <int QT>
+__device__ __forceinline__ void dequant_step(const uint32_t* w, int sub, uint32_t (&o)[32]) {
+  if constexpr (QT == ARTLITE_Q4_0) {
+#pragma unroll
+    for (int bi = 0; bi < 2; bi++) {
+      const int base = 18 * (2 * sub + bi);
+      const float d = half_at(w, base);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const uint32_t b0 = byte_at(w, base + 2 + 2 * j), b1 = byte_at(w, base + 3 + 2 * j);
+        o[16 * bi + j] = pack_bf16(__fmul_rn((float)((int)(b0 & 15) - 8), d), __fmul_rn((float)((int)(b1 & 15) - 8), d));
+        o[16 * bi + 8 + j] = pack_bf16(__fmul_rn((float)((int)(b0 >> 4) - 8), d), __fmul_rn((float)((int)(b1 >> 4) - 8), d));
+      }
+    }
+  } else if constexpr (QT == ARTLITE_Q8_0) {
+#pragma unroll
+    for (int bi = 0; bi < 2; bi++) {
+      const int base = 34 * (2 * sub + bi);
+      const float d = half_at(w, base);
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const int q0 = (int)(int8_t)byte_at(w, base + 2 + 2 * j), q1 = (int)(int8_t)byte_at(w, base + 3 + 2 * j);
+        o[16 * bi + j] = pack_bf16(__fmul_rn(d, (float)q0), __fmul_rn(d, (float)q1));
+      }
+    }
+  } else {  // Q4_K: the stage is one super-block; this step its groups 2 sub (low nibbles) and 2 sub + 1 (high)
+    const float d = half_at(w, 0), dmin = half_at(w, 2);
+#pragma unroll
+    for (int hb = 0; hb < 2; hb++) {
+      const int g = 2 * sub + hb;
+      int sc, mn;
+      if (g < 4) {
+        sc = byte_at(w, 4 + g) & 63;
+        mn = byte_at(w, 8 + g) & 63;
+      } else {
+        sc = (byte_at(w, 12 + g - 4) & 15) | (byte_at(w, 4 + g - 4) >> 6) << 4;
+        mn = (byte_at(w, 12 + g - 4) >> 4) | (byte_at(w, 8 + g - 4) >> 6) << 4;
+      }
+      const float dsc = __fmul_rn(d, (float)sc), dmn = __fmul_rn(dmin, (float)mn);
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const uint32_t b0 = byte_at(w, 16 + 32 * sub + 2 * j), b1 = byte_at(w, 17 + 32 * sub + 2 * j);
+        const int q0 = hb ? (int)(b0 >> 4) : (int)(b0 & 15), q1 = hb ? (int)(b1 >> 4) : (int)(b1 & 15);
+        o[16 * hb + j] = pack_bf16(__fsub_rn(__fmul_rn((float)q0, dsc), dmn), __fsub_rn(__fmul_rn((float)q1, dsc), dmn));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- the kernel
+
+template <int QT, bool GU>
+__global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_constant__ Params p) {
+  constexpr int CB = chunk_bytes(QT);
+  constexpr int NW = CB / 4;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = base;
+  uint8_t* sB = sA + S * A_BYTES;
+  uint8_t* sR = sB + S * B_BYTES;
+  Smem* sm = reinterpret_cast<Smem*>(sR + R * BM * CB);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = p.toff[p.E];
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; i++) {
+      mbar_init(&sm->full_a[i], 4);
+      mbar_init(&sm->full_b[i], 1);
+      mbar_init(&sm->empty[i], 1);
+    }
+    for (int i = 0; i < R; i++) {
+      mbar_init(&sm->raw_full[i], 1);
+      mbar_init(&sm->raw_empty[i], 4);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&sm->tfull[i], 1);
+      mbar_init(&sm->tempty[i], 4);
+    }
+    sm->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm->tmem_base)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = sm->tmem_base;
+  const int ksteps = p.K / BK;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- producer
+    int s = 0, sph = 0, r = 0, rph = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const Tile T = tile_of(p, t);
+      for (int kc = 0; kc < p.K / KC; kc++) {
+        if (!wait(sm, &sm->raw_empty[r], rph ^ 1, p.status, 1)) goto out;
+        uint8_t* dst = sR + r * BM * CB;
+        mbar_expect_tx(&sm->raw_full[r], BM * CB);
+        if (GU) {
+          const int row = T.e * p.N + 64 * T.m;
+          tma_load_2d(dst, &p.map_w0, &sm->raw_full[r], kc * (CB / 2), row);
+          tma_load_2d(dst + 64 * CB, &p.map_w1, &sm->raw_full[r], kc * (CB / 2), row);
+        } else {
+          tma_load_2d(dst, &p.map_w0, &sm->raw_full[r], kc * (CB / 2), T.e * p.N + BM * T.m);
+        }
+        if (++r == R) r = 0, rph ^= 1;
+        for (int sub = 0; sub < KC / BK; sub++) {
+          if (!wait(sm, &sm->empty[s], sph ^ 1, p.status, 2)) goto out;
+          mbar_expect_tx(&sm->full_b[s], B_BYTES);
+          tma_load_2d(sB + s * B_BYTES, &p.map_x, &sm->full_b[s], kc * KC + sub * BK, (int)T.row0);
+          if (++s == S) s = 0, sph ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    int s = 0, sph = 0, acc = 0, aph = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const Tile T = tile_of(p, t);
+      if (!wait(sm, &sm->tempty[acc], aph ^ 1, p.status, 3)) goto out;
+      fence_after();
+      const uint32_t id = idesc(BM, T.n_mma);
+      const uint32_t d = tmem + acc * BNMAX;
+      for (int ks = 0; ks < ksteps; ks++) {
+        if (!wait(sm, &sm->full_a[s], sph, p.status, 4)) goto out;
+        if (!wait(sm, &sm->full_b[s], sph, p.status, 5)) goto out;
+        fence_after();
+        const uint64_t da = sdesc(smem_u32(sA + s * A_BYTES)), db = sdesc(smem_u32(sB + s * B_BYTES));
+#pragma unroll
+        for (int k = 0; k < BK / 16; k++) mma(d, da + 2 * k, db + 2 * k, id, (ks | k) != 0);
+        commit(&sm->empty[s]);
+        if (++s == S) s = 0, sph ^= 1;
+      }
+      commit(&sm->tfull[acc]);
+      if (++acc == 2) acc = 0, aph ^= 1;
+    }
+  } else if (warp >= 2 && warp < 6) {
+    // ---------------- dequant: thread i owns A row i
+    const int i = threadIdx.x - 64;
+    int raw_row = i;
+    if (GU) {
+      const int q = i >> 5, l = i & 31;
+      raw_row = l < 16 ? 16 * q + l : 64 + 16 * q + (l - 16);
+    }
+    int s = 0, sph = 0, r = 0, rph = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      for (int kc = 0; kc < p.K / KC; kc++) {
+        if (!wait(sm, &sm->raw_full[r], rph, p.status, 6)) goto out;
+        uint32_t w[NW];
+        const uint4* src = reinterpret_cast<const uint4*>(sR + r * BM * CB + raw_row * CB);
+#pragma unroll
+        for (int v = 0; v < NW / 4; v++) {
+          const uint4 u = src[v];
+          w[4 * v] = u.x, w[4 * v + 1] = u.y, w[4 * v + 2] = u.z, w[4 * v + 3] = u.w;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm->raw_empty[r]);
+        if (++r == R) r = 0, rph ^= 1;
+#pragma unroll
+        for (int sub = 0; sub < KC / BK; sub++) {
+          uint32_t o[32];
+          dequant_step<QT>(w, sub, o);
+          if (!wait(sm, &sm->empty[s], sph ^ 1, p.status, 7)) goto out;
+          uint8_t* row = sA + s * A_BYTES + i * 128;
+#pragma unroll
+          for (int c = 0; c < 8; c++)
+            *reinterpret_cast<uint4*>(row + ((c ^ (i & 7)) << 4)) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm->full_a[s]);
+          if (++s == S) s = 0, sph ^= 1;
+        }
+      }
+    }
+  } else if (warp >= 6) {
+    // ---------------- epilogue: TMEM lanes 32 q .. 32 q + 31
+    const int q = warp & 3;
+    int acc = 0, aph = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const Tile T = tile_of(p, t);
+      if (!wait(sm, &sm->tfull[acc], aph, p.status, 8)) goto out;
+      fence_after();
+      for (int c0 = 0; c0 < T.n_mma; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + acc * BNMAX + c0, v);
+        if (GU) {
+          const bool gate = lane < 16;
+          const int f = 64 * T.m + 16 * q + (lane & 15);
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const float mine = __uint_as_float(gate ? v[j] : v[16 + j]);
+            const float send = __uint_as_float(gate ? v[16 + j] : v[j]);
+            const float other = __shfl_xor_sync(0xFFFFFFFFu, send, 16);
+            const float g = gate ? mine : other, u = gate ? other : mine;
+            const int tok = c0 + j + (gate ? 0 : 16);
+            if (tok < T.valid) {
+              const float h = __fdividef(g, 1.0f + __expf(-g)) * u;
+              p.out[(T.row0 + tok) * p.N + f] = __bfloat16_as_ushort(__float2bfloat16_rn(h));
+            }
+          }
+        } else {
+          const int n = BM * T.m + 32 * q + lane;
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            if (c0 + j < T.valid)
+              p.out[(T.row0 + c0 + j) * p.N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j])));
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm->tempty[acc]);
+      if (++acc == 2) acc = 0, aph ^= 1;
+    }
+  }
+out:
+  __syncwarp();
+  __syncthreads();
+  if (*(volatile int*)&sm->abort && threadIdx.x == 0) {  // let issued copies and MMAs land before TMEM is freed
+    const long long t0 = clock64();
+    while (clock64() - t0 < 20000000LL) {
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+}  // namespace tc
+
+// ---------------------------------------------------------------- host side
+
+namespace {
+
+typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  }
+  return fn;
+}
+
+// a 2D map over rows x row_bytes of 16-bit elements (raw GGUF bytes or bf16 values)
+int make_map(CUtensorMap* m, const void* base, int64_t row_elems, int64_t rows, int box_x, int box_y, bool swizzle) {
+  EncodeTiled enc = encode_fn();
+  AL_CHECK(enc, ARTLITE_ECUDA, "tc gemm: cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)row_elems, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(row_elems * 2)};
+  const cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_y};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, swizzle ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
+                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  AL_CHECK(r == CUDA_SUCCESS, ARTLITE_ECUDA, "tc gemm: cuTensorMapEncodeTiled failed (%d): %lld x %lld box %d x %d",
+           (int)r, (long long)row_elems, (long long)rows, box_x, box_y);
+  return ARTLITE_OK;
+}
+
+}  // namespace
+
+bool tc_supported(int qtype, int K, int N) {
+  return tc::chunk_bytes(qtype) > 0 && K % tc::KC == 0 && N % tc::BM == 0;
+}
+
+size_t tc_sched_bytes(int E) { return sizeof(int32_t) * (E + 1); }
+
+int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
+  AL_CHECK(tc_supported(a.qtype, a.K, a.N), ARTLITE_EUNSUPPORTED, "tc gemm: type %d K %d N %d", a.qtype, a.K, a.N);
+  AL_CHECK(a.row_bytes % 16 == 0 && a.row_bytes == (int64_t)a.K / tc::KC * tc::chunk_bytes(a.qtype), ARTLITE_EINVAL,
+           "tc gemm: row bytes %lld", (long long)a.row_bytes);
+  AL_CHECK(((uintptr_t)a.w0 % 16) == 0 && (!gu || ((uintptr_t)a.w1 % 16) == 0) && ((uintptr_t)a.x % 16) == 0,
+           ARTLITE_EINVAL, "tc gemm: unaligned operand");
+  AL_CHECK(a.x_rows >= a.P + tc::BNMAX, ARTLITE_EINVAL, "tc gemm: x holds %lld rows, needs %lld", (long long)a.x_rows,
+           (long long)(a.P + tc::BNMAX));
+  if (a.P == 0) return ARTLITE_OK;
+  const int MT = gu ? a.N / 64 : a.N / tc::BM;
+  tc::Params p{};
+  const int cb = tc::chunk_bytes(a.qtype);
+  const int64_t wrows = (int64_t)a.E * a.N;
+  AL_TRY(make_map(&p.map_w0, a.w0, a.row_bytes / 2, wrows, cb / 2, gu ? 64 : tc::BM, false));
+  if (gu) AL_TRY(make_map(&p.map_w1, a.w1, a.row_bytes / 2, wrows, cb / 2, 64, false));
+  else p.map_w1 = p.map_w0;
+  AL_TRY(make_map(&p.map_x, a.x, a.K, a.x_rows, tc::BK, tc::BNMAX, true));
+  AL_TRY(launch_unit_scan(a.counts, a.E, tc::BNMAX, MT, static_cast<int32_t*>(a.sched), st));
+  p.offsets = a.offsets;
+  p.toff = static_cast<const int32_t*>(a.sched);
+  p.out = a.out;
+  p.status = a.status;
+  p.E = a.E;
+  p.K = a.K;
+  p.N = a.N;
+  p.MT = MT;
+  const size_t smem = 1024 + tc::S * (tc::A_BYTES + tc::B_BYTES) + tc::R * tc::BM * cb + sizeof(tc::Smem) + 64;
+  int dev, sms;
+  AL_CUDA(cudaGetDevice(&dev));
+  AL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  auto go = [&](auto kern) -> int {
+    AL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<sms, tc::kThreads, smem, st>>>(p);
+    AL_LAUNCHED();
+    return ARTLITE_OK;
+  };
+  switch (a.qtype) {
+    case ARTLITE_Q4_0: return gu ? go(tc::tc_expert_gemm<ARTLITE_Q4_0, true>) : go(tc::tc_expert_gemm<ARTLITE_Q4_0, false>);
+    case ARTLITE_Q8_0: return gu ? go(tc::tc_expert_gemm<ARTLITE_Q8_0, true>) : go(tc::tc_expert_gemm<ARTLITE_Q8_0, false>);
+    case ARTLITE_Q4_K: return gu ? go(tc::tc_expert_gemm<ARTLITE_Q4_K, true>) : go(tc::tc_expert_gemm<ARTLITE_Q4_K, false>);
+    default: break;
+  }
+  set_error("tc gemm: type %d", a.qtype);
+  return ARTLITE_EUNSUPPORTED;
+}
+
+}  // namespace artlite

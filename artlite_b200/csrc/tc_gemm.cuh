@@ -1,0 +1,35 @@
+// The tcgen05 grouped expert GEMM (tc_gemm.cu): declarations.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace artlite {
+
+struct TcGemmArgs {
+  int qtype;              // the weights' GGUF type (Q4_0, Q8_0, Q4_K)
+  const uint8_t* w0;      // gu: gate rows (E F x row_bytes); down: down rows (E H x row_bytes)
+  const uint8_t* w1;      // gu: up rows
+  int64_t row_bytes;
+  int K;                  // reduction (gu: H, down: F)
+  int N;                  // weight rows per expert (gu: F, down: H)
+  int E;
+  const uint16_t* x;      // bf16 rows in dispatch order (gu: gathered tokens, P x H; down: h, P x F)
+  int64_t x_rows;         // rows the x buffer holds (>= P + 256: the token tiles read whole 256-row boxes)
+  int64_t P;
+  const int64_t* offsets; // [E + 1]
+  const int32_t* counts;  // [E]
+  void* sched;            // tc_sched_bytes(E) of device scratch (the tile scan)
+  uint16_t* out;          // bf16 rows in dispatch order (gu: h, P x F; down: y, P x H)
+  DevStatus* status;
+};
+
+// whether the tcgen05 path reads this type at these shapes (K, N multiples of 256 / 128)
+bool tc_supported(int qtype, int K, int N);
+size_t tc_sched_bytes(int E);
+int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st);
+
+}  // namespace artlite

@@ -1,0 +1,111 @@
+"""The whole GGUF MoE block on the GPU: router logits, routing, dispatch, SwiGLU experts read from the raw GGUF blocks,
+the weighted combine (``artlite_moe_create`` / ``set_weights`` / ``forward``, include/artlite_moe.h).
+
+The block the reference composes from ``MoEPrefill.items`` with its host steps (src/artlite/moe/prefill.py:102-195)
+and defines in its oracle (``ref.moe_route`` + ``ref.moe_ffn``, tests/moe/ref.py:11-52), as one object. Host side:
+NumPy + ctypes; activations are fp32 or bf16 (NumPy uint16 bit patterns); the GGUF tensors are passed as their raw
+bytes (``GGUFFile.tensor(name).raw`` views, or ``artlite_b200.gguf``'s) and copied to HBM verbatim."""
+
+import ctypes
+
+import numpy as np
+
+from .._lib import QTYPES, Error, MoeDesc, check, lib
+
+PATHS = {"auto": 0, "gemv": 1, "tc": 2}
+
+
+def _ptr(a) -> int:
+    """A host array's address, or a device address given as an int / an object with ``data_ptr()``."""
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    if isinstance(a, int):
+        return a
+    if hasattr(a, "data_ptr"):
+        return int(a.data_ptr())
+    raise TypeError(type(a))
+
+
+class MoEBlock:
+    """``n_layers`` MoE blocks of one shape (a stack, each with its own weights) on one CUDA device.
+
+    ``act_dtype``: "f32" (x / y float32) or "bf16" (x / y uint16 bf16 bits); ``path``: "auto" (tcgen05 grouped GEMMs
+    for prefill-sized batches, the dequant-GEMVs for decode batches), "gemv" or "tc"."""
+
+    def __init__(self, *, hidden: int, n_experts: int, top_k: int, expert_ffn: int, max_tokens: int,
+                 n_layers: int = 1, gating: str = "softmax", act_dtype: str = "bf16", device: int = -1,
+                 path: str = "auto"):
+        assert gating in ("softmax", "sigmoid") and act_dtype in ("f32", "bf16") and path in PATHS
+        self.H, self.E, self.K, self.F = hidden, n_experts, top_k, expert_ffn
+        self.act = act_dtype
+        self.max_tokens = max_tokens
+        d = MoeDesc(hidden=hidden, n_experts=n_experts, top_k=top_k, expert_ffn=expert_ffn, n_layers=n_layers,
+                    gating=int(gating == "sigmoid"), act_dtype=QTYPES["BF16" if act_dtype == "bf16" else "F32"],
+                    max_tokens=max_tokens, device=device, path=PATHS[path], ep_rank=0, ep_world=1)
+        h = ctypes.c_void_p()
+        check(lib().artlite_moe_create(ctypes.byref(d), ctypes.byref(h)))
+        self._h = h
+
+    @property
+    def np_dtype(self):
+        return np.uint16 if self.act == "bf16" else np.float32
+
+    def set_weights(self, layer: int, *, gate, up, down, router, qtype: str, down_qtype: str | None = None,
+                    router_qtype: str = "F32") -> None:
+        """Layer ``layer``'s raw GGUF tensors (blk.L.ffn_gate_exps / ffn_up_exps / ffn_down_exps / ffn_gate_inp)."""
+        keep = [np.ascontiguousarray(a) if isinstance(a, np.ndarray) else a for a in (gate, up, down, router)]
+        check(lib().artlite_moe_set_weights(self._h, layer, QTYPES[qtype], _ptr(keep[0]), _ptr(keep[1]),
+                                            QTYPES[down_qtype or qtype], _ptr(keep[2]), _ptr(keep[3]),
+                                            QTYPES[router_qtype]))
+
+    def set_router_bias(self, layer: int, bias: np.ndarray | None) -> None:
+        """A per-expert bias added to the router logits (None: none)."""
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        check(lib().artlite_moe_set_router_bias(self._h, layer, None if b is None else b.ctypes.data))
+
+    def forward(self, x: np.ndarray, layer: int = 0, out: np.ndarray | None = None) -> np.ndarray:
+        """y (T, H) of x (T, H) (host arrays: the call returns when y is back)."""
+        x = np.ascontiguousarray(x, self.np_dtype)
+        T = x.shape[0]
+        if x.shape[1] != self.H:
+            raise Error(f"moe_forward: x has {x.shape[1]} columns, H is {self.H}")
+        y = out if out is not None else np.empty((T, self.H), self.np_dtype)
+        check(lib().artlite_moe_forward(self._h, layer, x.ctypes.data, y.ctypes.data, T, None))
+        return y
+
+    def forward_ptr(self, x, y, T: int, layer: int = 0, stream: int = 0) -> None:
+        """The forward on device (or pinned host) buffers given by address; enqueued on ``stream`` (0: the block's)."""
+        check(lib().artlite_moe_forward(self._h, layer, _ptr(x), _ptr(y), T, ctypes.c_void_p(stream or None)))
+
+    def sync(self, timeout_ms: int = 0) -> None:
+        check(lib().artlite_moe_sync(self._h, timeout_ms))
+
+    def debug(self, T: int) -> dict[str, np.ndarray]:
+        """The last forward's logits, routing and dispatch (T: its tokens)."""
+        out = {"logits": np.empty((T, self.E), np.float32), "ids": np.empty((T, self.K), np.int32),
+               "w": np.empty((T, self.K), np.float32), "offsets": np.empty(self.E + 1, np.int64),
+               "perm": np.empty(T * self.K, np.int32)}
+        check(lib().artlite_moe_debug(self._h, *(out[k].ctypes.data for k in ("logits", "ids", "w", "offsets",
+                                                                              "perm"))))
+        return out
+
+    def stage_times(self, layer: int = 0) -> list[float]:
+        """Layer ``layer``'s per-stage device times (ms) of its last forward (ARTLITE_MOE_TIMING=1 at creation)."""
+        ms = (ctypes.c_float * 16)()
+        n = ctypes.c_int()
+        check(lib().artlite_moe_stage_times(self._h, layer, ms, ctypes.byref(n)))
+        return list(ms[:n.value])
+
+    def path(self, layer: int = 0) -> str:
+        return {0: "none", 1: "gemv", 2: "tc"}[lib().artlite_moe_path(self._h, layer)]
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().artlite_moe_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

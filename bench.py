@@ -1,0 +1,359 @@
+"""MoE-layer tokens/s of the GGUF MoE block on B200 (a 48-layer stack of Qwen3-30B-A3B-shape
+blocks, H=2048, E=128, top-8, F=768, Q4_0 weights, 16384 tokens), and the CPU reference arm.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one forward of every layer of the stack over the step's token batch (the layers are independent blocks,
+each with its own weights, all fed the same batch: the synthetic random weights would overflow bf16 through a chained
+stack without the model's norms). value = tokens x layers / second over all ranks ("MoE-layer tokens/s").
+
+Our arm: weights are generated on the GPU (seeded torch CUDA generator: fp16 d from |N(0, 0.02)|, nibbles uniform;
+router fp32 N(0, 0.02); x bf16 N(0, 1)) and handed to the library as raw GGUF blocks; inputs resident in HBM before
+the timed region; the weights stream from HBM each layer (340 MB a layer, far above the 126 MB L2, so no L2 flush is
+needed). The timed region: W untimed steps, then K steps between CUDA events on the launching stream, a barrier and
+a synchronize on both sides, the max over ranks. `e2e`: the same steps through the C ABI with pinned HOST x / y buffers
+(the library copies x in and y out on every call, inside the timed region). With N > 1 every rank runs the whole stack
+on its own batch (experts replicated, no collective): weak scaling.
+
+`roofline`: the dominant kernel (the tcgen05 gate/up GEMM), its algorithmic FLOPs per launch (2 P H 2F, P = T K pairs)
+over its average duration from CUDA events recorded between the forward's kernels on the forward's stream during the
+timed steps, against the measured dense bf16 peak (MEASURED_PEAKS.json, sustained: a kernel inside a long step).
+`cpu_baseline`: the reference's CPU path (its NumPy moe_ffn restated in oracle/moe_np.py, its compiled dequant_rows
+and moe_route from oracle/_ref when they load here, else the C restatement) on a bounded token sample of one layer.
+
+--impl reference: that CPU path alone, as the reference arm (rank 0; other ranks exit 0)."""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+H, E, K, F = 2048, 128, 8, 768
+LAYERS, TOKENS, QTYPE = 48, 16384, "Q4_0"
+METRIC = "MoE-layer tokens/s, Qwen3-30B-A3B shape Q4_0, 1/2/4/8 B200; % of roofline"
+UNIT = "tokens/s"
+WORKLOAD = "qwen3-30b-a3b-moe-stack48-q4_0-t16384"
+
+
+def measured_peaks() -> tuple[dict, str]:
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------- clocks during the timed region
+
+REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+           0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+           0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class Clocks:
+    def __init__(self, gpu: int):
+        self.gpu, self.proc, self.lines = gpu, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], 0, set()
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 3:
+                continue
+            try:
+                s, m, r = float(parts[0]), float(parts[1]), int(parts[2], 16)
+            except ValueError:
+                continue
+            sm.append(s)
+            mx = max(mx, m)
+            for bit, name in REASONS.items():
+                if r & bit and name != "gpu_idle":
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- the CPU reference path
+
+def cpu_reference_sample(T: int, seed: int = 0) -> dict:
+    """The reference's CPU path on T tokens of one layer: (routing, moe_ffn) timed; returns tokens/s and what ran."""
+    from oracle import lib as olib
+    from oracle import moe_np
+
+    ref = olib.reference()
+    impl = ref if ref is not None else olib.oracle()
+    kind = "reference" if ref is not None else "port"
+    layer, x, _ = moe_np.make_block(seed, T, qtype=QTYPE, H=H, E=E, F=F)
+    xf = moe_np.bf16_to_f32(x)
+
+    def expert(e: int):
+        return (impl.dequant_rows(QTYPE, layer.gate[e * F:(e + 1) * F], H),
+                impl.dequant_rows(QTYPE, layer.up[e * F:(e + 1) * F], H),
+                impl.dequant_rows(QTYPE, layer.down[e * H:(e + 1) * H], F))
+
+    t0 = time.perf_counter()
+    logits = xf @ layer.router.T
+    ids, w = impl.route(logits, K)
+    moe_np.moe_ffn(xf, ids, w, expert)
+    dt = time.perf_counter() - t0
+    return {"seconds": dt, "tokens": T, "kind": kind, "cores": os.cpu_count()}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    T = args.cpu_tokens
+    for _ in range(args.warmup):
+        cpu_reference_sample(T, seed=1)
+    times = []
+    for s in range(args.steps):
+        r = cpu_reference_sample(T, seed=2 + s)
+        times.append(r["seconds"])
+    ms = 1000.0 * float(np.mean(times))
+    value = T / (ms / 1000.0)  # one layer per step
+    sample = f"{T} tokens x 1 layer of the workload per step (router, routing, moe_ffn with the dequant of the " \
+             f"experts they touch); numpy BLAS and the reference's dequant threads on all host cores"
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy: oracle.moe_np.make_block)",
+            "config": {"workload": WORKLOAD, "tokens_per_step": T, "layers_per_step": 1, "hidden": H, "experts": E,
+                       "top_k": K, "expert_ffn": F, "qtype": QTYPE},
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": r["cores"], "kind": r["kind"], "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+
+def gen_layer(torch, g, dev):
+    """One layer's raw Q4_0 tensors on the GPU: gate / up (E F rows of H), down (E H rows of F), router (E, H) fp32."""
+    def q4_0(rows, cols):
+        n = cols // 32
+        raw = torch.empty((rows, n, 18), dtype=torch.uint8, device=dev)
+        d = (torch.randn((rows, n), generator=g, device=dev) * 0.02).abs().half()
+        raw[..., 0:2] = d.view(torch.uint8).view(rows, n, 2)
+        raw[..., 2:] = torch.randint(0, 256, (rows, n, 16), dtype=torch.uint8, generator=g, device=dev)
+        return raw.view(rows, n * 18)
+
+    router = torch.randn((E, H), generator=g, device=dev) * 0.02
+    return q4_0(E * F, H), q4_0(E * F, H), q4_0(E * H, F), router
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--cpu-tokens", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    os.environ["ARTLITE_MOE_TIMING"] = "1"  # per-stage CUDA events between the forward's kernels (no syncs)
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+
+    from artlite_b200 import _lib
+    from artlite_b200.moe.block import MoEBlock
+
+    L, T = args.layers, args.tokens
+    block = MoEBlock(hidden=H, n_experts=E, top_k=K, expert_ffn=F, max_tokens=T, n_layers=L, act_dtype="bf16",
+                     device=local, path="auto")
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    for layer in range(L):
+        gate, up, down, router = gen_layer(torch, g, dev)
+        block.set_weights(layer, gate=gate.data_ptr(), up=up.data_ptr(), down=down.data_ptr(),
+                          router=router.data_ptr(), qtype=QTYPE)
+        del gate, up, down, router
+    torch.cuda.empty_cache()
+    x = (torch.randn((T, H), generator=g, device=dev)).to(torch.bfloat16)
+    ys = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for layer in range(L):
+            block.forward_ptr(x.data_ptr(), ys[layer & 1].data_ptr(), T, layer=layer, stream=stream.cuda_stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    launches0 = _lib.lib().artlite_moe_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = _lib.lib().artlite_moe_launch_count() - launches0
+    barrier()
+    torch.cuda.synchronize()
+    ms_total = e0.elapsed_time(e1)
+    # per-stage times of every layer's forward in the last timed step (events on the forward's stream)
+    stages = np.array([block.stage_times(layer) for layer in range(L)])
+    path = block.path(0)
+    clk = clocks.stop()
+    t_max = torch.tensor([ms_total], device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms_total = float(t_max.item())
+    ms_step = ms_total / args.steps
+    value = world * T * L / (ms_step / 1000.0)
+
+    # e2e: the C ABI with pinned host x / y (copies inside the timed region)
+    e2e = None
+    if not args.no_e2e:
+        xh = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+        xh.copy_(x.cpu())
+        yh = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+
+        def step_host():
+            for layer in range(L):
+                block.forward_ptr(xh.data_ptr(), yh.data_ptr(), T, layer=layer, stream=stream.cuda_stream)
+
+        step_host()
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        n_e2e = max(1, min(args.steps, 3))
+        for _ in range(n_e2e):
+            step_host()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) * 1000.0 / n_e2e
+        dev_ms = ev0.elapsed_time(ev1) / n_e2e
+        e_ms = torch.tensor([max(wall, dev_ms)], device=dev)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e_ms = float(e_ms.item())
+        e2e = {"value": world * T * L / (e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": L * T * H * 2,
+               "d2h_bytes_per_step": L * T * H * 2, "ms_per_step": e_ms}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    peaks, peak_src = measured_peaks()
+    # stages (tc path): router, route+dispatch, gather + gate/up, down, combine
+    roof = None
+    if path == "tc" and stages.shape[1] >= 4:
+        gu_ms = float(stages[:, 2].mean())
+        P = T * K
+        flops = 2.0 * P * H * (2 * F)
+        achieved = flops / (gu_ms / 1000.0) / 1e12
+        peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+        roof = {"kernel": "tc_expert_gemm<Q4_0, gate/up> (+ the dispatch gather, same stage)", "bound": "tensor",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": traffic_from_profiles(), "peak_source": f"{peak_src} bf16_tflops_sustained",
+                "flops_per_launch": flops, "ms_per_launch": gu_ms}
+    stage_names = ["router", "route+dispatch", "gather+gate_up", "down", "combine"] if path == "tc" else \
+        ["router", "route+dispatch", "gate_up", "down", "combine"]
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_tokens)
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded torch CUDA generator: Q4_0 d=|N(0,0.02)| fp16, nibbles uniform; x bf16 N(0,1))",
+            "config": {"workload": WORKLOAD, "layers": L, "tokens_per_rank": T, "hidden": H, "experts": E, "top_k": K,
+                       "expert_ffn": F, "qtype": QTYPE, "path": path,
+                       "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (340 MB of weights streamed per layer)"},
+            "stage_ms_mean": dict(zip(stage_names, [float(v) for v in stages.mean(0)])),
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clk}
+    print(json.dumps(line), flush=True)
+    block.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def traffic_from_profiles():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if there is one."""
+    p = os.path.join(REPO, "profiles", "tc_expert_gemm_gu_q4_0.md")
+    if not os.path.exists(p):
+        return None
+    for ln in open(p):
+        if ln.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(ln.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_baseline(T: int) -> dict:
+    """The reference's CPU path on a bounded sample (about 10-30 s of CPU work)."""
+    t0 = time.perf_counter()
+    secs, toks, r = 0.0, 0, None
+    i = 0
+    while time.perf_counter() - t0 < 10.0 or i < 2:
+        r = cpu_reference_sample(T, seed=50 + i)
+        if i > 0:  # (the first sample warms the caches)
+            secs += r["seconds"]
+            toks += r["tokens"]
+        i += 1
+        if time.perf_counter() - t0 > 30.0:
+            break
+    return {"value": toks / secs, "unit": UNIT, "cores": r["cores"], "kind": r["kind"],
+            "sample": f"{i - 1} samples of {T} tokens x 1 layer (router, routing, moe_ffn with the dequant of the "
+                      f"experts they touch), numpy BLAS on all cores, the reference's dequant threads"}
+
+
+if __name__ == "__main__":
+    main()

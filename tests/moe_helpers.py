@@ -1,0 +1,49 @@
+"""Helpers of the block tests: synthetic layers (oracle.moe_np), the oracle's y for the GPU's own routing."""
+
+import numpy as np
+
+from oracle import lib as olib
+from oracle import moe_np
+
+_ORC = None
+
+
+def orc():
+    global _ORC
+    if _ORC is None:
+        _ORC = olib.oracle()
+    return _ORC
+
+
+def expert_fn(layer: moe_np.Layer):
+    """expert(e) -> fp32 (gate, up, down) by the C oracle's dequant (bit-identical to the reference's)."""
+    o = orc()
+    F, H = layer.F, layer.H
+
+    def get(e: int):
+        return (o.dequant_rows(layer.qtype, layer.gate[e * F:(e + 1) * F], H),
+                o.dequant_rows(layer.qtype, layer.up[e * F:(e + 1) * F], H),
+                o.dequant_rows(layer.qtype, layer.down[e * H:(e + 1) * H], F))
+    return get
+
+
+def x_f32(x: np.ndarray) -> np.ndarray:
+    return moe_np.bf16_to_f32(x) if x.dtype == np.uint16 else np.asarray(x, np.float32)
+
+
+def oracle_y(layer: moe_np.Layer, x: np.ndarray, ids: np.ndarray, w: np.ndarray, tokens=None) -> np.ndarray:
+    """ref.moe_ffn's y (fp32) of the tokens (all, or the given subset) under the routing (ids, w)."""
+    xf = x_f32(x)
+    if tokens is not None:
+        xf, ids, w = xf[tokens], ids[tokens], w[tokens]
+    return moe_np.moe_ffn(xf, ids, w, expert_fn(layer))
+
+
+def make_block(layer: moe_np.Layer, T: int, *, act: str, path: str, gating: str = "softmax", n_layers: int = 1,
+               top_k: int = 8):
+    from artlite_b200.moe.block import MoEBlock
+    b = MoEBlock(hidden=layer.H, n_experts=layer.E, top_k=top_k, expert_ffn=layer.F, max_tokens=T, act_dtype=act,
+                 path=path, gating=gating, n_layers=n_layers)
+    for L in range(n_layers):
+        b.set_weights(L, gate=layer.gate, up=layer.up, down=layer.down, router=layer.router, qtype=layer.qtype)
+    return b

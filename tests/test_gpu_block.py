@@ -1,0 +1,143 @@
+"""GPU parity of the whole block (router -> routing -> dispatch -> SwiGLU experts from raw GGUF blocks -> combine)
+through the C ABI (artlite_b200.moe.block.MoEBlock), against the oracle: the reference's ref.moe_ffn restated in NumPy
+with the reference-exact fp32 dequant (tests/moe_helpers.py), under the routing the oracle computes from the GPU's own
+logits (which must equal the GPU's routing bit for bit).
+
+Tolerances (max relative error rel_max = max|a - b| / max|b|, tests/numerics.py:50-53):
+  - fp32 path (the dequant-GEMVs: fp32 dequant, fp32 accumulation, fp32 x and y): rel_max <= 2e-3;
+  - bf16 (bf16 x / y, or the tcgen05 path: weights rounded to bf16 after the exact fp32 dequant, h and y in bf16):
+    rel_max <= 1e-2."""
+
+import numpy as np
+import pytest
+
+from oracle import moe_np
+from tests.moe_helpers import make_block, oracle_y, orc, x_f32
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL, BF16_TOL = 2e-3, 1e-2
+
+
+def run(layer, x, *, act, path, T, gating="softmax", k=8, bias=None):
+    b = make_block(layer, T, act=act, path=path, gating=gating, top_k=k)
+    if bias is not None:
+        b.set_router_bias(0, bias)
+    y = b.forward(x)
+    dbg = b.debug(T)
+    b.close()
+    return (moe_np.bf16_to_f32(y) if act == "bf16" else y), dbg
+
+
+def check_routing(dbg, x, layer, k, gating="softmax", bias=None):
+    """GPU logits close to the fp32 product; GPU routing == the oracle's routing of those logits, bit for bit."""
+    want = x_f32(x) @ layer.router.T
+    if bias is not None:
+        want = want + bias
+    assert moe_np.rel_max(dbg["logits"], want) < 1e-5
+    ids, w = orc().route(dbg["logits"], k, gating=gating)
+    assert np.array_equal(dbg["ids"], ids)
+    assert np.abs(dbg["w"].astype(np.float64) - w).max() <= 2 ** -23
+    off, perm, _ = orc().dispatch(ids, layer.E)
+    assert np.array_equal(dbg["offsets"], off) and np.array_equal(dbg["perm"], perm)
+    return ids, w
+
+
+def test_config1_fp32(golden):
+    """BASELINE config 1 (T=16, H=2048, E=128, K=8, F=768, Q4_0, fp32 x) against the reference's own moe_ffn output
+    (tests/golden: ref.moe_route + ref.moe_ffn with gguf-py's dequant)."""
+    layer, x, _ = moe_np.make_block(0, 16, qtype="Q4_0", x_bf16=False)
+    y, dbg = run(layer, x, act="f32", path="gemv", T=16)
+    ids, w = check_routing(dbg, x, layer, 8)
+    assert np.array_equal(ids, golden["block_c1_ids"])
+    assert moe_np.rel_max(y, golden["block_c1_y"]) <= FP32_TOL
+    assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= FP32_TOL
+
+
+@pytest.mark.parametrize("B", [1, 4, 16, 64])
+def test_decode_q4k(B):
+    """Config 2's decode batches (Q4_K, bf16 x) on the dequant-GEMV path."""
+    layer, x, _ = moe_np.make_block(B, B, qtype="Q4_K")
+    y, dbg = run(layer, x, act="bf16", path="gemv", T=B)
+    ids, w = check_routing(dbg, x, layer, 8)
+    assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= BF16_TOL
+
+
+@pytest.mark.parametrize("qtype", ["Q4_0", "Q8_0", "Q4_K"])
+def test_decode_fp32_tight(qtype):
+    """fp32 activations through the GEMV path: the tight bound."""
+    layer, x, _ = moe_np.make_block(5, 24, qtype=qtype, x_bf16=False, E=32, H=512, F=256)
+    y, dbg = run(layer, x, act="f32", path="gemv", T=24)
+    ids, w = check_routing(dbg, x, layer, 8)
+    assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= FP32_TOL
+
+
+@pytest.mark.parametrize("qtype", ["Q4_0", "Q8_0", "Q4_K"])
+def test_tcgen05_small(qtype):
+    """The tcgen05 grouped GEMMs at a small shape: E=16, H=512, F=256, T=200 (ragged expert groups)."""
+    layer, x, _ = moe_np.make_block(11, 200, qtype=qtype, E=16, H=512, F=256)
+    y, dbg = run(layer, x, act="bf16", path="tc", T=200)
+    ids, w = check_routing(dbg, x, layer, 8)
+    assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= BF16_TOL
+
+
+@pytest.mark.parametrize("qtype", ["Q4_0", "Q8_0"])
+def test_tcgen05_full_shape(qtype):
+    """The tcgen05 path at the Qwen3-30B-A3B shape (H=2048, E=128, K=8, F=768), T=512, checked on 48 tokens."""
+    T = 512
+    layer, x, _ = moe_np.make_block(21, T, qtype=qtype)
+    y, dbg = run(layer, x, act="bf16", path="tc", T=T)
+    ids, w = check_routing(dbg, x, layer, 8)
+    tok = np.arange(0, T, T // 48)
+    assert moe_np.rel_max(y[tok], oracle_y(layer, x, ids, w, tokens=tok)) <= BF16_TOL
+
+
+def test_prefill_zipf_q8():
+    """Config 3 (T=4096, Q8_0, Zipf(1.1)-skewed routing, bf16): the dispatch in full, outputs on 32 tokens."""
+    T = 4096
+    layer, x, bias = moe_np.make_block(3, T, qtype="Q8_0", zipf=1.1)
+    y, dbg = run(layer, x, act="bf16", path="tc", T=T, bias=bias)
+    ids, w = check_routing(dbg, x, layer, 8, bias=bias)
+    counts = np.bincount(ids.ravel(), minlength=128)
+    assert counts.max() > 4 * counts.mean()  # (the skew is there)
+    tok = np.arange(0, T, T // 32)
+    assert moe_np.rel_max(y[tok], oracle_y(layer, x, ids, w, tokens=tok)) <= BF16_TOL
+
+
+def test_paths_agree():
+    """The GEMV and the tcgen05 path on the same input (Q4_0, T=256)."""
+    layer, x, _ = moe_np.make_block(8, 256, qtype="Q4_0", E=32, H=1024, F=512)
+    y1, _ = run(layer, x, act="bf16", path="gemv", T=256)
+    y2, _ = run(layer, x, act="bf16", path="tc", T=256)
+    assert moe_np.rel_max(y2, y1) <= BF16_TOL
+
+
+def test_tiny_and_sigmoid():
+    """Tiny shapes (E=8, K=2, T=1 and 3) and sigmoid gating (Flint's), on both paths."""
+    for T in (1, 3):
+        layer, x, _ = moe_np.make_block(30 + T, T, qtype="Q4_0", E=8, H=256, F=256)
+        for path in ("gemv", "tc"):
+            for gating in ("softmax", "sigmoid"):
+                y, dbg = run(layer, x, act="bf16", path=path, T=T, gating=gating, k=2)
+                ids, w = check_routing(dbg, x, layer, 2, gating=gating)
+                assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= BF16_TOL
+
+
+def test_repeatable():
+    """The same input twice: bit-identical outputs (the combine sums in slot order, no atomics)."""
+    layer, x, _ = moe_np.make_block(9, 300, qtype="Q4_0", E=32, H=512, F=256)
+    b = make_block(layer, 300, act="bf16", path="tc")
+    y1 = b.forward(x).copy()
+    y2 = b.forward(x)
+    b.close()
+    assert np.array_equal(y1, y2)
+
+
+def test_zero_tokens_and_errors():
+    from artlite_b200 import Error
+    layer, x, _ = moe_np.make_block(1, 4, qtype="Q4_0", E=8, H=256, F=256)
+    b = make_block(layer, 4, act="bf16", path="auto", top_k=2)
+    assert b.forward(x[:0]).shape == (0, 256)
+    with pytest.raises(Error, match="max_tokens"):
+        b.forward(np.zeros((5, 256), np.uint16))
+    b.close()
