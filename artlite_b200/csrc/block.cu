@@ -28,8 +28,9 @@ struct artlite_moe {
   cudaStream_t st = nullptr;
   int E_local = 0, e0 = 0;  // this rank's experts [e0, e0 + E_local)
   struct Layer {
-    artlite::DevBuf gate, up, down, router, bias;
+    artlite::DevBuf gate, up, down, router, bias, planes;
     bool has_bias = false;
+    int n_planes = 0;  // the router's bf16 planes (router_split): 3 for an F32 router, 1 for BF16
     int qtype = -1, down_qtype = -1, router_qtype = -1;
     int64_t rb_gu = 0, rb_dn = 0;
   };
@@ -203,6 +204,12 @@ int artlite_moe_set_weights(artlite_moe* h, int layer, int qtype, const void* ga
   AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.gate.ptr) + gu_bytes, 0, 64, h->st));
   AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.up.ptr) + gu_bytes, 0, 64, h->st));
   AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.down.ptr) + dn_bytes, 0, 64, h->st));
+  L.n_planes = 0;
+  if (router_tc_supported(d.n_experts, d.hidden, d.act_dtype)) {
+    L.n_planes = router_qtype == ARTLITE_F32 ? 3 : 1;
+    AL_TRY(L.planes.reserve(sizeof(uint16_t) * 3 * d.n_experts * H));
+    AL_TRY(router_split(L.router.ptr, router_qtype, d.n_experts, (int)H, L.planes.as<uint16_t>(), h->st));
+  }
   return wait(h->st, 0);
 }
 
@@ -238,8 +245,13 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
   AL_TRY(mark());
   // 1. router logits
   // (kernels of this forward: router, route, 3 dispatch, then 4 (gemv) or 6 (tc), then the combine)
-  AL_TRY(launch_router(xd, d.act_dtype, L.router.ptr, L.router_qtype, L.has_bias ? L.bias.as<float>() : nullptr, T, H,
-                       E, h->logits.as<float>(), st));
+  if (L.n_planes)
+    AL_TRY(launch_router_tc(static_cast<const uint16_t*>(xd), L.planes.as<uint16_t>(), L.n_planes,
+                            L.has_bias ? L.bias.as<float>() : nullptr, T, H, E, T, h->logits.as<float>(),
+                            h->status.as<DevStatus>(), st));
+  else
+    AL_TRY(launch_router(xd, d.act_dtype, L.router.ptr, L.router_qtype, L.has_bias ? L.bias.as<float>() : nullptr, T,
+                         H, E, h->logits.as<float>(), st));
   AL_TRY(mark());
   // 2. routing
   RouteArgs ra{h->logits.as<float>(), T, E, E, 0, E, K, d.gating, K <= 16 && E % 16 == 0 && E <= 512,

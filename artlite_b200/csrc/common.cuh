@@ -86,5 +86,6 @@ int64_t launch_count();
 void count_launch(int n = 1);
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
 }  // namespace artlite

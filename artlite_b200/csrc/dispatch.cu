@@ -13,7 +13,6 @@
 
 namespace artlite {
 
-__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
 size_t dispatch_scratch_bytes(int64_t P, int E) {
   const int64_t nblk = P ? cdiv(P, kDispatchBlockPairs) : 1;

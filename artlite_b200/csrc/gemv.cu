@@ -18,7 +18,6 @@
 
 namespace artlite {
 
-__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
 namespace {
 

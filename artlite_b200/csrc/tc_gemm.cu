@@ -27,6 +27,7 @@
 #include "quant.cuh"
 #include "tc_gemm.cuh"
 
+
 namespace artlite {
 namespace tc {
 
@@ -76,14 +77,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // a bounded wait: false once the CTA aborted (this wait ran out, or another role's did)
-__device__ __forceinline__ bool wait(Smem* sm, uint64_t* bar, uint32_t parity, DevStatus* st, int where) {
+__device__ __forceinline__ bool wait(int* abort, uint64_t* bar, uint32_t parity, DevStatus* st, int where) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*(volatile int*)&sm->abort) return false;
+    if (*(volatile int*)abort) return false;
     if (clock64() - t0 > kWaitCycles) {
-      *(volatile int*)&sm->abort = 1;
+      *(volatile int*)abort = 1;
       report(st, ARTLITE_ETIMEOUT, where, (int)blockIdx.x, 0);
       return false;
     }
@@ -271,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const Tile T = tile_of(p, t);
       for (int kc = 0; kc < p.K / KC; kc++) {
-        if (!wait(sm, &sm->raw_empty[r], rph ^ 1, p.status, 1)) goto out;
+        if (!wait(&sm->abort, &sm->raw_empty[r], rph ^ 1, p.status, 1)) goto out;
         uint8_t* dst = sR + r * BM * CB;
         mbar_expect_tx(&sm->raw_full[r], BM * CB);
         if (GU) {
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
         }
         if (++r == R) r = 0, rph ^= 1;
         for (int sub = 0; sub < KC / BK; sub++) {
-          if (!wait(sm, &sm->empty[s], sph ^ 1, p.status, 2)) goto out;
+          if (!wait(&sm->abort, &sm->empty[s], sph ^ 1, p.status, 2)) goto out;
           mbar_expect_tx(&sm->full_b[s], B_BYTES);
           tma_load_2d(sB + s * B_BYTES, &p.map_x, &sm->full_b[s], kc * KC + sub * BK, (int)T.row0);
           if (++s == S) s = 0, sph ^= 1;
@@ -295,13 +296,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
     int s = 0, sph = 0, acc = 0, aph = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const Tile T = tile_of(p, t);
-      if (!wait(sm, &sm->tempty[acc], aph ^ 1, p.status, 3)) goto out;
+      if (!wait(&sm->abort, &sm->tempty[acc], aph ^ 1, p.status, 3)) goto out;
       fence_after();
       const uint32_t id = idesc(BM, T.n_mma);
       const uint32_t d = tmem + acc * BNMAX;
       for (int ks = 0; ks < ksteps; ks++) {
-        if (!wait(sm, &sm->full_a[s], sph, p.status, 4)) goto out;
-        if (!wait(sm, &sm->full_b[s], sph, p.status, 5)) goto out;
+        if (!wait(&sm->abort, &sm->full_a[s], sph, p.status, 4)) goto out;
+        if (!wait(&sm->abort, &sm->full_b[s], sph, p.status, 5)) goto out;
         fence_after();
         const uint64_t da = sdesc(smem_u32(sA + s * A_BYTES)), db = sdesc(smem_u32(sB + s * B_BYTES));
 #pragma unroll
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
     int s = 0, sph = 0, r = 0, rph = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       for (int kc = 0; kc < p.K / KC; kc++) {
-        if (!wait(sm, &sm->raw_full[r], rph, p.status, 6)) goto out;
+        if (!wait(&sm->abort, &sm->raw_full[r], rph, p.status, 6)) goto out;
         uint32_t w[NW];
         const uint4* src = reinterpret_cast<const uint4*>(sR + r * BM * CB + raw_row * CB);
 #pragma unroll
@@ -338,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
         for (int sub = 0; sub < KC / BK; sub++) {
           uint32_t o[32];
           dequant_step<QT>(w, sub, o);
-          if (!wait(sm, &sm->empty[s], sph ^ 1, p.status, 7)) goto out;
+          if (!wait(&sm->abort, &sm->empty[s], sph ^ 1, p.status, 7)) goto out;
           uint8_t* row = sA + s * A_BYTES + i * 128;
 #pragma unroll
           for (int c = 0; c < 8; c++)
@@ -356,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
     int acc = 0, aph = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const Tile T = tile_of(p, t);
-      if (!wait(sm, &sm->tfull[acc], aph, p.status, 8)) goto out;
+      if (!wait(&sm->abort, &sm->tfull[acc], aph, p.status, 8)) goto out;
       fence_after();
       for (int c0 = 0; c0 < T.n_mma; c0 += 32) {
         uint32_t v[32];
@@ -407,6 +408,140 @@ out:
 
 }  // namespace tc
 
+// ---------------------------------------------------------------- the router on the tensor cores
+//
+// logits (T x E fp32) = x (T x H bf16) . W_r^T, with W_r (fp32) split into three bf16 planes hi + mid + lo
+// (hi = bf16(w), mid = bf16(w - hi), lo = bf16(w - hi - mid): |w - (hi + mid + lo)| <= 2^-24 |w|); every product of a
+// bf16 x with a plane is exact in fp32 and the three MMAs accumulate into one fp32 accumulator: the fp32 GEMM's logits
+// to within fp32 rounding of the sums. Per tile 128 experts (A: the planes, TMA, 128-byte swizzle) x 128 tokens (B),
+// K in stages of 64 (each stage the three planes and the token rows). Warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+// (logits[t, e] + bias[e], fp32, coalesced over e).
+namespace rt {
+constexpr int BM = 128, BN = 128, BK = 64, S = 3, PLANES = 3;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE = PLANES * A_BYTES + B_BYTES;
+constexpr int kThreads = 192;
+
+struct Params {
+  CUtensorMap map_w, map_x;  // w: the planes stacked (PLANES E rows of H), x: T rows of H
+  const float* bias;
+  float* logits;
+  DevStatus* status;
+  int64_t T;
+  int E, H, planes;
+};
+
+struct Smem {
+  uint64_t full[S], empty[S], tfull;
+  uint32_t tmem_base;
+  int abort;
+};
+}  // namespace rt
+
+__global__ void __launch_bounds__(rt::kThreads, 1) router_tc_kernel(const __grid_constant__ rt::Params p) {
+  using namespace rt;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  rt::Smem* sm = reinterpret_cast<rt::Smem*>(base + S * STAGE);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mtiles = p.E / BM;
+  const int tile_t = blockIdx.x / mtiles, tile_m = blockIdx.x % mtiles;
+  const int64_t t0 = (int64_t)tile_t * BN;
+  const int valid = (int)min64((int64_t)BN, p.T - t0);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; i++) {
+      tc::mbar_init(&sm->full[i], 1);
+      tc::mbar_init(&sm->empty[i], 1);
+    }
+    tc::mbar_init(&sm->tfull, 1);
+    sm->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_u32(&sm->tmem_base)),
+                 "r"(128));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = sm->tmem_base;
+  const int ksteps = p.H / BK;
+  if (warp == 0 && lane == 0) {
+    int s = 0, ph = 0;
+    for (int ks = 0; ks < ksteps; ks++) {
+      if (!tc::wait(&sm->abort, &sm->empty[s], ph ^ 1, p.status, 21)) goto out;
+      uint8_t* st = base + s * STAGE;
+      tc::mbar_expect_tx(&sm->full[s], p.planes * A_BYTES + B_BYTES);
+      for (int pl = 0; pl < p.planes; pl++)
+        tc::tma_load_2d(st + pl * A_BYTES, &p.map_w, &sm->full[s], ks * BK, pl * p.E + tile_m * BM);
+      tc::tma_load_2d(st + PLANES * A_BYTES, &p.map_x, &sm->full[s], ks * BK, (int)t0);
+      if (++s == S) s = 0, ph ^= 1;
+    }
+  } else if (warp == 1 && lane == 0) {
+    int s = 0, ph = 0;
+    const uint32_t id = tc::idesc(BM, BN);
+    for (int ks = 0; ks < ksteps; ks++) {
+      if (!tc::wait(&sm->abort, &sm->full[s], ph, p.status, 22)) goto out;
+      tc::fence_after();
+      uint8_t* st = base + s * STAGE;
+      const uint64_t db = tc::sdesc(tc::smem_u32(st + PLANES * A_BYTES));
+      for (int pl = 0; pl < p.planes; pl++) {
+        const uint64_t da = tc::sdesc(tc::smem_u32(st + pl * A_BYTES));
+#pragma unroll
+        for (int k = 0; k < BK / 16; k++) tc::mma(tmem, da + 2 * k, db + 2 * k, id, (ks | pl | k) != 0);
+      }
+      tc::commit(&sm->empty[s]);
+      if (++s == S) s = 0, ph ^= 1;
+    }
+    tc::commit(&sm->tfull);
+  } else if (warp >= 2) {
+    const int q = warp & 3;
+    if (!tc::wait(&sm->abort, &sm->tfull, 0, p.status, 23)) goto out;
+    tc::fence_after();
+    const int e = tile_m * BM + 32 * q + lane;
+    const float b = p.bias ? p.bias[e] : 0.0f;
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t v[32];
+      tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (c0 + j < valid) p.logits[(t0 + c0 + j) * p.E + e] = __uint_as_float(v[j]) + b;
+    }
+    tc::fence_before();
+  }
+out:
+  __syncwarp();
+  __syncthreads();
+  if (*(volatile int*)&sm->abort && threadIdx.x == 0) {
+    const long long c = clock64();
+    while (clock64() - c < 20000000LL) {
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128));
+  }
+}
+
+// W_r (E x H, fp32 or bf16) -> the bf16 planes (planes x E x H): fp32 into hi, mid, lo; bf16 copied as one plane
+__global__ void router_split_kernel(const void* w, int w_dtype, int64_t n, uint16_t* planes) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  if (w_dtype == ARTLITE_BF16) {
+    planes[i] = reinterpret_cast<const uint16_t*>(w)[i];
+    return;
+  }
+  const float v = reinterpret_cast<const float*>(w)[i];
+  const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+  const float r1 = __fsub_rn(v, __bfloat162float(hi));
+  const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+  const float r2 = __fsub_rn(r1, __bfloat162float(mid));
+  planes[i] = __bfloat16_as_ushort(hi);
+  planes[n + i] = __bfloat16_as_ushort(mid);
+  planes[2 * n + i] = __bfloat16_as_ushort(__float2bfloat16_rn(r2));
+}
+
 // ---------------------------------------------------------------- host side
 
 namespace {
@@ -445,6 +580,42 @@ int make_map(CUtensorMap* m, const void* base, int64_t row_elems, int64_t rows, 
 }
 
 }  // namespace
+
+
+bool router_tc_supported(int E, int H, int x_dtype) {
+  return x_dtype == ARTLITE_BF16 && E % rt::BM == 0 && H % rt::BK == 0;
+}
+
+int router_split(const void* w, int w_dtype, int E, int H, uint16_t* planes, cudaStream_t st) {
+  const int64_t n = (int64_t)E * H;
+  router_split_kernel<<<(unsigned)cdiv(n, 256), 256, 0, st>>>(w, w_dtype, n, planes);
+  AL_LAUNCHED();
+  return ARTLITE_OK;
+}
+
+int launch_router_tc(const uint16_t* x, const uint16_t* planes, int n_planes, const float* bias, int64_t T, int H,
+                     int E, int64_t x_rows, float* logits, DevStatus* status, cudaStream_t st) {
+  AL_CHECK(router_tc_supported(E, H, ARTLITE_BF16) && n_planes >= 1 && n_planes <= rt::PLANES, ARTLITE_EUNSUPPORTED,
+           "router tc: E %d H %d planes %d", E, H, n_planes);
+  AL_CHECK(((uintptr_t)x % 16) == 0 && ((uintptr_t)planes % 16) == 0, ARTLITE_EINVAL, "router tc: unaligned operand");
+  if (T == 0) return ARTLITE_OK;
+  rt::Params p{};
+  AL_TRY(make_map(&p.map_w, planes, H, (int64_t)n_planes * E, rt::BK, rt::BM, true));
+  AL_TRY(make_map(&p.map_x, x, H, x_rows, rt::BK, rt::BN, true));
+  p.bias = bias;
+  p.logits = logits;
+  p.status = status;
+  p.T = T;
+  p.E = E;
+  p.H = H;
+  p.planes = n_planes;
+  const size_t smem = 1024 + rt::S * rt::STAGE + sizeof(rt::Smem) + 64;
+  AL_CUDA(cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const unsigned grid = (unsigned)(cdiv(T, rt::BN) * (E / rt::BM));
+  router_tc_kernel<<<grid, rt::kThreads, smem, st>>>(p);
+  AL_LAUNCHED();
+  return ARTLITE_OK;
+}
 
 bool tc_supported(int qtype, int K, int N) {
   return tc::chunk_bytes(qtype) > 0 && K % tc::KC == 0 && N % tc::BM == 0;

@@ -32,4 +32,11 @@ bool tc_supported(int qtype, int K, int N);
 size_t tc_sched_bytes(int E);
 int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st);
 
+// The router on the tensor cores: logits (T x E fp32) = x (T x H bf16, x_rows >= T + 128 rows readable) . W^T from
+// the bf16 planes of W (router_split: 3 for an fp32 W, 1 for a bf16 W), + bias (E, may be null).
+bool router_tc_supported(int E, int H, int x_dtype);
+int router_split(const void* w, int w_dtype, int E, int H, uint16_t* planes, cudaStream_t st);
+int launch_router_tc(const uint16_t* x, const uint16_t* planes, int n_planes, const float* bias, int64_t T, int H,
+                     int E, int64_t x_rows, float* logits, DevStatus* status, cudaStream_t st);
+
 }  // namespace artlite
