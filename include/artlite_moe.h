@@ -84,6 +84,19 @@ int artlite_moe_plan(const int32_t* ids, int64_t n, int k, int E, int cols, int 
 int artlite_moe_dispatch(const int32_t* ids, int64_t n, int k, int E, int64_t* offsets, int32_t* perm,
                          int32_t* slot);
 
+/*
+ * The same dispatch for callers that must not allocate device memory while they run (a serving loop that reserves its
+ * memory budget at start-up, code whose device memory a framework's caching allocator owns): it allocates nothing.
+ * No counterpart in the reference. ids, offsets, perm and slot must be device memory of the current device; the
+ * scratch is a 1 MiB static device array of this library (held on every GPU that loads it until exit), so a call
+ * takes at most ceil(n k / 4096) E <= 262144 block counts (n k <= 8,388,608 pairs at E = 128) and rejects more with
+ * ARTLITE_EINVAL. The first call on a device looks the array's address up (cudaGetSymbolAddress) for that device; make
+ * it before any stream capture. Enqueued on `stream` (NULL: the default stream), then waited for; every call shares
+ * the array, so calls that overlap on the GPU race.
+ */
+int artlite_moe_dispatch_noalloc(const int32_t* ids, int64_t n, int k, int E, int64_t* offsets, int32_t* perm,
+                                 int32_t* slot, void* stream);
+
 /* Whether artlite_dequant_rows reads a GGUF type name ("Q4_0", "Q8_0", "Q4_K", ...; dequant.h:9-11). */
 int artlite_dequant_supported(const char* qtype);
 
