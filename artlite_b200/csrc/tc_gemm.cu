@@ -8,15 +8,17 @@
 //         and the matching 16 up rows (TMEM lanes 32q + l: l < 16 gate feature 16q + l, l >= 16 up feature 16q + l - 16);
 //         out h[(token), f] = silu(g) u in bf16 (ref.swiglu, tests/moe/ref.py:21-24).
 //   down  A = 128 down rows; out y[(token), n] in bf16.
-// Warp roles (320 threads, one CTA per SM, persistent over a static round-robin of tiles):
+// Warp roles (448 threads, one CTA per SM, persistent over a static round-robin of tiles):
 //   warp 0      TMA producer: raw weight bytes (2D tensor map over the GGUF rows, 16-bit elements, 256 K-values
 //               per stage: 144 B a row for Q4_0 / Q4_K, 272 B for Q8_0) and the token rows (bf16, 128-byte swizzle);
 //               it also allocates and frees the 512 TMEM columns.
 //   warp 1      MMA issuer: tcgen05.mma kind::f16 (bf16 x bf16 -> fp32), one thread; tcgen05.commit frees stages.
-//   warps 2-5   dequant: a thread per weight row; the row's raw bytes (one stage) into registers, then per 64 values
-//               the reference's exact fp32 decode (quant.cuh's arithmetic), rounded once to bf16, written into the A
-//               stage in the UMMA K-major 128-byte-swizzle layout; fence.proxy.async, then an mbarrier arrive.
-//   warps 6-9   epilogue: tcgen05.ld of 32 columns at a time, SwiGLU (gu) or the plain rows (down), bf16 stores.
+//   warps 2-9   dequant, two groups of four warps (two warps per SM sub-partition): in group g a thread per weight
+//               row decodes steps 2g and 2g + 1 (64 values each) of every 256-value stage, from only the raw bytes of
+//               those steps loaded into registers; the reference's exact fp32 values (magic-number byte conversion,
+//               f32x2 arithmetic), rounded once to bf16, written into the A stage in the UMMA K-major
+//               128-byte-swizzle layout; fence.proxy.async, then an mbarrier arrive.
+//   warps 10-13 epilogue: tcgen05.ld of 32 columns at a time, SwiGLU (gu) or the plain rows (down), bf16 stores.
 // Every mbarrier wait is bounded (kWaitCycles): on expiry the CTA records ARTLITE_ETIMEOUT in the status word, stops
 // issuing, lets copies and MMAs already issued land, frees its TMEM and exits.
 #include <cuda.h>
@@ -31,14 +33,17 @@
 namespace artlite {
 namespace tc {
 
-constexpr int BM = 128, BNMAX = 256, BK = 64, KC = 256, S = 3, R = 2;
+constexpr int BM = 128, BNMAX = 256, BK = 64, KC = 256, S = 3, RMAX = 3;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BNMAX * BK * 2;
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;  // 14 warps: producer, MMA, 8 dequant, 4 epilogue
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at the B200's clocks
 
 __host__ __device__ constexpr int chunk_bytes(int qt) {  // raw bytes of 256 values of a row
   return qt == ARTLITE_Q8_0 ? 272 : (qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_K) ? 144 : 0;
 }
+
+// raw weight stages: three of 18 KB for the 144-byte formats, two of 34 KB for Q8_0 (shared memory)
+__host__ __device__ constexpr int raw_stages(int qt) { return qt == ARTLITE_Q8_0 ? 2 : 3; }
 
 struct Params {
   CUtensorMap map_w0, map_w1, map_x;
@@ -50,7 +55,7 @@ struct Params {
 };
 
 struct Smem {
-  uint64_t full_a[S], full_b[S], empty[S], raw_full[R], raw_empty[R], tfull[2], tempty[2];
+  uint64_t full_a[S], full_b[S], empty[S], raw_full[RMAX], raw_empty[RMAX], tfull[2], tempty[2];
   uint32_t tmem_base;
   int abort;
 };
@@ -163,65 +168,134 @@ __device__ __forceinline__ Tile tile_of(const Params& p, int t) {
 }
 
 // ---------------------------------------------------------------- dequant of one 64-value step into bf16 pairs
+//
+// Exact integer -> fp32 by the "magic number": a byte b placed under the exponent of 2^23 (0x4B000000 | b) is the
+// float 2^23 + b, and subtracting 2^23 (+ an offset) leaves b (- the offset) exactly. Byte selection is one PRMT per
+// value; the fp32 arithmetic runs on f32x2 pairs (two values an instruction); each value is then the reference's fp32
+// result exactly (the same products / differences, rounded to nearest once each, no FMA) before its one rounding to
+// bf16.
 
 __device__ __forceinline__ uint32_t byte_at(const uint32_t* w, int b) { return (w[b >> 2] >> ((b & 3) * 8)) & 0xFFu; }
 __device__ __forceinline__ float half_at(const uint32_t* w, int b) {
-  return __half2float(__ushort_as_half((unsigned short)(byte_at(w, b) | (byte_at(w, b + 1) << 8))));
+  const uint32_t v = (b & 3) == 0 ? (w[b >> 2] & 0xFFFFu) : (b & 3) == 2 ? (w[b >> 2] >> 16)
+                                                                         : (byte_at(w, b) | (byte_at(w, b + 1) << 8));
+  return __half2float(__ushort_as_half((unsigned short)v));
 }
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
 }
+// the 4 bytes of w as the floats 2^23 + byte, in pairs
+__device__ __forceinline__ void magic4(uint32_t w, uint64_t& p01, uint64_t& p23) {
+  const uint32_t a = __byte_perm(w, 0x4B00u, 0x5440), b = __byte_perm(w, 0x4B00u, 0x5441);
+  const uint32_t c = __byte_perm(w, 0x4B00u, 0x5442), d = __byte_perm(w, 0x4B00u, 0x5443);
+  asm("mov.b64 %0, {%1, %2};" : "=l"(p01) : "r"(a), "r"(b));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(p23) : "r"(c), "r"(d));
+}
+__device__ __forceinline__ uint64_t dup2(float v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2(uint64_t v) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return pack_bf16(a, b);
+}
+// the 16 bytes starting at byte o (o even) of w as 4 words
+__device__ __forceinline__ void words16(const uint32_t* w, int o, uint32_t (&q)[4]) {
+#pragma unroll
+  for (int k = 0; k < 4; k++)
+    q[k] = (o & 2) ? __funnelshift_r(w[(o >> 2) + k], w[(o >> 2) + k + 1], 16) : w[(o >> 2) + k];
+}
 
-// w: a row's raw bytes of one 256-value stage; o: 32 words = values 64 sub .. 64 sub + 63 as bf16 pairs
-template <int QT>
-__device__ __forceinline__ void dequant_step(const uint32_t* w, int sub, uint32_t (&o)[32]) {
-  if constexpr (QT == ARTLITE_Q4_0) {
+// Q4_0 block at byte o of the stage's row bytes: 32 values (q - 8) d as 16 bf16 pairs into o16
+__device__ __forceinline__ void dq_q4_0_block(const uint32_t* w, int o, uint32_t* o16) {
+  const uint64_t d = dup2(half_at(w, o)), off = dup2(-8388616.0f);  // -(2^23 + 8)
+  uint32_t q[4];
+  words16(w, o + 2, q);
 #pragma unroll
-    for (int bi = 0; bi < 2; bi++) {
-      const int base = 18 * (2 * sub + bi);
-      const float d = half_at(w, base);
+  for (int k = 0; k < 4; k++) {
+    uint64_t a, b, c, e;
+    magic4(q[k] & 0x0F0F0F0Fu, a, b);          // values 4k .. 4k + 3 (low nibbles)
+    magic4((q[k] >> 4) & 0x0F0F0F0Fu, c, e);   // values 16 + 4k .. 16 + 4k + 3 (high nibbles)
+    o16[2 * k] = bf16x2(mul2(add2(a, off), d));
+    o16[2 * k + 1] = bf16x2(mul2(add2(b, off), d));
+    o16[8 + 2 * k] = bf16x2(mul2(add2(c, off), d));
+    o16[8 + 2 * k + 1] = bf16x2(mul2(add2(e, off), d));
+  }
+}
+
+// Q8_0 block at byte o: 32 values d q (q int8: biased by 128 into a byte, then the magic)
+__device__ __forceinline__ void dq_q8_0_block(const uint32_t* w, int o, uint32_t* o16) {
+  const uint64_t d = dup2(half_at(w, o)), off = dup2(-8388736.0f);  // -(2^23 + 128)
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const uint32_t b0 = byte_at(w, base + 2 + 2 * j), b1 = byte_at(w, base + 3 + 2 * j);
-        o[16 * bi + j] = pack_bf16(__fmul_rn((float)((int)(b0 & 15) - 8), d), __fmul_rn((float)((int)(b1 & 15) - 8), d));
-        o[16 * bi + 8 + j] = pack_bf16(__fmul_rn((float)((int)(b0 >> 4) - 8), d), __fmul_rn((float)((int)(b1 >> 4) - 8), d));
-      }
-    }
-  } else if constexpr (QT == ARTLITE_Q8_0) {
+  for (int h = 0; h < 2; h++) {
+    uint32_t q[4];
+    words16(w, o + 2 + 16 * h, q);
 #pragma unroll
-    for (int bi = 0; bi < 2; bi++) {
-      const int base = 34 * (2 * sub + bi);
-      const float d = half_at(w, base);
-#pragma unroll
-      for (int j = 0; j < 16; j++) {
-        const int q0 = (int)(int8_t)byte_at(w, base + 2 + 2 * j), q1 = (int)(int8_t)byte_at(w, base + 3 + 2 * j);
-        o[16 * bi + j] = pack_bf16(__fmul_rn(d, (float)q0), __fmul_rn(d, (float)q1));
-      }
-    }
-  } else {  // Q4_K: the stage is one super-block; this step its groups 2 sub (low nibbles) and 2 sub + 1 (high)
-    const float d = half_at(w, 0), dmin = half_at(w, 2);
-#pragma unroll
-    for (int hb = 0; hb < 2; hb++) {
-      const int g = 2 * sub + hb;
-      int sc, mn;
-      if (g < 4) {
-        sc = byte_at(w, 4 + g) & 63;
-        mn = byte_at(w, 8 + g) & 63;
-      } else {
-        sc = (byte_at(w, 12 + g - 4) & 15) | (byte_at(w, 4 + g - 4) >> 6) << 4;
-        mn = (byte_at(w, 12 + g - 4) >> 4) | (byte_at(w, 8 + g - 4) >> 6) << 4;
-      }
-      const float dsc = __fmul_rn(d, (float)sc), dmn = __fmul_rn(dmin, (float)mn);
-#pragma unroll
-      for (int j = 0; j < 16; j++) {
-        const uint32_t b0 = byte_at(w, 16 + 32 * sub + 2 * j), b1 = byte_at(w, 17 + 32 * sub + 2 * j);
-        const int q0 = hb ? (int)(b0 >> 4) : (int)(b0 & 15), q1 = hb ? (int)(b1 >> 4) : (int)(b1 & 15);
-        o[16 * hb + j] = pack_bf16(__fsub_rn(__fmul_rn((float)q0, dsc), dmn), __fsub_rn(__fmul_rn((float)q1, dsc), dmn));
-      }
+    for (int k = 0; k < 4; k++) {
+      uint64_t a, b;
+      magic4(q[k] ^ 0x80808080u, a, b);
+      o16[8 * h + 2 * k] = bf16x2(mul2(d, add2(a, off)));
+      o16[8 * h + 2 * k + 1] = bf16x2(mul2(d, add2(b, off)));
     }
   }
 }
+
+// Q4_K group g of the stage's super-block: 32 values q (d sc_g) - dmin mn_g
+__device__ __forceinline__ void dq_q4_k_group(const uint32_t* w, int g, uint32_t* o16) {
+  const float d = half_at(w, 0), dmin = half_at(w, 2);
+  int sc, mn;
+  if (g < 4) {
+    sc = byte_at(w, 4 + g) & 63;
+    mn = byte_at(w, 8 + g) & 63;
+  } else {
+    sc = (byte_at(w, 12 + g - 4) & 15) | (byte_at(w, 4 + g - 4) >> 6) << 4;
+    mn = (byte_at(w, 12 + g - 4) >> 4) | (byte_at(w, 8 + g - 4) >> 6) << 4;
+  }
+  const uint64_t dsc = dup2(__fmul_rn(d, (float)sc)), ndmn = dup2(-__fmul_rn(dmin, (float)mn));
+  const uint64_t off = dup2(-8388608.0f);  // -2^23
+  const int wq = 4 + 8 * (g >> 1);         // the group's 32 qs bytes: words wq .. wq + 7
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const uint32_t v = (g & 1) ? (w[wq + k] >> 4) & 0x0F0F0F0Fu : w[wq + k] & 0x0F0F0F0Fu;
+    uint64_t a, b;
+    magic4(v, a, b);
+    o16[2 * k] = bf16x2(add2(mul2(add2(a, off), dsc), ndmn));
+    o16[2 * k + 1] = bf16x2(add2(mul2(add2(b, off), dsc), ndmn));
+  }
+}
+
+// values 64 sub .. 64 sub + 63 of the stage (w: the row's raw bytes of the 256-value stage, as words) as 32 bf16 pairs
+template <int QT>
+__device__ __forceinline__ void dequant_step(const uint32_t* w, int sub, uint32_t (&o)[32]) {
+#pragma unroll
+  for (int hb = 0; hb < 2; hb++) {
+    if constexpr (QT == ARTLITE_Q4_0) dq_q4_0_block(w, 18 * (2 * sub + hb), o + 16 * hb);
+    else if constexpr (QT == ARTLITE_Q8_0) dq_q8_0_block(w, 34 * (2 * sub + hb), o + 16 * hb);
+    else dq_q4_k_group(w, 2 * sub + hb, o + 16 * hb);
+  }
+}
+
+// the 16-byte words of a row's stage bytes that dequant group grp (its steps 2 grp, 2 grp + 1) reads
+template <int QT>
+struct RawSpan {
+  // Q4_0: blocks 4 grp .. 4 grp + 3 = bytes 72 grp .. 72 grp + 71; Q8_0: bytes 136 grp ..; Q4_K: the header and
+  // qs bytes 16 + 64 grp ..
+  static constexpr int first(int grp) { return QT == ARTLITE_Q4_0 ? 4 * grp : QT == ARTLITE_Q8_0 ? 8 * grp : 0; }
+  static constexpr int count = QT == ARTLITE_Q8_0 ? 9 : 5;
+};
 
 // ---------------------------------------------------------------- the kernel
 
@@ -229,6 +303,7 @@ template <int QT, bool GU>
 __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_constant__ Params p) {
   constexpr int CB = chunk_bytes(QT);
   constexpr int NW = CB / 4;
+  constexpr int R = raw_stages(QT);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = base;
@@ -246,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
     }
     for (int i = 0; i < R; i++) {
       mbar_init(&sm->raw_full[i], 1);
-      mbar_init(&sm->raw_empty[i], 4);
+      mbar_init(&sm->raw_empty[i], 8);
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&sm->tfull[i], 1);
@@ -267,8 +342,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
   const int ksteps = p.K / BK;
 
   if (warp == 0 && lane == 0) {
-    // ---------------- producer
-    int s = 0, sph = 0, r = 0, rph = 0;
+    // ---------------- producer of the token rows (B stages)
+    int s = 0, sph = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const Tile T = tile_of(p, t);
+      for (int ks = 0; ks < ksteps; ks++) {
+        if (!wait(&sm->abort, &sm->empty[s], sph ^ 1, p.status, 2)) goto out;
+        mbar_expect_tx(&sm->full_b[s], B_BYTES);
+        tma_load_2d(sB + s * B_BYTES, &p.map_x, &sm->full_b[s], ks * BK, (int)T.row0);
+        if (++s == S) s = 0, sph ^= 1;
+      }
+    }
+  } else if (warp == 0 && lane == 1) {
+    // ---------------- producer of the raw weight rows (R stages of 256 values, ahead of the B stages)
+    int r = 0, rph = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const Tile T = tile_of(p, t);
       for (int kc = 0; kc < p.K / KC; kc++) {
@@ -283,12 +370,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
           tma_load_2d(dst, &p.map_w0, &sm->raw_full[r], kc * (CB / 2), T.e * p.N + BM * T.m);
         }
         if (++r == R) r = 0, rph ^= 1;
-        for (int sub = 0; sub < KC / BK; sub++) {
-          if (!wait(&sm->abort, &sm->empty[s], sph ^ 1, p.status, 2)) goto out;
-          mbar_expect_tx(&sm->full_b[s], B_BYTES);
-          tma_load_2d(sB + s * B_BYTES, &p.map_x, &sm->full_b[s], kc * KC + sub * BK, (int)T.row0);
-          if (++s == S) s = 0, sph ^= 1;
-        }
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -313,33 +394,51 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
       commit(&sm->tfull[acc]);
       if (++acc == 2) acc = 0, aph ^= 1;
     }
-  } else if (warp >= 2 && warp < 6) {
-    // ---------------- dequant: thread i owns A row i
-    const int i = threadIdx.x - 64;
+  } else if (warp >= 2 && warp < 10) {
+    // ---------------- dequant: two groups of 4 warps; thread i of group grp owns A row i and writes steps 2 grp and
+    // 2 grp + 1 of every 256-value stage (64 values each), reading only the raw bytes of those steps
+    const int grp = (warp - 2) >> 2, i = threadIdx.x - 64 - 128 * grp;
     int raw_row = i;
     if (GU) {
       const int q = i >> 5, l = i & 31;
       raw_row = l < 16 ? 16 * q + l : 64 + 16 * q + (l - 16);
     }
-    int s = 0, sph = 0, r = 0, rph = 0;
+    int n = 0, r = 0, rph = 0;  // n: the step counter shared with the producer and the MMA issuer
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       for (int kc = 0; kc < p.K / KC; kc++) {
         if (!wait(&sm->abort, &sm->raw_full[r], rph, p.status, 6)) goto out;
-        uint32_t w[NW];
+        uint32_t w[NW + 4];
         const uint4* src = reinterpret_cast<const uint4*>(sR + r * BM * CB + raw_row * CB);
+        if (grp == 0) {
 #pragma unroll
-        for (int v = 0; v < NW / 4; v++) {
-          const uint4 u = src[v];
-          w[4 * v] = u.x, w[4 * v + 1] = u.y, w[4 * v + 2] = u.z, w[4 * v + 3] = u.w;
+          for (int v = 0; v < (QT == ARTLITE_Q8_0 ? 9 : 5); v++) {
+            const uint4 u = src[v];
+            w[4 * v] = u.x, w[4 * v + 1] = u.y, w[4 * v + 2] = u.z, w[4 * v + 3] = u.w;
+          }
+        } else {
+          if (QT == ARTLITE_Q4_K) {  // (the header)
+            const uint4 u = src[0];
+            w[0] = u.x, w[1] = u.y, w[2] = u.z, w[3] = u.w;
+          }
+#pragma unroll
+          for (int v = (QT == ARTLITE_Q4_K ? 5 : RawSpan<QT>::first(1));
+               v < (QT == ARTLITE_Q4_K ? 9 : RawSpan<QT>::first(1) + RawSpan<QT>::count); v++) {
+            const uint4 u = src[v];
+            w[4 * v] = u.x, w[4 * v + 1] = u.y, w[4 * v + 2] = u.z, w[4 * v + 3] = u.w;
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm->raw_empty[r]);
         if (++r == R) r = 0, rph ^= 1;
 #pragma unroll
-        for (int sub = 0; sub < KC / BK; sub++) {
+        for (int j = 0; j < 2; j++) {
+          const int sub = 2 * grp + j;
+          const int step = n + sub, s = step % S;
+          const uint32_t ph = (step / S) & 1;
           uint32_t o[32];
-          dequant_step<QT>(w, sub, o);
-          if (!wait(&sm->abort, &sm->empty[s], sph ^ 1, p.status, 7)) goto out;
+          if (grp == 0) dequant_step<QT>(w, j, o);
+          else dequant_step<QT>(w, 2 + j, o);
+          if (!wait(&sm->abort, &sm->empty[s], ph ^ 1, p.status, 7)) goto out;
           uint8_t* row = sA + s * A_BYTES + i * 128;
 #pragma unroll
           for (int c = 0; c < 8; c++)
@@ -347,11 +446,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm->full_a[s]);
-          if (++s == S) s = 0, sph ^= 1;
         }
+        n += KC / BK;
       }
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 10) {
     // ---------------- epilogue: TMEM lanes 32 q .. 32 q + 31
     const int q = warp & 3;
     int acc = 0, aph = 0;
@@ -649,7 +748,8 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
   p.K = a.K;
   p.N = a.N;
   p.MT = MT;
-  const size_t smem = 1024 + tc::S * (tc::A_BYTES + tc::B_BYTES) + tc::R * tc::BM * cb + sizeof(tc::Smem) + 64;
+  const size_t smem = 1024 + tc::S * (tc::A_BYTES + tc::B_BYTES) + tc::raw_stages(a.qtype) * tc::BM * cb +
+                      sizeof(tc::Smem) + 64;
   int dev, sms;
   AL_CUDA(cudaGetDevice(&dev));
   AL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
