@@ -18,7 +18,8 @@ QTYPES = {"F32": 0, "F16": 1, "Q4_0": 2, "Q4_1": 3, "Q8_0": 8, "Q4_K": 12, "Q5_K
 EXPORTS = ("artlite_moe_last_error", "artlite_moe_version", "artlite_moe_route", "artlite_moe_plan",
            "artlite_moe_dispatch", "artlite_moe_dispatch_noalloc", "artlite_dequant_supported", "artlite_dequant_rows", "artlite_moe_create",
            "artlite_moe_set_weights", "artlite_moe_set_router_bias", "artlite_moe_forward", "artlite_moe_sync", "artlite_moe_debug",
-           "artlite_moe_stage_times", "artlite_moe_path", "artlite_moe_launch_count", "artlite_moe_destroy")
+           "artlite_moe_stage_times", "artlite_moe_path", "artlite_moe_launch_count", "artlite_moe_destroy",
+           "artlite_moe_ep_unique_id", "artlite_moe_ep_init", "artlite_moe_ep_plan")
 
 
 class Error(RuntimeError):
@@ -58,6 +59,9 @@ _SIGS = {
     "artlite_moe_path": ([_P, _I], _I),
     "artlite_moe_launch_count": ([], _I64),
     "artlite_moe_destroy": ([_P], _I),
+    "artlite_moe_ep_unique_id": ([_P, _I], _I),
+    "artlite_moe_ep_init": ([_P, _P, _I], _I),
+    "artlite_moe_ep_plan": ([_P, _P, _I, _I, _I, _P, _P, _P, _P], _I),
 }
 
 _lib = None

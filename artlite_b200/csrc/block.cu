@@ -21,44 +21,12 @@
 #include "common.cuh"
 #include "kernels.cuh"
 #include "tc_gemm.cuh"
+#include "block.cuh"
 
-struct artlite_moe {
-  artlite_moe_desc d{};
-  int dev = 0;
-  cudaStream_t st = nullptr;
-  int E_local = 0, e0 = 0;  // this rank's experts [e0, e0 + E_local)
-  struct Layer {
-    artlite::DevBuf gate, up, down, router, bias, planes;
-    bool has_bias = false;
-    int n_planes = 0;  // the router's bf16 planes (router_split): 3 for an F32 router, 1 for BF16
-    int qtype = -1, down_qtype = -1, router_qtype = -1;
-    int64_t rb_gu = 0, rb_dn = 0;
-  };
-  std::vector<Layer> layers;
-  // workspaces
-  artlite::DevBuf xin, yout, logits, ids, w, offsets, perm, slot, counts, blk, unit_gu, unit_dn, status;
-  artlite::DevBuf h, y, xp, tiles;
-  int64_t last_T = 0;
-  int last_path = 0;
-  bool timing = false;
-  std::vector<cudaEvent_t> ev;  // [n_layers][kStages]: the last forward of each layer, read without a sync
-  std::vector<int> n_stages;    // per layer
-  std::vector<int> paths;       // per layer: the expert path of its last forward
-};
 
-namespace artlite {
-constexpr int kStages = 8;
-}
 
 namespace artlite {
 namespace {
-
-int choose_path(const artlite_moe& h, int64_t T, int qtype) {
-  if (h.d.path == 1 || h.d.path == 2) return h.d.path;
-  // tcgen05 for prefill-sized batches of the formats its loader reads, the GEMVs otherwise
-  if (T * h.d.top_k >= 4 * h.d.n_experts && tc_supported(qtype, h.d.hidden, h.d.expert_ffn)) return 2;
-  return 1;
-}
 
 int status_error(const DevStatus& s, int E) {
   if (s.code == ARTLITE_EDEVICE) {
@@ -100,6 +68,138 @@ int wait(cudaStream_t st, int timeout_ms) {
 }  // namespace
 }  // namespace artlite
 
+
+namespace artlite {
+
+int wait_deadline(cudaStream_t st, int timeout_ms) { return wait(st, timeout_ms); }
+
+int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L) {
+  const artlite_moe_desc& d = h.d;
+  const bool tc = tc_supported(L.qtype, d.hidden, d.expert_ffn) && tc_supported(L.down_qtype, d.expert_ffn, d.hidden);
+  if (d.path == 1 || !tc) return 1;
+  if (d.path == 2) return 2;
+  // tcgen05 for prefill-sized batches (on average 4 pairs an expert or more), the GEMVs for decode batches
+  return P >= 4 * (int64_t)h.E_local ? 2 : 1;
+}
+
+int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* xd, int64_t T, cudaStream_t st,
+                       Marker& mk) {
+  const artlite_moe_desc& d = h->d;
+  const int H = d.hidden, E = d.n_experts, K = d.top_k;
+  if (T > 0) {
+    if (L.n_planes)
+      AL_TRY(launch_router_tc(static_cast<const uint16_t*>(xd), L.planes.as<uint16_t>(), L.n_planes,
+                              L.has_bias ? L.bias.as<float>() : nullptr, T, H, E, T, h->logits.as<float>(),
+                              h->status.as<DevStatus>(), st));
+    else
+      AL_TRY(launch_router(xd, d.act_dtype, L.router.ptr, L.router_qtype, L.has_bias ? L.bias.as<float>() : nullptr,
+                           T, H, E, h->logits.as<float>(), st));
+  }
+  AL_TRY(mk.mark());
+  RouteArgs ra{h->logits.as<float>(), T, E, E, 0, E, K, d.gating, K <= 16 && E % 16 == 0 && E <= 512,
+               h->ids.as<int32_t>(), h->w.as<float>()};
+  AL_TRY(launch_route(ra, st));
+  DispatchArgs da{};
+  da.ids = h->ids.as<int32_t>();
+  da.P = T * K;
+  da.E = E;
+  da.blk_counts = h->blk.as<int32_t>();
+  da.offsets = h->offsets.as<int64_t>();
+  da.perm = h->perm.as<int32_t>();
+  da.slot = h->slot.as<int32_t>();
+  da.counts = h->counts.as<int32_t>();
+  da.status = h->status.as<DevStatus>();
+  AL_TRY(launch_dispatch(da, st));
+  return mk.mark();
+}
+
+int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const void* x, int x_dtype, bool gathered,
+                const int32_t* perm, int k, int64_t P, int E_run, const int64_t* offsets, const int32_t* counts,
+                int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk) {
+  const artlite_moe_desc& d = h->d;
+  const int H = d.hidden, F = d.expert_ffn;
+  *y_rows = h->y.ptr;
+  if (path == 1) {
+    *y_dtype = ARTLITE_F32;
+    if (P == 0) return ARTLITE_OK;
+    const int rt_gu = gemv_row_tile(F), rt_dn = gemv_row_tile(H);
+    AL_TRY(launch_unit_scan(counts, E_run, kGemvTokens, F / rt_gu, h->unit_gu.as<int32_t>(), st));
+    AL_TRY(launch_unit_scan(counts, E_run, kGemvTokens, H / rt_dn, h->unit_dn.as<int32_t>(), st));
+    ExpertGemvArgs g{};
+    g.qtype = L.qtype;
+    g.w0 = L.gate.as<uint8_t>();
+    g.w1 = L.up.as<uint8_t>();
+    g.row_bytes = L.rb_gu;
+    g.K = H;
+    g.N = F;
+    g.E = E_run;
+    g.x = x;
+    g.x_dtype = x_dtype;
+    g.perm = perm;
+    g.offsets = offsets;
+    g.unit_off = h->unit_gu.as<int32_t>();
+    g.rt = rt_gu;
+    g.k = k;
+    g.out = h->h.as<float>();
+    AL_TRY(launch_gemv_gu(g, st));
+    AL_TRY(mk.mark());
+    ExpertGemvArgs dn = g;
+    dn.qtype = L.down_qtype;
+    dn.w0 = L.down.as<uint8_t>();
+    dn.w1 = nullptr;
+    dn.row_bytes = L.rb_dn;
+    dn.K = F;
+    dn.N = H;
+    dn.x = h->h.ptr;
+    dn.x_dtype = ARTLITE_F32;
+    dn.unit_off = h->unit_dn.as<int32_t>();
+    dn.rt = rt_dn;
+    dn.out = h->y.as<float>();
+    AL_TRY(launch_gemv_down(dn, st));
+    return mk.mark();
+  }
+  *y_dtype = ARTLITE_BF16;
+  if (P == 0) return ARTLITE_OK;
+  const uint16_t* xg = static_cast<const uint16_t*>(x);
+  if (!gathered) {
+    AL_TRY(launch_gather(x, x_dtype, perm, P, k, H, h->xp.as<uint16_t>(), st));
+    xg = h->xp.as<uint16_t>();
+    x_rows = (int64_t)(h->xp.bytes / (sizeof(uint16_t) * H));
+  }
+  TcGemmArgs g{};
+  g.qtype = L.qtype;
+  g.w0 = L.gate.as<uint8_t>();
+  g.w1 = L.up.as<uint8_t>();
+  g.row_bytes = L.rb_gu;
+  g.K = H;
+  g.N = F;
+  g.E = E_run;
+  g.x = xg;
+  g.x_rows = x_rows;
+  g.status = h->status.as<DevStatus>();
+  g.P = P;
+  g.offsets = offsets;
+  g.counts = counts;
+  g.sched = h->tiles.ptr;
+  g.out = h->h.as<uint16_t>();
+  AL_TRY(launch_tc_gemm(g, /*gu=*/true, st));
+  AL_TRY(mk.mark());
+  TcGemmArgs dn = g;
+  dn.qtype = L.down_qtype;
+  dn.w0 = L.down.as<uint8_t>();
+  dn.w1 = nullptr;
+  dn.row_bytes = L.rb_dn;
+  dn.K = F;
+  dn.N = H;
+  dn.x = h->h.as<uint16_t>();
+  dn.x_rows = (int64_t)(h->h.bytes / (sizeof(uint16_t) * F));
+  dn.out = h->y.as<uint16_t>();
+  AL_TRY(launch_tc_gemm(dn, /*gu=*/false, st));
+  return mk.mark();
+}
+
+}  // namespace artlite
+
 using namespace artlite;
 
 extern "C" {
@@ -120,8 +220,6 @@ int artlite_moe_create(const artlite_moe_desc* desc, artlite_moe** out) {
   const int world = d.ep_world > 0 ? d.ep_world : 1;
   AL_CHECK(d.ep_rank >= 0 && d.ep_rank < world && d.n_experts % world == 0, ARTLITE_EINVAL,
            "moe_create: rank %d of %d with %d experts", d.ep_rank, world, d.n_experts);
-  AL_CHECK(world == 1, ARTLITE_EUNSUPPORTED, "moe_create: expert parallelism goes through artlite_moe_ep_* (world %d)",
-           world);
   std::unique_ptr<artlite_moe> h(new artlite_moe);
   h->d = d;
   if (d.device >= 0) AL_CUDA(cudaSetDevice(d.device));
@@ -160,6 +258,7 @@ int artlite_moe_create(const artlite_moe_desc* desc, artlite_moe** out) {
   AL_TRY(h->xin.reserve(act * T * H));
   AL_TRY(h->yout.reserve(act * T * H));
   AL_CUDA(cudaMemsetAsync(h->status.ptr, 0, sizeof(DevStatus), h->st));
+  if (world > 1) AL_TRY(ep_create(h.get()));
   AL_CUDA(cudaStreamSynchronize(h->st));
   *out = h.release();
   return ARTLITE_OK;
@@ -222,135 +321,41 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
   AL_CHECK(T == 0 || (x && y), ARTLITE_EINVAL, "moe_forward: null x / y");
   const artlite_moe_desc& d = h->d;
   const artlite_moe::Layer& L = h->layers[layer];
-  const int H = d.hidden, E = d.n_experts, K = d.top_k, F = d.expert_ffn;
+  const int H = d.hidden, E = d.n_experts, K = d.top_k;
   const int64_t P = T * K;
   const size_t act = d.act_dtype == ARTLITE_BF16 ? 2 : 4;
   AL_CUDA(cudaSetDevice(h->dev));
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->st;
   h->last_T = T;
-  if (T == 0) return ARTLITE_OK;
-  const bool x_dev = is_device_ptr(x) && ((uintptr_t)x % 16) == 0;
-  const bool y_dev = is_device_ptr(y) && ((uintptr_t)y % 16) == 0;
+  if (T == 0 && h->E_local == E) return ARTLITE_OK;  // (with expert parallelism a rank without tokens still serves)
+  const bool x_dev = T > 0 && is_device_ptr(x) && ((uintptr_t)x % 16) == 0;
+  const bool y_dev = T > 0 && is_device_ptr(y) && ((uintptr_t)y % 16) == 0;
   const void* xd = x;
-  if (!x_dev) {
+  if (T > 0 && !x_dev) {
     AL_CUDA(cudaMemcpyAsync(h->xin.ptr, x, act * T * H, cudaMemcpyDefault, st));
     xd = h->xin.ptr;
   }
   void* yd = y_dev ? y : h->yout.ptr;
-  int ns = 0;
-  auto mark = [&]() -> int {
-    if (h->timing && ns < kStages) AL_CUDA(cudaEventRecord(h->ev[(size_t)layer * kStages + ns++], st));
-    return ARTLITE_OK;
-  };
-  AL_TRY(mark());
-  // 1. router logits
-  // (kernels of this forward: router, route, 3 dispatch, then 4 (gemv) or 6 (tc), then the combine)
-  if (L.n_planes)
-    AL_TRY(launch_router_tc(static_cast<const uint16_t*>(xd), L.planes.as<uint16_t>(), L.n_planes,
-                            L.has_bias ? L.bias.as<float>() : nullptr, T, H, E, T, h->logits.as<float>(),
-                            h->status.as<DevStatus>(), st));
-  else
-    AL_TRY(launch_router(xd, d.act_dtype, L.router.ptr, L.router_qtype, L.has_bias ? L.bias.as<float>() : nullptr, T,
-                         H, E, h->logits.as<float>(), st));
-  AL_TRY(mark());
-  // 2. routing
-  RouteArgs ra{h->logits.as<float>(), T, E, E, 0, E, K, d.gating, K <= 16 && E % 16 == 0 && E <= 512,
-               h->ids.as<int32_t>(), h->w.as<float>()};
-  AL_TRY(launch_route(ra, st));
-  // 3. dispatch
-  DispatchArgs da{};
-  da.ids = h->ids.as<int32_t>();
-  da.P = P;
-  da.E = E;
-  da.blk_counts = h->blk.as<int32_t>();
-  da.offsets = h->offsets.as<int64_t>();
-  da.perm = h->perm.as<int32_t>();
-  da.slot = h->slot.as<int32_t>();
-  da.counts = h->counts.as<int32_t>();
-  da.status = h->status.as<DevStatus>();
-  AL_TRY(launch_dispatch(da, st));
-  AL_TRY(mark());
-  const int path = choose_path(*h, T, L.qtype) == 2 && tc_supported(L.down_qtype, F, H) ? 2 : 1;
-  h->last_path = path;
-  h->paths[layer] = path;
-  if (path == 1) {
-    const int rt_gu = gemv_row_tile(F), rt_dn = gemv_row_tile(H);
-    AL_TRY(launch_unit_scan(h->counts.as<int32_t>(), E, kGemvTokens, F / rt_gu, h->unit_gu.as<int32_t>(), st));
-    AL_TRY(launch_unit_scan(h->counts.as<int32_t>(), E, kGemvTokens, H / rt_dn, h->unit_dn.as<int32_t>(), st));
-    ExpertGemvArgs g{};
-    g.qtype = L.qtype;
-    g.w0 = L.gate.as<uint8_t>();
-    g.w1 = L.up.as<uint8_t>();
-    g.row_bytes = L.rb_gu;
-    g.K = H;
-    g.N = F;
-    g.E = E;
-    g.x = xd;
-    g.x_dtype = d.act_dtype;
-    g.perm = h->perm.as<int32_t>();
-    g.offsets = h->offsets.as<int64_t>();
-    g.unit_off = h->unit_gu.as<int32_t>();
-    g.rt = rt_gu;
-    g.k = K;
-    g.out = h->h.as<float>();
-    AL_TRY(launch_gemv_gu(g, st));
-    AL_TRY(mark());
-    ExpertGemvArgs dn = g;
-    dn.qtype = L.down_qtype;
-    dn.w0 = L.down.as<uint8_t>();
-    dn.w1 = nullptr;
-    dn.row_bytes = L.rb_dn;
-    dn.K = F;
-    dn.N = H;
-    dn.x = h->h.ptr;
-    dn.x_dtype = ARTLITE_F32;
-    dn.unit_off = h->unit_dn.as<int32_t>();
-    dn.rt = rt_dn;
-    dn.out = h->y.as<float>();
-    AL_TRY(launch_gemv_down(dn, st));
-    AL_TRY(mark());
-    AL_TRY(launch_combine(h->y.ptr, ARTLITE_F32, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype,
-                          st));
+  Marker mk{h, layer, st};
+  AL_TRY(mk.mark());
+  if (h->E_local < E) {
+    AL_TRY(ep_forward(h, layer, xd, yd, T, st, mk));
   } else {
-    AL_TRY(launch_gather(xd, d.act_dtype, h->perm.as<int32_t>(), P, K, H, h->xp.as<uint16_t>(), st));
-    TcGemmArgs g{};
-    g.qtype = L.qtype;
-    g.w0 = L.gate.as<uint8_t>();
-    g.w1 = L.up.as<uint8_t>();
-    g.row_bytes = L.rb_gu;
-    g.K = H;
-    g.N = F;
-    g.E = E;
-    g.x = h->xp.as<uint16_t>();
-    g.x_rows = (int64_t)(h->xp.bytes / (sizeof(uint16_t) * H));
-    g.status = h->status.as<DevStatus>();
-    g.P = P;
-    g.offsets = h->offsets.as<int64_t>();
-    g.counts = h->counts.as<int32_t>();
-    g.sched = h->tiles.ptr;
-    g.out = h->h.as<uint16_t>();
-    AL_TRY(launch_tc_gemm(g, /*gu=*/true, st));
-    AL_TRY(mark());
-    TcGemmArgs dn = g;
-    dn.qtype = L.down_qtype;
-    dn.w0 = L.down.as<uint8_t>();
-    dn.w1 = nullptr;
-    dn.row_bytes = L.rb_dn;
-    dn.K = F;
-    dn.N = H;
-    dn.x = h->h.as<uint16_t>();
-    dn.x_rows = (int64_t)(h->h.bytes / (sizeof(uint16_t) * F));
-    dn.out = h->y.as<uint16_t>();
-    AL_TRY(launch_tc_gemm(dn, /*gu=*/false, st));
-    AL_TRY(mark());
-    AL_TRY(launch_combine(h->y.ptr, ARTLITE_BF16, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype,
-                          st));
+    AL_TRY(route_and_dispatch(h, L, xd, T, st, mk));
+    const int path = expert_path(*h, P, L);
+    h->last_path = path;
+    h->paths[layer] = path;
+    void* yrows;
+    int ydt;
+    AL_TRY(run_experts(h, L, path, xd, d.act_dtype, false, h->perm.as<int32_t>(), K, P, E, h->offsets.as<int64_t>(),
+                       h->counts.as<int32_t>(), 0, &yrows, &ydt, st, mk));
+    AL_TRY(launch_combine(yrows, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st));
   }
-  AL_TRY(mark());
-  h->n_stages[layer] = ns;
-  if (!y_dev) {
+  AL_TRY(mk.mark());
+  h->n_stages[layer] = mk.ns;
+  if (T > 0 && !y_dev) {
     AL_CUDA(cudaMemcpyAsync(y, yd, act * T * H, cudaMemcpyDefault, st));
-    AL_TRY(wait(st, 0));
+    AL_TRY(wait_deadline(st, 0));
     DevStatus s;
     AL_CUDA(cudaMemcpy(&s, h->status.ptr, sizeof s, cudaMemcpyDeviceToHost));
     if (s.code) {
@@ -381,7 +386,6 @@ int artlite_moe_sync(artlite_moe* h, int timeout_ms) {
   AL_CHECK(h, ARTLITE_EINVAL, "moe_sync: null handle");
   AL_CUDA(cudaSetDevice(h->dev));
   AL_TRY(wait(h->st, timeout_ms));
-  AL_CUDA(cudaDeviceSynchronize());
   DevStatus s;
   AL_CUDA(cudaMemcpy(&s, h->status.ptr, sizeof s, cudaMemcpyDeviceToHost));
   if (s.code) {
@@ -428,9 +432,10 @@ int64_t artlite_moe_launch_count(void) { return artlite::launch_count(); }
 int artlite_moe_destroy(artlite_moe* h) {
   if (!h) return ARTLITE_OK;
   cudaSetDevice(h->dev);
-  cudaStreamSynchronize(h->st);
+  if (!h->ep_failed) wait(h->st, 0);  // (bounded; after a failed exchange nothing is waited for)
   for (cudaEvent_t e : h->ev)
     if (e) cudaEventDestroy(e);
+  ep_destroy(h);
   cudaStreamDestroy(h->st);
   delete h;
   return ARTLITE_OK;

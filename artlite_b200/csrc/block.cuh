@@ -1,0 +1,94 @@
+// The MoE block handle's state, shared by block.cu (single GPU) and ep.cu (expert parallelism over NCCL).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "common.cuh"
+
+struct artlite_moe {
+  artlite_moe_desc d{};
+  int dev = 0;
+  cudaStream_t st = nullptr;
+  int E_local = 0, e0 = 0;  // this rank's experts [e0, e0 + E_local)
+  struct Layer {
+    artlite::DevBuf gate, up, down, router, bias, planes;
+    bool has_bias = false;
+    int n_planes = 0;  // the router's bf16 planes (router_split): 3 for an F32 router, 1 for BF16
+    int qtype = -1, down_qtype = -1, router_qtype = -1;
+    int64_t rb_gu = 0, rb_dn = 0;
+  };
+  std::vector<Layer> layers;
+  // workspaces
+  artlite::DevBuf xin, yout, logits, ids, w, offsets, perm, slot, counts, blk, unit_gu, unit_dn, status;
+  artlite::DevBuf h, y, xp, tiles;
+  int64_t last_T = 0;
+  int last_path = 0;
+  bool timing = false;
+  std::vector<cudaEvent_t> ev;  // [n_layers][kStages]: the last forward of each layer, read without a sync
+  std::vector<int> n_stages;    // per layer
+  std::vector<int> paths;       // per layer: the expert path of its last forward
+  // expert parallelism (ep.cu): the NCCL communicator, exchange buffers, pinned host copies of the counts
+  void* comm = nullptr;                // ncclComm_t
+  artlite::DevBuf ep_rcounts, ep_loff, ep_lcounts, ep_ident, ep_seg, xl, xr, yr, ys;
+  int32_t* hb_counts = nullptr;        // pinned: [E] this rank's pairs per expert, then [world x E_local] received
+  int64_t* hb_loff = nullptr;          // pinned: [E_local + 1] offsets of the received rows per local expert
+  int32_t* hb_lcounts = nullptr;       // pinned: [E_local] received rows per local expert
+  int64_t* hb_seg = nullptr;           // pinned: [3][world x E_local] the received segments (from, to, rows)
+  std::vector<int64_t> ep_send_off, ep_recv_pos, ep_send_base, ep_recv_base, ep_send_rows, ep_recv_rows;
+  int64_t ep_max_rows = 0;             // rows a rank can receive: max_tokens K world
+  bool ep_failed = false;              // an exchange failed: the communicator is aborted, never waited for
+};
+
+
+namespace artlite {
+
+constexpr int kStages = 8;
+
+// per-stage CUDA events of a forward (ARTLITE_MOE_TIMING=1)
+struct Marker {
+  artlite_moe* h;
+  int layer;
+  cudaStream_t st;
+  int ns = 0;
+  int mark() {
+    if (h->timing && ns < kStages) {
+      const cudaError_t e = cudaEventRecord(h->ev[(size_t)layer * kStages + ns++], st);
+      if (e != cudaSuccess) {
+        set_error("event record: %s", cudaGetErrorString(e));
+        return ARTLITE_ECUDA;
+      }
+    }
+    return ARTLITE_OK;
+  }
+};
+
+// router logits, routing and the dispatch over all E experts of T tokens x (device, act dtype) into the handle's
+// logits / ids / w / offsets / perm / slot / counts
+int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* x, int64_t T, cudaStream_t st,
+                       Marker& mk);
+
+// The experts of a forward over P rows for E_run experts (offsets / counts on the device): rows are the tokens x
+// through perm / k (gathered = false), or already gathered bf16 rows in expert order (gathered = true, perm = the
+// identity, k = 1). Output rows in the same order into *y_rows (the handle's y buffer), fp32 (GEMV path) or bf16
+// (tcgen05 path) in *y_dtype.
+int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const void* x, int x_dtype, bool gathered,
+                const int32_t* perm, int k, int64_t P, int E_run, const int64_t* offsets, const int32_t* counts,
+                int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk);
+
+// which expert path a forward of P pairs takes
+int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L);
+
+// a bounded wait for the work enqueued on st so far
+int wait_deadline(cudaStream_t st, int timeout_ms);
+
+// expert parallelism (ep.cu)
+int launch_segment_copy(const void* src, void* dst, const int64_t* s, const int64_t* d, const int64_t* n, int nseg,
+                        int64_t row_bytes, int64_t total_rows, cudaStream_t st);
+int ep_create(artlite_moe* h);
+int ep_forward(artlite_moe* h, int layer, const void* x, void* y, int64_t T, cudaStream_t st, Marker& mk);
+void ep_destroy(artlite_moe* h);
+
+}  // namespace artlite

@@ -33,7 +33,7 @@
 namespace artlite {
 namespace tc {
 
-constexpr int BM = 128, BNMAX = 256, BK = 64, KC = 256, S = 3, RMAX = 3;
+constexpr int BM = 128, BNMAX = 256, BK = 64, KC = 256, SMAX = 5, RMAX = 3;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BNMAX * BK * 2;
 constexpr int kThreads = 448;  // 14 warps: producer, MMA, 8 dequant, 4 epilogue
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at the B200's clocks
@@ -55,7 +55,7 @@ struct Params {
 };
 
 struct Smem {
-  uint64_t full_a[S], full_b[S], empty[S], raw_full[RMAX], raw_empty[RMAX], tfull[2], tempty[2];
+  uint64_t full_a[SMAX], full_b[SMAX], empty[SMAX], raw_full[RMAX], raw_empty[RMAX], tfull[2], tempty[2];
   uint32_t tmem_base;
   int abort;
 };
@@ -126,6 +126,8 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
+// a 32-lane x 32-column TMEM load, asynchronous: its registers are valid after tmem_wait32 on the same array (the
+// wait names them as operands, so no use of them moves above it)
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -135,7 +137,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait32(uint32_t (&v)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]),
+                 "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]),
+                 "+r"(v[23]), "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]),
+                 "+r"(v[30]), "+r"(v[31])
+               :
+               : "memory");
 }
 
 struct Tile {
@@ -299,23 +310,105 @@ struct RawSpan {
 
 // ---------------------------------------------------------------- the kernel
 
-template <int QT, bool GU>
+// the kernel's shared-memory pipeline depth: A + B stages and raw weight stages, per format and mode
+__host__ __device__ constexpr int b_stage_bytes(bool pair) { return pair ? B_BYTES / 2 : B_BYTES; }
+__host__ __device__ constexpr int ab_stages(int qt, bool pair) { return pair ? (qt == ARTLITE_Q8_0 ? 4 : 5) : 3; }
+__host__ __device__ constexpr size_t smem_bytes(int qt, bool pair) {
+  return 1024 + (size_t)ab_stages(qt, pair) * (A_BYTES + b_stage_bytes(pair)) +
+         (size_t)raw_stages(qt) * BM * chunk_bytes(qt) + 512;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the shared::cluster address of this CTA's variable at p in cluster CTA `rank`
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// the pair's TMA load: the bytes land in this CTA, the transaction count goes to the barrier at `bar` (a
+// shared::cluster address, here the leader CTA's)
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+// MMA completion to the barrier at the same offset in both CTAs of the pair
+__device__ __forceinline__ void commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+// a wait whose barrier also receives the peer CTA's arrivals (acquire at cluster scope)
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool wait_cluster(int* abort, uint64_t* bar, uint32_t parity, DevStatus* st, int where) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*(volatile int*)abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *(volatile int*)abort = 1;
+      report(st, ARTLITE_ETIMEOUT, where, (int)blockIdx.x, 0);
+      return false;
+    }
+  }
+}
+
+// PAIR: a cluster of two CTAs on two SMs runs each tile as one M = 256 MMA (tcgen05 cta_group::2): each CTA
+// dequantises its own 128 weight rows (A halves) and loads half of the tile's token rows (B halves, N / 2 each), the
+// leader CTA issues the MMAs, whose completion is committed to both CTAs' barriers; each CTA's TMEM holds its 128
+// rows of the accumulator and its epilogue writes them. Per SM the token rows come from L2 once per 256 weight rows
+// instead of once per 128.
+template <int QT, bool GU, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_constant__ Params p) {
   constexpr int CB = chunk_bytes(QT);
   constexpr int NW = CB / 4;
   constexpr int R = raw_stages(QT);
+  constexpr int SS = ab_stages(QT, PAIR);
+  constexpr int BB = b_stage_bytes(PAIR);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = base;
-  uint8_t* sB = sA + S * A_BYTES;
-  uint8_t* sR = sB + S * B_BYTES;
+  uint8_t* sB = sA + SS * A_BYTES;
+  uint8_t* sR = sB + SS * BB;
   Smem* sm = reinterpret_cast<Smem*>(sR + R * BM * CB);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = p.toff[p.E];
+  const uint32_t crank = PAIR ? cluster_rank() : 0;  // 0: the leader
+  const int t0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  constexpr int NPEER = PAIR ? 2 : 1;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; i++) {
-      mbar_init(&sm->full_a[i], 4);
+    for (int i = 0; i < SS; i++) {
+      mbar_init(&sm->full_a[i], 4 * NPEER);
       mbar_init(&sm->full_b[i], 1);
       mbar_init(&sm->empty[i], 1);
     }
@@ -325,73 +418,99 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&sm->tfull[i], 1);
-      mbar_init(&sm->tempty[i], 4);
+      mbar_init(&sm->tempty[i], 4 * NPEER);
     }
     sm->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm->tmem_base)),
-                 "r"(512));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm->tmem_base)),
+                   "r"(512));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm->tmem_base)),
+                   "r"(512));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();
+  else __syncthreads();
   fence_after();
   const uint32_t tmem = sm->tmem_base;
   const int ksteps = p.K / BK;
 
   if (warp == 0 && lane == 0) {
-    // ---------------- producer of the token rows (B stages)
+    // ---------------- producer of the token rows (B stages; in a pair each CTA its half, counted by the leader)
     int s = 0, sph = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    for (int t = t0; t < total; t += tstep) {
       const Tile T = tile_of(p, t);
+      const int half = T.n_mma / 2;
       for (int ks = 0; ks < ksteps; ks++) {
         if (!wait(&sm->abort, &sm->empty[s], sph ^ 1, p.status, 2)) goto out;
-        mbar_expect_tx(&sm->full_b[s], B_BYTES);
-        tma_load_2d(sB + s * B_BYTES, &p.map_x, &sm->full_b[s], ks * BK, (int)T.row0);
-        if (++s == S) s = 0, sph ^= 1;
+        if constexpr (PAIR) {
+          if (crank == 0) mbar_expect_tx(&sm->full_b[s], 2 * BB);
+          tma_load_2d_pair(sB + s * BB, &p.map_x, peer_addr(&sm->full_b[s], 0), ks * BK,
+                           (int)T.row0 + (int)crank * half);
+        } else {
+          mbar_expect_tx(&sm->full_b[s], BB);
+          tma_load_2d(sB + s * BB, &p.map_x, &sm->full_b[s], ks * BK, (int)T.row0);
+        }
+        if (++s == SS) s = 0, sph ^= 1;
       }
     }
   } else if (warp == 0 && lane == 1) {
     // ---------------- producer of the raw weight rows (R stages of 256 values, ahead of the B stages)
     int r = 0, rph = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    for (int t = t0; t < total; t += tstep) {
       const Tile T = tile_of(p, t);
+      const int m = NPEER * T.m + (int)crank;  // this CTA's 64 features (gu) / 128 rows (down)
       for (int kc = 0; kc < p.K / KC; kc++) {
         if (!wait(&sm->abort, &sm->raw_empty[r], rph ^ 1, p.status, 1)) goto out;
         uint8_t* dst = sR + r * BM * CB;
         mbar_expect_tx(&sm->raw_full[r], BM * CB);
         if (GU) {
-          const int row = T.e * p.N + 64 * T.m;
+          const int row = T.e * p.N + 64 * m;
           tma_load_2d(dst, &p.map_w0, &sm->raw_full[r], kc * (CB / 2), row);
           tma_load_2d(dst + 64 * CB, &p.map_w1, &sm->raw_full[r], kc * (CB / 2), row);
         } else {
-          tma_load_2d(dst, &p.map_w0, &sm->raw_full[r], kc * (CB / 2), T.e * p.N + BM * T.m);
+          tma_load_2d(dst, &p.map_w0, &sm->raw_full[r], kc * (CB / 2), T.e * p.N + BM * m);
         }
         if (++r == R) r = 0, rph ^= 1;
       }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
+  } else if (warp == 1 && lane == 0 && crank == 0) {
+    // ---------------- MMA issuer (the leader of a pair)
     int s = 0, sph = 0, acc = 0, aph = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    for (int t = t0; t < total; t += tstep) {
       const Tile T = tile_of(p, t);
-      if (!wait(&sm->abort, &sm->tempty[acc], aph ^ 1, p.status, 3)) goto out;
+      if (!(PAIR ? wait_cluster(&sm->abort, &sm->tempty[acc], aph ^ 1, p.status, 3)
+                 : wait(&sm->abort, &sm->tempty[acc], aph ^ 1, p.status, 3)))
+        goto out;
       fence_after();
-      const uint32_t id = idesc(BM, T.n_mma);
+      const uint32_t id = idesc(PAIR ? 2 * BM : BM, T.n_mma);
       const uint32_t d = tmem + acc * BNMAX;
       for (int ks = 0; ks < ksteps; ks++) {
-        if (!wait(&sm->abort, &sm->full_a[s], sph, p.status, 4)) goto out;
-        if (!wait(&sm->abort, &sm->full_b[s], sph, p.status, 5)) goto out;
+        if (!(PAIR ? wait_cluster(&sm->abort, &sm->full_a[s], sph, p.status, 4)
+                   : wait(&sm->abort, &sm->full_a[s], sph, p.status, 4)))
+          goto out;
+        if (!(PAIR ? wait_cluster(&sm->abort, &sm->full_b[s], sph, p.status, 5)
+                   : wait(&sm->abort, &sm->full_b[s], sph, p.status, 5)))
+          goto out;
         fence_after();
-        const uint64_t da = sdesc(smem_u32(sA + s * A_BYTES)), db = sdesc(smem_u32(sB + s * B_BYTES));
+        const uint64_t da = sdesc(smem_u32(sA + s * A_BYTES)), db = sdesc(smem_u32(sB + s * BB));
 #pragma unroll
-        for (int k = 0; k < BK / 16; k++) mma(d, da + 2 * k, db + 2 * k, id, (ks | k) != 0);
-        commit(&sm->empty[s]);
-        if (++s == S) s = 0, sph ^= 1;
+        for (int k = 0; k < BK / 16; k++) {
+          if constexpr (PAIR) mma_pair(d, da + 2 * k, db + 2 * k, id, (ks | k) != 0);
+          else mma(d, da + 2 * k, db + 2 * k, id, (ks | k) != 0);
+        }
+        if constexpr (PAIR) commit_pair(&sm->empty[s]);
+        else commit(&sm->empty[s]);
+        if (++s == SS) s = 0, sph ^= 1;
       }
-      commit(&sm->tfull[acc]);
+      if constexpr (PAIR) commit_pair(&sm->tfull[acc]);
+      else commit(&sm->tfull[acc]);
       if (++acc == 2) acc = 0, aph ^= 1;
     }
   } else if (warp >= 2 && warp < 10) {
@@ -404,7 +523,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
       raw_row = l < 16 ? 16 * q + l : 64 + 16 * q + (l - 16);
     }
     int n = 0, r = 0, rph = 0;  // n: the step counter shared with the producer and the MMA issuer
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    const uint32_t full_a0 = PAIR ? peer_addr(&sm->full_a[0], 0) : 0;  // (the leader's barriers, for a peer's arrivals)
+    for (int t = t0; t < total; t += tstep) {
       for (int kc = 0; kc < p.K / KC; kc++) {
         if (!wait(&sm->abort, &sm->raw_full[r], rph, p.status, 6)) goto out;
         uint32_t w[NW + 4];
@@ -433,8 +553,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
 #pragma unroll
         for (int j = 0; j < 2; j++) {
           const int sub = 2 * grp + j;
-          const int step = n + sub, s = step % S;
-          const uint32_t ph = (step / S) & 1;
+          const int step = n + sub, s = step % SS;
+          const uint32_t ph = (step / SS) & 1;
           uint32_t o[32];
           if (grp == 0) dequant_step<QT>(w, j, o);
           else dequant_step<QT>(w, 2 + j, o);
@@ -445,7 +565,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
             *reinterpret_cast<uint4*>(row + ((c ^ (i & 7)) << 4)) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sm->full_a[s]);
+          if (lane == 0) {
+            if (PAIR && crank != 0) arrive_cluster(full_a0 + s * (uint32_t)sizeof(uint64_t));
+            else mbar_arrive(&sm->full_a[s]);
+          }
         }
         n += KC / BK;
       }
@@ -454,13 +577,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
     // ---------------- epilogue: TMEM lanes 32 q .. 32 q + 31
     const int q = warp & 3;
     int acc = 0, aph = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const Tile T = tile_of(p, t);
+    const uint32_t tempty0 = PAIR ? peer_addr(&sm->tempty[0], 0) : 0;
+    for (int t = t0; t < total; t += tstep) {
+      Tile T = tile_of(p, t);
+      T.m = NPEER * T.m + (int)crank;  // this CTA's rows
       if (!wait(&sm->abort, &sm->tfull[acc], aph, p.status, 8)) goto out;
       fence_after();
-      for (int c0 = 0; c0 < T.n_mma; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + acc * BNMAX + c0, v);
+      // 32 columns at a time, the next chunk's TMEM load in flight while this chunk is stored
+      const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + acc * BNMAX;
+      const int nch = (T.n_mma + 31) / 32;
+      auto emit = [&](const uint32_t(&v)[32], int c0) {
         if (GU) {
           const bool gate = lane < 16;
           const int f = 64 * T.m + 16 * q + (lane & 15);
@@ -483,10 +609,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
             if (c0 + j < T.valid)
               p.out[(T.row0 + c0 + j) * p.N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j])));
         }
+      };
+      uint32_t va[32], vb[32];
+      tmem_ld32(base, va);
+      tmem_wait32(va);
+      for (int c = 0; c < nch; c += 2) {
+        if (c + 1 < nch) tmem_ld32(base + 32 * (c + 1), vb);
+        emit(va, 32 * c);
+        if (c + 1 < nch) {
+          tmem_wait32(vb);
+          if (c + 2 < nch) tmem_ld32(base + 32 * (c + 2), va);
+          emit(vb, 32 * (c + 1));
+          if (c + 2 < nch) tmem_wait32(va);
+        }
       }
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm->tempty[acc]);
+      if (lane == 0) {
+        if (PAIR && crank != 0) arrive_cluster(tempty0 + acc * (uint32_t)sizeof(uint64_t));
+        else mbar_arrive(&sm->tempty[acc]);
+      }
       if (++acc == 2) acc = 0, aph ^= 1;
     }
   }
@@ -498,10 +640,12 @@ out:
     while (clock64() - t0 < 20000000LL) {
     }
   }
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // (the leader's MMAs read the peer's shared memory until here)
+  else __syncthreads();
   if (warp == 0) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    if constexpr (PAIR) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    else asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
   }
 }
 
@@ -602,6 +746,7 @@ __global__ void __launch_bounds__(rt::kThreads, 1) router_tc_kernel(const __grid
     for (int c0 = 0; c0 < BN; c0 += 32) {
       uint32_t v[32];
       tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + c0, v);
+      tc::tmem_wait32(v);
 #pragma unroll
       for (int j = 0; j < 32; j++)
         if (c0 + j < valid) p.logits[(t0 + c0 + j) * p.E + e] = __uint_as_float(v[j]) + b;
@@ -722,6 +867,14 @@ bool tc_supported(int qtype, int K, int N) {
 
 size_t tc_sched_bytes(int E) { return sizeof(int32_t) * (E + 1); }
 
+// the pair (cta_group::2) kernel with ARTLITE_TC_PAIR=1 (measured slower than the one-CTA kernel at the benchmark's
+// shapes: the token operand's L2 traffic is not what bounds it), when the shape splits into pairs
+bool tc_use_pair(int N, bool gu) {
+  const char* v = getenv("ARTLITE_TC_PAIR");
+  const bool on = v && v[0] == '1';
+  return on && (gu ? N % 128 == 0 : N % 256 == 0);
+}
+
 int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
   AL_CHECK(tc_supported(a.qtype, a.K, a.N), ARTLITE_EUNSUPPORTED, "tc gemm: type %d K %d N %d", a.qtype, a.K, a.N);
   AL_CHECK(a.row_bytes % 16 == 0 && a.row_bytes == (int64_t)a.K / tc::KC * tc::chunk_bytes(a.qtype), ARTLITE_EINVAL,
@@ -731,14 +884,15 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
   AL_CHECK(a.x_rows >= a.P + tc::BNMAX, ARTLITE_EINVAL, "tc gemm: x holds %lld rows, needs %lld", (long long)a.x_rows,
            (long long)(a.P + tc::BNMAX));
   if (a.P == 0) return ARTLITE_OK;
-  const int MT = gu ? a.N / 64 : a.N / tc::BM;
+  const bool pair = tc_use_pair(a.N, gu);
+  const int MT = (gu ? a.N / 64 : a.N / tc::BM) / (pair ? 2 : 1);  // tiles of weight rows per token tile
   tc::Params p{};
   const int cb = tc::chunk_bytes(a.qtype);
   const int64_t wrows = (int64_t)a.E * a.N;
   AL_TRY(make_map(&p.map_w0, a.w0, a.row_bytes / 2, wrows, cb / 2, gu ? 64 : tc::BM, false));
   if (gu) AL_TRY(make_map(&p.map_w1, a.w1, a.row_bytes / 2, wrows, cb / 2, 64, false));
   else p.map_w1 = p.map_w0;
-  AL_TRY(make_map(&p.map_x, a.x, a.K, a.x_rows, tc::BK, tc::BNMAX, true));
+  AL_TRY(make_map(&p.map_x, a.x, a.K, a.x_rows, tc::BK, pair ? tc::BNMAX / 2 : tc::BNMAX, true));
   AL_TRY(launch_unit_scan(a.counts, a.E, tc::BNMAX, MT, static_cast<int32_t*>(a.sched), st));
   p.offsets = a.offsets;
   p.toff = static_cast<const int32_t*>(a.sched);
@@ -748,23 +902,43 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
   p.K = a.K;
   p.N = a.N;
   p.MT = MT;
-  const size_t smem = 1024 + tc::S * (tc::A_BYTES + tc::B_BYTES) + tc::raw_stages(a.qtype) * tc::BM * cb +
-                      sizeof(tc::Smem) + 64;
+  const size_t smem = tc::smem_bytes(a.qtype, pair);
   int dev, sms;
   AL_CUDA(cudaGetDevice(&dev));
   AL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   auto go = [&](auto kern) -> int {
     AL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<sms, tc::kThreads, smem, st>>>(p);
+    if (pair) {
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3((unsigned)(sms & ~1));
+      cfg.blockDim = dim3(tc::kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      AL_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
+    } else {
+      kern<<<sms, tc::kThreads, smem, st>>>(p);
+    }
     AL_LAUNCHED();
     return ARTLITE_OK;
   };
+#define AL_TC_CASE(QT)                                                                              \
+  case QT:                                                                                          \
+    return pair ? (gu ? go(tc::tc_expert_gemm<QT, true, true>) : go(tc::tc_expert_gemm<QT, false, true>)) \
+                : (gu ? go(tc::tc_expert_gemm<QT, true, false>) : go(tc::tc_expert_gemm<QT, false, false>));
   switch (a.qtype) {
-    case ARTLITE_Q4_0: return gu ? go(tc::tc_expert_gemm<ARTLITE_Q4_0, true>) : go(tc::tc_expert_gemm<ARTLITE_Q4_0, false>);
-    case ARTLITE_Q8_0: return gu ? go(tc::tc_expert_gemm<ARTLITE_Q8_0, true>) : go(tc::tc_expert_gemm<ARTLITE_Q8_0, false>);
-    case ARTLITE_Q4_K: return gu ? go(tc::tc_expert_gemm<ARTLITE_Q4_K, true>) : go(tc::tc_expert_gemm<ARTLITE_Q4_K, false>);
+    AL_TC_CASE(ARTLITE_Q4_0)
+    AL_TC_CASE(ARTLITE_Q8_0)
+    AL_TC_CASE(ARTLITE_Q4_K)
     default: break;
   }
+#undef AL_TC_CASE
   set_error("tc gemm: type %d", a.qtype);
   return ARTLITE_EUNSUPPORTED;
 }

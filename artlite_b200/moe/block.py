@@ -15,6 +15,26 @@ from .._lib import QTYPES, Error, MoeDesc, check, lib
 PATHS = {"auto": 0, "gemv": 1, "tc": 2}
 
 
+def ep_unique_id() -> bytes:
+    """A new NCCL unique id (128 bytes) for ``MoEBlock.ep_init``."""
+    buf = ctypes.create_string_buffer(128)
+    check(lib().artlite_moe_ep_unique_id(buf, 128))
+    return buf.raw
+
+
+def ep_plan(send_counts: np.ndarray, recv_counts: np.ndarray, world: int, rank: int, E: int):
+    """The exchange plan of one rank (``artlite_moe_ep_plan``, host only): (send_off (E,), recv_pos (world, E / world),
+    local_off (E / world + 1,), local_counts (E / world,))."""
+    El = E // world
+    sc = np.ascontiguousarray(send_counts, np.int32)
+    rc = np.ascontiguousarray(recv_counts, np.int32).reshape(world * El)
+    send_off, recv_pos = np.zeros(E, np.int64), np.zeros((world, El), np.int64)
+    local_off, local_counts = np.zeros(El + 1, np.int64), np.zeros(El, np.int32)
+    check(lib().artlite_moe_ep_plan(sc.ctypes.data, rc.ctypes.data, world, rank, E, send_off.ctypes.data,
+                                    recv_pos.ctypes.data, local_off.ctypes.data, local_counts.ctypes.data))
+    return send_off, recv_pos, local_off, local_counts
+
+
 def _ptr(a) -> int:
     """A host array's address, or a device address given as an int / an object with ``data_ptr()``."""
     if isinstance(a, np.ndarray):
@@ -34,17 +54,23 @@ class MoEBlock:
 
     def __init__(self, *, hidden: int, n_experts: int, top_k: int, expert_ffn: int, max_tokens: int,
                  n_layers: int = 1, gating: str = "softmax", act_dtype: str = "bf16", device: int = -1,
-                 path: str = "auto"):
+                 path: str = "auto", ep_rank: int = 0, ep_world: int = 1):
         assert gating in ("softmax", "sigmoid") and act_dtype in ("f32", "bf16") and path in PATHS
         self.H, self.E, self.K, self.F = hidden, n_experts, top_k, expert_ffn
         self.act = act_dtype
         self.max_tokens = max_tokens
         d = MoeDesc(hidden=hidden, n_experts=n_experts, top_k=top_k, expert_ffn=expert_ffn, n_layers=n_layers,
                     gating=int(gating == "sigmoid"), act_dtype=QTYPES["BF16" if act_dtype == "bf16" else "F32"],
-                    max_tokens=max_tokens, device=device, path=PATHS[path], ep_rank=0, ep_world=1)
+                    max_tokens=max_tokens, device=device, path=PATHS[path], ep_rank=ep_rank, ep_world=ep_world)
         h = ctypes.c_void_p()
         check(lib().artlite_moe_create(ctypes.byref(d), ctypes.byref(h)))
         self._h = h
+
+    def ep_init(self, unique_id: bytes) -> None:
+        """Joins this rank's block to the NCCL communicator of ``unique_id`` (from ``ep_unique_id`` on one rank,
+        shared with the others by the caller): collective over the ``ep_world`` ranks."""
+        buf = ctypes.create_string_buffer(bytes(unique_id), len(unique_id))
+        check(lib().artlite_moe_ep_init(self._h, buf, len(unique_id)))
 
     @property
     def np_dtype(self):

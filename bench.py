@@ -12,8 +12,9 @@ router fp32 N(0, 0.02); x bf16 N(0, 1)) and handed to the library as raw GGUF bl
 the timed region; the weights stream from HBM each layer (340 MB a layer, far above the 126 MB L2, so no L2 flush is
 needed). The timed region: W untimed steps, then K steps between CUDA events on the launching stream, a barrier and
 a synchronize on both sides, the max over ranks. `e2e`: the same steps through the C ABI with pinned HOST x / y buffers
-(the library copies x in and y out on every call, inside the timed region). With N > 1 every rank runs the whole stack
-on its own batch (experts replicated, no collective): weak scaling.
+(the library copies x in and y out on every call, inside the timed region). With N > 1 the block is expert-parallel:
+rank r owns experts [r E / N, (r + 1) E / N) and T / N of the 16384 tokens; every layer exchanges token rows and
+expert outputs over NCCL (artlite_b200/csrc/ep.cu): strong scaling (the total work is fixed).
 
 `roofline`: the dominant kernel (the tcgen05 gate/up GEMM), its algorithmic FLOPs per launch (2 P H 2F, P = T K pairs)
 over its average duration from CUDA events recorded between the forward's kernels on the forward's stream during the
@@ -143,7 +144,7 @@ def run_reference(args) -> None:
     sample = f"{T} tokens x 1 layer of the workload per step (router, routing, moe_ffn with the dequant of the " \
              f"experts they touch); numpy BLAS and the reference's dequant threads on all host cores"
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy: oracle.moe_np.make_block)",
             "config": {"workload": WORKLOAD, "tokens_per_step": T, "layers_per_step": 1, "hidden": H, "experts": E,
                        "top_k": K, "expert_ffn": F, "qtype": QTYPE},
@@ -201,17 +202,25 @@ def main() -> None:
     from artlite_b200 import _lib
     from artlite_b200.moe.block import MoEBlock
 
-    L, T = args.layers, args.tokens
+    L = args.layers
+    assert args.tokens % world == 0 and E % world == 0
+    T = args.tokens // world  # this rank's tokens
     block = MoEBlock(hidden=H, n_experts=E, top_k=K, expert_ffn=F, max_tokens=T, n_layers=L, act_dtype="bf16",
-                     device=local, path="auto")
+                     device=local, path="auto", ep_rank=rank, ep_world=world)
     g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
+    g.manual_seed(1000)  # the same weights on every rank (each keeps its own experts' rows)
     for layer in range(L):
         gate, up, down, router = gen_layer(torch, g, dev)
         block.set_weights(layer, gate=gate.data_ptr(), up=up.data_ptr(), down=down.data_ptr(),
                           router=router.data_ptr(), qtype=QTYPE)
         del gate, up, down, router
     torch.cuda.empty_cache()
+    if world > 1:
+        from artlite_b200.moe.block import ep_unique_id
+        uid = [ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        block.ep_init(uid[0])
+    g.manual_seed(2000 + rank)
     x = (torch.randn((T, H), generator=g, device=dev)).to(torch.bfloat16)
     ys = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     stream = torch.cuda.Stream(device=dev)
@@ -252,7 +261,7 @@ def main() -> None:
         dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     ms_total = float(t_max.item())
     ms_step = ms_total / args.steps
-    value = world * T * L / (ms_step / 1000.0)
+    value = world * T * L / (ms_step / 1000.0)  # all ranks' tokens x layers per second
 
     # e2e: the C ABI with pinned host x / y (copies inside the timed region)
     e2e = None
@@ -285,42 +294,47 @@ def main() -> None:
         e2e = {"value": world * T * L / (e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": L * T * H * 2,
                "d2h_bytes_per_step": L * T * H * 2, "ms_per_step": e_ms}
 
+    # (every rank closes its block, then leaves the process group together)
+    block.close()
+    barrier()
+    if world > 1:
+        dist.destroy_process_group()
     if rank != 0:
-        if world > 1:
-            dist.destroy_process_group()
         return
     peaks, peak_src = measured_peaks()
     # stages (tc path): router, route+dispatch, gather + gate/up, down, combine
     roof = None
     if path == "tc" and stages.shape[1] >= 4:
-        gu_ms = float(stages[:, 2].mean())
+        gu_ms = float(stages[:, 3 if world > 1 else 2].mean())
         P = T * K
         flops = 2.0 * P * H * (2 * F)
         achieved = flops / (gu_ms / 1000.0) / 1e12
         peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
-        roof = {"kernel": "tc_expert_gemm<Q4_0, gate/up> (+ the dispatch gather, same stage)", "bound": "tensor",
+        roof = {"kernel": "tc_expert_gemm<Q4_0, gate/up>" + ("" if world > 1 else " (+ the dispatch gather, same stage)"),
+                "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "traffic": traffic_from_profiles(), "peak_source": f"{peak_src} bf16_tflops_sustained",
                 "flops_per_launch": flops, "ms_per_launch": gu_ms}
-    stage_names = ["router", "route+dispatch", "gather+gate_up", "down", "combine"] if path == "tc" else \
-        ["router", "route+dispatch", "gate_up", "down", "combine"]
+    if world > 1:
+        stage_names = ["router", "route+dispatch", "gather+count/row exchange", "gate_up", "down", "return exchange",
+                       "combine"]
+    else:
+        stage_names = ["router", "route+dispatch", "gather+gate_up", "down", "combine"] if path == "tc" else \
+            ["router", "route+dispatch", "gate_up", "down", "combine"]
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_tokens)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded torch CUDA generator: Q4_0 d=|N(0,0.02)| fp16, nibbles uniform; x bf16 N(0,1))",
-            "config": {"workload": WORKLOAD, "layers": L, "tokens_per_rank": T, "hidden": H, "experts": E, "top_k": K,
-                       "expert_ffn": F, "qtype": QTYPE, "path": path,
-                       "parallelism": "replicas" if world > 1 else "single",
+            "config": {"workload": WORKLOAD, "layers": L, "tokens": T * world, "tokens_per_rank": T, "hidden": H,
+                       "experts": E, "top_k": K, "expert_ffn": F, "qtype": QTYPE, "path": path,
+                       "parallelism": f"ep{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (340 MB of weights streamed per layer)"},
             "stage_ms_mean": dict(zip(stage_names, [float(v) for v in stages.mean(0)])),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clk}
     print(json.dumps(line), flush=True)
-    block.close()
-    if world > 1:
-        dist.destroy_process_group()
 
 
 def traffic_from_profiles():

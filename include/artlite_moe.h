@@ -177,6 +177,29 @@ int64_t artlite_moe_launch_count(void);
 
 int artlite_moe_destroy(artlite_moe* h);
 
+/* ---------------------------------------------------------------- expert parallelism (ep_world > 1)
+ * The reference runs on one NPU and has no counterpart (its closest analogue is the 8-column deal of moe_plan,
+ * moe_host.cpp:256-274, an intra-device split). One process per GPU; rank r of W owns experts [r E / W, (r + 1) E / W)
+ * and its own tokens; artlite_moe_forward exchanges token rows and expert outputs with NCCL (loaded at run time:
+ * libnccl.so.2, or ARTLITE_NCCL_LIB). */
+
+/* A new NCCL unique id (NCCL_UNIQUE_ID_BYTES = 128 bytes into out): made on one rank, shared with the others. */
+int artlite_moe_ep_unique_id(void* out, int bytes);
+
+/* Joins the handle (created with ep_world = W, ep_rank = r) to the communicator of unique_id; collective over the W
+ * ranks. */
+int artlite_moe_ep_init(artlite_moe* h, const void* unique_id, int bytes);
+
+/*
+ * The exchange plan of one rank (host only, no GPU): send_counts (E) this rank's pairs per expert; recv_counts
+ * (world x E / world) the pairs each rank sends for this rank's experts. Out: send_off (E) each expert's first row in
+ * this rank's expert-ordered rows; recv_pos (world x E / world) where the rows from rank q for local expert e land in
+ * the received rows (grouped by local expert, then by rank); local_off (E / world + 1) / local_counts (E / world) the
+ * received rows per local expert.
+ */
+int artlite_moe_ep_plan(const int32_t* send_counts, const int32_t* recv_counts, int world, int rank, int E,
+                        int64_t* send_off, int64_t* recv_pos, int64_t* local_off, int32_t* local_counts);
+
 #ifdef __cplusplus
 }
 #endif

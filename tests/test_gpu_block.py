@@ -104,6 +104,21 @@ def test_prefill_zipf_q8():
     assert moe_np.rel_max(y[tok], oracle_y(layer, x, ids, w, tokens=tok)) <= BF16_TOL
 
 
+@pytest.mark.parametrize("qtype", ["Q4_0", "Q8_0", "Q4_K"])
+def test_tcgen05_single_and_pair_agree(qtype, monkeypatch):
+    """The one-CTA and the two-CTA (cta_group::2) tcgen05 kernels agree (the same bf16 operands and K order: equal up
+    to the tensor core's accumulation within an instruction); the shape splits into pairs (F % 128 == 0,
+    H % 256 == 0)."""
+    layer, x, _ = moe_np.make_block(12, 333, qtype=qtype, E=16, H=512, F=256)
+    monkeypatch.setenv("ARTLITE_TC_PAIR", "0")
+    y1, _ = run(layer, x, act="bf16", path="tc", T=333)
+    monkeypatch.setenv("ARTLITE_TC_PAIR", "1")
+    y2, dbg = run(layer, x, act="bf16", path="tc", T=333)
+    assert moe_np.rel_max(y2, y1) <= 2e-3
+    ids, w = check_routing(dbg, x, layer, 8)
+    assert moe_np.rel_max(y2, oracle_y(layer, x, ids, w)) <= BF16_TOL
+
+
 def test_paths_agree():
     """The GEMV and the tcgen05 path on the same input (Q4_0, T=256)."""
     layer, x, _ = moe_np.make_block(8, 256, qtype="Q4_0", E=32, H=1024, F=512)
