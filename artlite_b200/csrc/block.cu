@@ -29,6 +29,10 @@ namespace artlite {
 namespace {
 
 int status_error(const DevStatus& s, int E) {
+  if (s.code == ARTLITE_ETIMEOUT) {
+    set_error("moe: a bounded device wait ran out (site %d, block %d)", s.a, s.b);
+    return ARTLITE_ETIMEOUT;
+  }
   if (s.code == ARTLITE_EDEVICE) {
     set_error("moe: expert id %d of %d from the routing", s.a, E);
     return ARTLITE_EDEVICE;
@@ -83,11 +87,14 @@ int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L) {
 }
 
 int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* xd, int64_t T, cudaStream_t st,
-                       Marker& mk) {
+                       Marker& mk, int mult_gu, int mult_dn) {
   const artlite_moe_desc& d = h->d;
   const int H = d.hidden, E = d.n_experts, K = d.top_k;
   if (T > 0) {
-    if (L.n_planes)
+    if (router_small_ok(T, H))
+      AL_TRY(launch_router_small(xd, d.act_dtype, L.router.ptr, L.router_qtype, L.has_bias ? L.bias.as<float>() : nullptr,
+                                 T, H, E, h->logits.as<float>(), st));
+    else if (L.n_planes)
       AL_TRY(launch_router_tc(static_cast<const uint16_t*>(xd), L.planes.as<uint16_t>(), L.n_planes,
                               L.has_bias ? L.bias.as<float>() : nullptr, T, H, E, T, h->logits.as<float>(),
                               h->status.as<DevStatus>(), st));
@@ -98,7 +105,6 @@ int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* 
   AL_TRY(mk.mark());
   RouteArgs ra{h->logits.as<float>(), T, E, E, 0, E, K, d.gating, K <= 16 && E % 16 == 0 && E <= 512,
                h->ids.as<int32_t>(), h->w.as<float>()};
-  AL_TRY(launch_route(ra, st));
   DispatchArgs da{};
   da.ids = h->ids.as<int32_t>();
   da.P = T * K;
@@ -109,22 +115,46 @@ int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* 
   da.slot = h->slot.as<int32_t>();
   da.counts = h->counts.as<int32_t>();
   da.status = h->status.as<DevStatus>();
-  AL_TRY(launch_dispatch(da, st));
+  if (mult_gu > 0 && T > 0) {  // decode-sized: one kernel, with the GEMVs' unit scans
+    da.unit_rows = kGemvTokens;
+    da.unit_mult = mult_gu;
+    da.unit_off = h->unit_gu.as<int32_t>();
+    AL_TRY(launch_route_dispatch_small(ra, da, mult_dn, h->unit_dn.as<int32_t>(), st));
+  } else {
+    AL_TRY(launch_route(ra, st));
+    AL_TRY(launch_dispatch(da, st));
+  }
   return mk.mark();
+}
+
+// The decode-sized plan of a forward: both GEMVs' items per expert and token group (0, 0 when the fused routing /
+// dispatch kernel does not apply).
+void small_plan(const artlite_moe& h, const artlite_moe::Layer& L, int path, int64_t T, int* mult_gu, int* mult_dn) {
+  const artlite_moe_desc& d = h.d;
+  *mult_gu = *mult_dn = 0;
+  if (path != 1 || T <= 0 || !small_dispatch_ok(T * d.top_k, d.n_experts) || !router_small_ok(T, d.hidden)) return;
+  const int rt_gu = gemv_row_tile(L.qtype, d.hidden, d.expert_ffn, true);
+  const int rt_dn = gemv_row_tile(L.down_qtype, d.expert_ffn, d.hidden, false);
+  if (rt_gu <= 0 || rt_dn <= 0) return;
+  *mult_gu = (int)cdiv(d.expert_ffn, rt_gu);
+  *mult_dn = (int)cdiv(d.hidden, rt_dn);
 }
 
 int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const void* x, int x_dtype, bool gathered,
                 const int32_t* perm, int k, int64_t P, int E_run, const int64_t* offsets, const int32_t* counts,
-                int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk) {
+                int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk, bool units_ready) {
   const artlite_moe_desc& d = h->d;
   const int H = d.hidden, F = d.expert_ffn;
   *y_rows = h->y.ptr;
   if (path == 1) {
     *y_dtype = ARTLITE_F32;
     if (P == 0) return ARTLITE_OK;
-    const int rt_gu = gemv_row_tile(F), rt_dn = gemv_row_tile(H);
-    AL_TRY(launch_unit_scan(counts, E_run, kGemvTokens, F / rt_gu, h->unit_gu.as<int32_t>(), st));
-    AL_TRY(launch_unit_scan(counts, E_run, kGemvTokens, H / rt_dn, h->unit_dn.as<int32_t>(), st));
+    const int rt_gu = gemv_row_tile(L.qtype, H, F, true), rt_dn = gemv_row_tile(L.down_qtype, F, H, false);
+    AL_CHECK(rt_gu > 0 && rt_dn > 0, ARTLITE_EUNSUPPORTED, "expert gemv: no row tile for F %d / H %d", F, H);
+    if (!units_ready) {
+      AL_TRY(launch_unit_scan(counts, E_run, kGemvTokens, (int)cdiv(F, rt_gu), h->unit_gu.as<int32_t>(), st));
+      AL_TRY(launch_unit_scan(counts, E_run, kGemvTokens, (int)cdiv(H, rt_dn), h->unit_dn.as<int32_t>(), st));
+    }
     ExpertGemvArgs g{};
     g.qtype = L.qtype;
     g.w0 = L.gate.as<uint8_t>();
@@ -303,6 +333,13 @@ int artlite_moe_set_weights(artlite_moe* h, int layer, int qtype, const void* ga
   AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.gate.ptr) + gu_bytes, 0, 64, h->st));
   AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.up.ptr) + gu_bytes, 0, 64, h->st));
   AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.down.ptr) + dn_bytes, 0, 64, h->st));
+  L.has_dm = false;
+  if (qtype == ARTLITE_Q4_K && down_qtype == ARTLITE_Q4_K && F % 64 == 0 && H % 128 == 0) {
+    AL_TRY(make_raw_map(&L.dm_gate, L.gate.ptr, L.rb_gu, h->E_local * F, 144, 64));
+    AL_TRY(make_raw_map(&L.dm_up, L.up.ptr, L.rb_gu, h->E_local * F, 144, 64));
+    AL_TRY(make_raw_map(&L.dm_down, L.down.ptr, L.rb_dn, h->E_local * H, 144, 128));
+    L.has_dm = true;
+  }
   L.n_planes = 0;
   if (router_tc_supported(d.n_experts, d.hidden, d.act_dtype)) {
     L.n_planes = router_qtype == ARTLITE_F32 ? 3 : 1;
@@ -341,15 +378,21 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
   if (h->E_local < E) {
     AL_TRY(ep_forward(h, layer, xd, yd, T, st, mk));
   } else {
-    AL_TRY(route_and_dispatch(h, L, xd, T, st, mk));
     const int path = expert_path(*h, P, L);
     h->last_path = path;
     h->paths[layer] = path;
-    void* yrows;
-    int ydt;
-    AL_TRY(run_experts(h, L, path, xd, d.act_dtype, false, h->perm.as<int32_t>(), K, P, E, h->offsets.as<int64_t>(),
-                       h->counts.as<int32_t>(), 0, &yrows, &ydt, st, mk));
-    AL_TRY(launch_combine(yrows, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st));
+    if (path == 1 && decode_fused_ok(*h, L, T)) {
+      AL_TRY(launch_decode(h, L, xd, yd, T, st));
+    } else {
+      int mult_gu, mult_dn;
+      small_plan(*h, L, path, T, &mult_gu, &mult_dn);
+      AL_TRY(route_and_dispatch(h, L, xd, T, st, mk, mult_gu, mult_dn));
+      void* yrows;
+      int ydt;
+      AL_TRY(run_experts(h, L, path, xd, d.act_dtype, false, h->perm.as<int32_t>(), K, P, E, h->offsets.as<int64_t>(),
+                         h->counts.as<int32_t>(), 0, &yrows, &ydt, st, mk, mult_gu > 0));
+      AL_TRY(launch_combine(yrows, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st));
+    }
   }
   AL_TRY(mk.mark());
   h->n_stages[layer] = mk.ns;
@@ -360,6 +403,7 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
     AL_CUDA(cudaMemcpy(&s, h->status.ptr, sizeof s, cudaMemcpyDeviceToHost));
     if (s.code) {
       AL_CUDA(cudaMemset(h->status.ptr, 0, sizeof s));
+      if (h->bar.ptr) AL_CUDA(cudaMemset(h->bar.ptr, 0, h->bar.bytes));  // (a wait that ran out may leave it mid-way)
       return status_error(s, E);
     }
   }
@@ -382,6 +426,54 @@ int artlite_moe_set_router_bias(artlite_moe* h, int layer, const float* bias) {
   return wait(h->st, 0);
 }
 
+int artlite_moe_forward_graph(artlite_moe* h, int layer, const void* x, void* y, int64_t T, void* stream) {
+  AL_CHECK(h, ARTLITE_EINVAL, "moe_forward_graph: null handle");
+  AL_CHECK(h->E_local == h->d.n_experts, ARTLITE_EUNSUPPORTED,
+           "moe_forward_graph: not with expert parallelism (its exchange sizes are host values of each forward)");
+  AL_CHECK(T > 0 && is_device_ptr(x) && is_device_ptr(y) && ((uintptr_t)x % 16) == 0 && ((uintptr_t)y % 16) == 0,
+           ARTLITE_EINVAL, "moe_forward_graph: T > 0 and 16-byte aligned device x / y");
+  AL_CUDA(cudaSetDevice(h->dev));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->st;
+  for (const artlite_moe::Graph& g : h->graphs)
+    if (g.layer == layer && g.T == T && g.x == x && g.y == y) {
+      AL_CUDA(cudaGraphLaunch(g.exec, st));
+      h->last_T = T;
+      return ARTLITE_OK;
+    }
+  // capture one forward on a side stream (the tensor maps and workspaces it names stay valid: the handle owns them)
+  cudaStream_t cap;
+  AL_CUDA(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+  const bool timing = h->timing;
+  h->timing = false;  // (no per-stage events inside a graph)
+  cudaGraph_t graph = nullptr;
+  int rc = ARTLITE_OK;
+  if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    rc = ARTLITE_ECUDA;
+    set_error("moe_forward_graph: begin capture failed");
+  } else {
+    rc = artlite_moe_forward(h, layer, x, y, T, cap);
+    const cudaError_t e = cudaStreamEndCapture(cap, &graph);
+    if (rc == ARTLITE_OK && e != cudaSuccess) {
+      rc = ARTLITE_ECUDA;
+      set_error("moe_forward_graph: capture failed: %s", cudaGetErrorString(e));
+    }
+  }
+  h->timing = timing;
+  cudaStreamDestroy(cap);
+  if (rc != ARTLITE_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return rc;
+  }
+  cudaGraphExec_t exec;
+  const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  AL_CHECK(ie == cudaSuccess, ARTLITE_ECUDA, "moe_forward_graph: instantiate: %s", cudaGetErrorString(ie));
+  h->graphs.push_back({layer, T, x, y, exec});
+  AL_CUDA(cudaGraphLaunch(exec, st));
+  return ARTLITE_OK;
+}
+
 int artlite_moe_sync(artlite_moe* h, int timeout_ms) {
   AL_CHECK(h, ARTLITE_EINVAL, "moe_sync: null handle");
   AL_CUDA(cudaSetDevice(h->dev));
@@ -390,6 +482,7 @@ int artlite_moe_sync(artlite_moe* h, int timeout_ms) {
   AL_CUDA(cudaMemcpy(&s, h->status.ptr, sizeof s, cudaMemcpyDeviceToHost));
   if (s.code) {
     AL_CUDA(cudaMemset(h->status.ptr, 0, sizeof s));
+    if (h->bar.ptr) AL_CUDA(cudaMemset(h->bar.ptr, 0, h->bar.bytes));  // (a wait that ran out may leave it mid-way)
     return status_error(s, h->d.n_experts);
   }
   return ARTLITE_OK;
@@ -436,6 +529,7 @@ int artlite_moe_destroy(artlite_moe* h) {
   for (cudaEvent_t e : h->ev)
     if (e) cudaEventDestroy(e);
   ep_destroy(h);
+  for (artlite_moe::Graph& g : h->graphs) cudaGraphExecDestroy(g.exec);
   cudaStreamDestroy(h->st);
   delete h;
   return ARTLITE_OK;

@@ -1,6 +1,7 @@
 // The MoE block handle's state, shared by block.cu (single GPU) and ep.cu (expert parallelism over NCCL).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -19,17 +20,31 @@ struct artlite_moe {
     int n_planes = 0;  // the router's bf16 planes (router_split): 3 for an F32 router, 1 for BF16
     int qtype = -1, down_qtype = -1, router_qtype = -1;
     int64_t rb_gu = 0, rb_dn = 0;
+    // Q4_K: tensor maps of the raw rows for the fused decode kernel (gate / up: boxes of 64 rows, down: 128 rows,
+    // one 144-byte super-block wide)
+    bool has_dm = false;
+    CUtensorMap dm_gate, dm_up, dm_down;
   };
   std::vector<Layer> layers;
   // workspaces
   artlite::DevBuf xin, yout, logits, ids, w, offsets, perm, slot, counts, blk, unit_gu, unit_dn, status;
   artlite::DevBuf h, y, xp, tiles;
+  artlite::DevBuf bar;  // the fused decode kernel's grid barrier (zeroed once; left zeroed by every complete run)
   int64_t last_T = 0;
   int last_path = 0;
   bool timing = false;
   std::vector<cudaEvent_t> ev;  // [n_layers][kStages]: the last forward of each layer, read without a sync
   std::vector<int> n_stages;    // per layer
   std::vector<int> paths;       // per layer: the expert path of its last forward
+  // CUDA graphs of whole forwards (artlite_moe_forward_graph), keyed by (layer, T, x, y, stream)
+  struct Graph {
+    int layer;
+    int64_t T;
+    const void* x;
+    void* y;
+    cudaGraphExec_t exec;
+  };
+  std::vector<Graph> graphs;
   // expert parallelism (ep.cu): the NCCL communicator, exchange buffers, pinned host copies of the counts
   void* comm = nullptr;                // ncclComm_t
   artlite::DevBuf ep_rcounts, ep_loff, ep_lcounts, ep_ident, ep_seg, xl, xr, yr, ys;
@@ -67,8 +82,10 @@ struct Marker {
 
 // router logits, routing and the dispatch over all E experts of T tokens x (device, act dtype) into the handle's
 // logits / ids / w / offsets / perm / slot / counts
+// mult_gu > 0: the decode-sized path (the small router when it applies, routing and dispatch in one kernel, which also
+// writes the GEMVs' unit scans: mult_gu / mult_dn items per expert and token group)
 int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* x, int64_t T, cudaStream_t st,
-                       Marker& mk);
+                       Marker& mk, int mult_gu = 0, int mult_dn = 0);
 
 // The experts of a forward over P rows for E_run experts (offsets / counts on the device): rows are the tokens x
 // through perm / k (gathered = false), or already gathered bf16 rows in expert order (gathered = true, perm = the
@@ -76,7 +93,7 @@ int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* 
 // (tcgen05 path) in *y_dtype.
 int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const void* x, int x_dtype, bool gathered,
                 const int32_t* perm, int k, int64_t P, int E_run, const int64_t* offsets, const int32_t* counts,
-                int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk);
+                int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk, bool units_ready = false);
 
 // which expert path a forward of P pairs takes
 int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L);
@@ -90,5 +107,9 @@ int launch_segment_copy(const void* src, void* dst, const int64_t* s, const int6
 int ep_create(artlite_moe* h);
 int ep_forward(artlite_moe* h, int layer, const void* x, void* y, int64_t T, cudaStream_t st, Marker& mk);
 void ep_destroy(artlite_moe* h);
+
+// the fused decode-batch forward (decode.cu): whether it applies, and the launch (x, y device, act dtype)
+bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t T);
+int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, void* y, int64_t T, cudaStream_t st);
 
 }  // namespace artlite

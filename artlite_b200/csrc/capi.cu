@@ -13,6 +13,8 @@
 #include <string>
 #include <vector>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -34,6 +36,14 @@ std::string& last_error() { return g_error; }
 static std::atomic<int64_t> g_launches{0};
 int64_t launch_count() { return g_launches.load(); }
 void count_launch(int n) { g_launches += n; }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("ARTLITE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 bool is_device_ptr(const void* p) {
   if (!p) return false;

@@ -47,6 +47,8 @@ __device__ __forceinline__ void store8(void* base, int dtype, int64_t i, const f
 // one CTA per token row, 8 values per thread (H % 8 == 0)
 __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype, const int32_t* slot, const float* w,
                                                       int64_t T, int k, int H, void* out, int out_dtype) {
+  griddep_wait();
+  griddep_launch();
   const int64_t t = blockIdx.x;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -65,9 +67,7 @@ int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float*
                    int out_dtype, cudaStream_t st) {
   AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "combine: H %d (a multiple of 8)", H);
   if (T == 0) return ARTLITE_OK;
-  combine_kernel<<<(unsigned)T, 256, 0, st>>>(y, y_dtype, slot, w, T, k, H, out, out_dtype);
-  AL_LAUNCHED();
-  return ARTLITE_OK;
+  return launch_pdl(combine_kernel, dim3((unsigned)T), dim3(256), 0, st, y, y_dtype, slot, w, T, k, H, out, out_dtype);
 }
 
 __global__ void __launch_bounds__(256) gather_kernel(const void* x, int x_dtype, const int32_t* perm, int64_t P, int k,

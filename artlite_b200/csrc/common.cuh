@@ -86,6 +86,60 @@ int64_t launch_count();
 void count_launch(int n = 1);
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Programmatic dependent launch: a kernel launched by launch_pdl may begin while the kernel before it on the stream is
+// still running, and must call griddep_wait() before it reads anything an earlier kernel wrote (the wait returns once
+// the earlier grids have completed and their memory is visible; without a programmatic predecessor it returns at
+// once). griddep_launch() lets the next such kernel begin launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();  // ARTLITE_PDL=0 turns programmatic launches into ordinary ones
+
+template <class... KArgs, class... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  AL_CUDA(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+  count_launch();
+  return ARTLITE_OK;
+}
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+// exclusive scan of one value per thread over a block of up to 1024 threads; returns the block total in *total
+template <class T>
+__device__ T block_exclusive_scan(T v, T* smem, T* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  T incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T n = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) smem[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    T s = lane < nw ? smem[lane] : T(0);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T n = __shfl_up_sync(0xFFFFFFFFu, s, o);
+      if (lane >= o) s += n;
+    }
+    if (lane < nw) smem[lane] = s;  // inclusive per warp
+  }
+  __syncthreads();
+  const T base = warp ? smem[warp - 1] : T(0);
+  *total = smem[nw - 1];
+  __syncthreads();
+  return base + incl - v;
+}
 
 }  // namespace artlite

@@ -10,6 +10,7 @@
 // Then the reference plan's chunk deal (moe_host.cpp:256-274) for the drop-in artlite_moe_plan.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "route.cuh"
 
 namespace artlite {
 
@@ -34,34 +35,6 @@ __global__ void __launch_bounds__(512) dispatch_count(DispatchArgs a) {
   }
   __syncthreads();
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) a.blk_counts[(int64_t)blockIdx.x * a.E + e] = hist[e];
-}
-
-// exclusive scan of one value per thread over a block of up to 1024 threads; returns the block total in *total
-template <class T>
-__device__ T block_exclusive_scan(T v, T* smem, T* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-  T incl = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const T n = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-    if (lane >= o) incl += n;
-  }
-  if (lane == 31) smem[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    T s = lane < nw ? smem[lane] : T(0);
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const T n = __shfl_up_sync(0xFFFFFFFFu, s, o);
-      if (lane >= o) s += n;
-    }
-    if (lane < nw) smem[lane] = s;  // inclusive per warp
-  }
-  __syncthreads();
-  const T base = warp ? smem[warp - 1] : T(0);
-  *total = smem[nw - 1];
-  __syncthreads();
-  return base + incl - v;
 }
 
 __global__ void __launch_bounds__(1024) dispatch_scan(DispatchArgs a, int nblk) {
@@ -152,6 +125,102 @@ int launch_dispatch(const DispatchArgs& a, cudaStream_t st) {
     AL_LAUNCHED();
   }
   return ARTLITE_OK;
+}
+
+
+// ---------------------------------------------------------------- decode-sized batches: routing and dispatch in one CTA
+//
+// For n k <= kSmallPairs pairs (and E <= kSmallExperts): one CTA of 1024 threads routes every token (a warp per row,
+// route.cuh), then histograms, scans and ranks the pairs exactly as the three dispatch kernels do for a single block
+// (the same stable order), and writes both expert GEMVs' unit scans. One launch instead of six.
+template <int J>
+__global__ void __launch_bounds__(1024) route_dispatch_small(RouteArgs r, DispatchArgs a, int mult2, int32_t* unit_off2) {
+  extern __shared__ int32_t sm[];
+  __shared__ int64_t s64[32];
+  __shared__ int32_t s32[32];
+  int32_t* wc = sm;                 // [32][E] per-warp counts of the current round
+  int32_t* run = sm + 32 * a.E;     // [E] placed so far
+  int32_t* cnt = run + a.E;         // [E] histogram
+  int64_t* off = reinterpret_cast<int64_t*>(cnt + a.E + (a.E & 1));  // [E] offsets
+  griddep_wait();
+  griddep_launch();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int64_t t = warp; t < r.n; t += 32) route_row<J>(r, t, lane);
+  for (int i = threadIdx.x; i < 34 * a.E; i += blockDim.x) sm[i] = 0;
+  __syncthreads();  // (the rows' ids are visible to the block)
+  for (int64_t p = threadIdx.x; p < a.P; p += blockDim.x) {
+    const int32_t x = a.ids[p];
+    if (x < 0 || x >= a.E)
+      report(a.status, ARTLITE_EDEVICE, x, a.E, 1);
+    else
+      atomicAdd(&cnt[x], 1);
+  }
+  __syncthreads();
+  const int e = threadIdx.x;
+  const int32_t c = e < a.E ? cnt[e] : 0;
+  int64_t tot64;
+  const int64_t o = block_exclusive_scan<int64_t>(c, s64, &tot64);
+  if (e < a.E) {
+    off[e] = o;
+    a.offsets[e] = o;
+    a.counts[e] = c;
+  }
+  if (e == 0) a.offsets[a.E] = tot64;
+  for (int which = 0; which < 2; which++) {
+    const int mult = which ? mult2 : a.unit_mult;
+    int32_t* uo = which ? unit_off2 : a.unit_off;
+    if (!uo) continue;
+    const int32_t u = e < a.E ? (c + a.unit_rows - 1) / a.unit_rows * mult : 0;
+    int32_t tot;
+    const int32_t v = block_exclusive_scan<int32_t>(u, s32, &tot);
+    if (e < a.E) uo[e] = v;
+    if (e == 0) uo[a.E] = tot;
+  }
+  __syncthreads();
+  const unsigned lt = (1u << lane) - 1u;
+  for (int64_t r0 = 0; r0 < a.P; r0 += 1024) {
+    const int64_t p = r0 + threadIdx.x;
+    int32_t x = p < a.P ? a.ids[p] : -1;
+    const bool valid = x >= 0 && x < a.E;
+    if (!valid) x = -1 - lane;
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, x);
+    const int rank = __popc(peers & lt);
+    const bool leader = rank == 0;
+    if (valid && leader) wc[warp * a.E + x] = __popc(peers);
+    __syncthreads();
+    if (valid) {
+      int32_t pre = run[x];
+      for (int w = 0; w < warp; w++) pre += wc[w * a.E + x];
+      const int64_t dest = off[x] + pre + rank;
+      a.perm[dest] = (int32_t)p;
+      a.slot[p] = (int32_t)dest;
+    }
+    __syncthreads();
+    if (valid && leader) {
+      atomicAdd(&run[x], __popc(peers));
+      wc[warp * a.E + x] = 0;
+    }
+    __syncthreads();
+  }
+}
+
+bool small_dispatch_ok(int64_t P, int E) { return P <= kSmallPairs && E <= kSmallExperts; }
+
+int launch_route_dispatch_small(const RouteArgs& r, const DispatchArgs& a, int mult2, int32_t* unit_off2,
+                                cudaStream_t st) {
+  AL_CHECK(small_dispatch_ok(a.P, a.E) && a.P == r.n * r.k, ARTLITE_EINVAL, "route_dispatch_small: P %lld E %d",
+           (long long)a.P, a.E);
+  const size_t smem = sizeof(int32_t) * (34 * (size_t)a.E + 1) + sizeof(int64_t) * a.E;
+  const int J = (r.E + 31) / 32;
+  auto go = [&](auto kern) -> int {
+    AL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    return launch_pdl(kern, dim3(1), dim3(1024), smem, st, r, a, mult2, unit_off2);
+  };
+  if (J <= 1) return go(route_dispatch_small<1>);
+  if (J <= 2) return go(route_dispatch_small<2>);
+  if (J <= 4) return go(route_dispatch_small<4>);
+  if (J <= 8) return go(route_dispatch_small<8>);
+  return go(route_dispatch_small<16>);
 }
 
 // ---------------------------------------------------------------- the reference plan's chunk deal

@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "kernels.cuh"
 #include "quant.cuh"
+#include "rq.cuh"
 
 namespace artlite {
 
@@ -177,11 +178,48 @@ __global__ void __launch_bounds__(kWarps * 32) expert_gemv(ExpertGemvArgs a, con
   }
 }
 
+
+template <int QT, bool GU>
+__global__ void __launch_bounds__(rq::kWarps * 32, 2) expert_gemv_rq(ExpertGemvArgs a, int R) {
+  extern __shared__ __align__(16) float sm[];
+  float* xs = sm;
+  int32_t* uo = reinterpret_cast<int32_t*>(sm + rq::stage_floats(a.K));  // [E + 1]
+  griddep_wait();
+  griddep_launch();
+  for (int i = threadIdx.x; i <= a.E; i += blockDim.x) uo[i] = a.unit_off[i];
+  __syncthreads();
+  const int total = uo[a.E];
+  const int i0 = (int)((int64_t)blockIdx.x * total / gridDim.x), i1 = (int)((int64_t)(blockIdx.x + 1) * total / gridDim.x);
+  rq::run_items<QT, GU>(a, R, uo, a.offsets, a.perm, xs, i0, i1);
+}
+
+// rows per warp of the register-decoding kernel (0: the type or shape goes to the staged kernel)
+int gemv_rq_rows_per_warp(int qtype, int K, bool gu) {
+  if (!(qtype == ARTLITE_Q4_0 || qtype == ARTLITE_Q8_0 || qtype == ARTLITE_Q4_K) || K % 256 || K <= 0) return 0;
+  return 32 / (K / 256) / (gu ? 2 : 1);
+}
+
 namespace {
 
 template <bool GU>
 int launch_gemv(const ExpertGemvArgs& a, const int32_t* unit_off, int rt, cudaStream_t st) {
-  constexpr int NT = 8;
+  constexpr int NT = kGemvTokens;
+  const int R = gemv_rq_rows_per_warp(a.qtype, a.K, GU);
+  if (R > 0 && rt == R * rq::kWarps) {
+    const size_t smem = sizeof(float) * rq::stage_floats(a.K) + sizeof(int32_t) * (a.E + 1);
+    int dev, sms;
+    AL_CUDA(cudaGetDevice(&dev));
+    AL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    auto go = [&](auto kern) -> int {
+      AL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      int per_sm = 0;
+      AL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, rq::kWarps * 32, smem));
+      return launch_pdl(kern, dim3(std::max(1, per_sm) * sms), dim3(rq::kWarps * 32), smem, st, a, R);
+    };
+    if (a.qtype == ARTLITE_Q4_0) return go(expert_gemv_rq<ARTLITE_Q4_0, GU>);
+    if (a.qtype == ARTLITE_Q8_0) return go(expert_gemv_rq<ARTLITE_Q8_0, GU>);
+    return go(expert_gemv_rq<ARTLITE_Q4_K, GU>);
+  }
   int per, bytes;
   AL_TRY(qtype_block(a.qtype, &per, &bytes));
   AL_CHECK(a.K % 32 == 0 && a.K % per == 0 && a.N % rt == 0, ARTLITE_EUNSUPPORTED, "expert gemv: K %d N %d RT %d",
@@ -217,7 +255,9 @@ int launch_gemv(const ExpertGemvArgs& a, const int32_t* unit_off, int rt, cudaSt
 
 }  // namespace
 
-int gemv_row_tile(int N) {
+int gemv_row_tile(int qtype, int K, int N, bool gu) {
+  const int R = gemv_rq_rows_per_warp(qtype, K, gu);
+  if (R > 0) return R * rq::kWarps;
   for (int rt : {16, 8})
     if (N % rt == 0) return rt;
   return 0;

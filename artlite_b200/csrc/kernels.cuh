@@ -45,6 +45,12 @@ struct DispatchArgs {
 constexpr int kDispatchBlockPairs = 4096;
 size_t dispatch_scratch_bytes(int64_t P, int E);
 int launch_dispatch(const DispatchArgs& a, cudaStream_t st);
+// decode-sized batches: the routing (r) and the dispatch (a, its unit scan and a second one: mult2 / unit_off2) in one
+// CTA; r.ids is a.ids
+constexpr int kSmallPairs = 4096, kSmallExperts = 512;
+bool small_dispatch_ok(int64_t P, int E);
+int launch_route_dispatch_small(const RouteArgs& r, const DispatchArgs& a, int mult2, int32_t* unit_off2,
+                                cudaStream_t st);
 
 // The reference plan's chunk deal (moe_host.cpp:256-274) from a dispatch: experts / counts / sizes / rows / pos.
 struct ChunkPlanArgs {
@@ -72,6 +78,11 @@ int launch_dequant_rows(int qtype, const uint8_t* raw, int64_t n, int64_t row_by
 // logits (T x E fp32) = x (T x H, f32 or bf16) . W_r^T (E x H, f32 or bf16) (+ bias (E), if not null)
 int launch_router(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H, int E,
                   float* logits, cudaStream_t st);
+// the same for decode-sized batches (T <= kRouterSmallTokens, H % 4 == 0), spread over (E / 2) x (T / 16) CTAs
+constexpr int kRouterSmallTokens = 256;
+bool router_small_ok(int64_t T, int H);
+int launch_router_small(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H,
+                        int E, float* logits, cudaStream_t st);
 
 // ---------------------------------------------------------------- gemv.cu (CUDA-core dequant path)
 struct ExpertGemvArgs {
@@ -86,13 +97,15 @@ struct ExpertGemvArgs {
   int x_dtype;
   const int32_t* perm;     // dispatch order -> pair (gu: token = pair / k)
   const int64_t* offsets;  // [E + 1]
-  const int32_t* unit_off; // [E + 1] items per expert, ceil(n_e / 8) * (N / rt), scanned (launch_unit_scan)
+  const int32_t* unit_off; // [E + 1] items per expert, ceil(n_e / 8) * ceil(N / rt), scanned (launch_unit_scan)
   int rt;                  // weight rows per item (gemv_row_tile(N))
   int k;
   float* out;        // gu: h (P x F fp32, dispatch order); down: y (P x H fp32, dispatch order)
 };
 constexpr int kGemvTokens = 8;  // pairs per item
-int gemv_row_tile(int N);
+// weight rows per item (the register-decoding kernel's, else 16 or 8 dividing N; 0: none); items per expert and token
+// group: ceil(N / rows)
+int gemv_row_tile(int qtype, int K, int N, bool gu);
 int launch_gemv_gu(const ExpertGemvArgs& a, cudaStream_t st);
 int launch_gemv_down(const ExpertGemvArgs& a, cudaStream_t st);
 

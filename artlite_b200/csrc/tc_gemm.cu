@@ -825,6 +825,9 @@ int make_map(CUtensorMap* m, const void* base, int64_t row_elems, int64_t rows, 
 
 }  // namespace
 
+int make_raw_map(CUtensorMap* m, const void* base, int64_t row_bytes, int64_t rows, int box_bytes, int box_rows) {
+  return make_map(m, base, row_bytes / 2, rows, box_bytes / 2, box_rows, false);
+}
 
 bool router_tc_supported(int E, int H, int x_dtype) {
   return x_dtype == ARTLITE_BF16 && E % rt::BM == 0 && H % rt::BK == 0;

@@ -27,6 +27,9 @@ struct TcGemmArgs {
   DevStatus* status;
 };
 
+// a 2D tensor map over raw rows (rows x row_bytes, 16-byte multiples), box box_rows x box_bytes, no swizzle
+int make_raw_map(CUtensorMap* m, const void* base, int64_t row_bytes, int64_t rows, int box_bytes, int box_rows);
+
 // whether the tcgen05 path reads this type at these shapes (K, N multiples of 256 / 128)
 bool tc_supported(int qtype, int K, int N);
 size_t tc_sched_bytes(int E);

@@ -103,6 +103,10 @@ class MoEBlock:
         """The forward on device (or pinned host) buffers given by address; enqueued on ``stream`` (0: the block's)."""
         check(lib().artlite_moe_forward(self._h, layer, _ptr(x), _ptr(y), T, ctypes.c_void_p(stream or None)))
 
+    def forward_graph(self, x, y, T: int, layer: int = 0, stream: int = 0) -> None:
+        """``forward_ptr`` as a CUDA graph, captured on the first call per (layer, T, x, y) and replayed after."""
+        check(lib().artlite_moe_forward_graph(self._h, layer, _ptr(x), _ptr(y), T, ctypes.c_void_p(stream or None)))
+
     def sync(self, timeout_ms: int = 0) -> None:
         check(lib().artlite_moe_sync(self._h, timeout_ms))
 

@@ -170,6 +170,74 @@ def gen_layer(torch, g, dev):
     return q4_0(E * F, H), q4_0(E * F, H), q4_0(E * H, F), router
 
 
+def gen_layer_q4k(torch, g, dev):
+    """One layer's raw Q4_K tensors on the GPU (144-byte super-blocks: d, dmin fp16 |N(0, 0.02)|, twelve bytes of
+    uniform 6-bit scales / mins, 128 bytes of uniform nibbles) and the router (E, H) fp32."""
+    def q4k(rows, cols):
+        n = cols // 256
+        raw = torch.randint(0, 256, (rows, n, 144), dtype=torch.uint8, generator=g, device=dev)
+        for o in (0, 2):
+            d = (torch.randn((rows, n), generator=g, device=dev) * 0.02).abs().half()
+            raw[..., o:o + 2] = d.view(torch.uint8).view(rows, n, 2)
+        return raw.view(rows, n * 144)
+
+    router = torch.randn((E, H), generator=g, device=dev) * 0.02
+    return q4k(E * F, H), q4k(E * F, H), q4k(E * H, F), router
+
+
+def run_decode(args) -> None:
+    """BASELINE config 2 on one GPU: decode batches B = 1, 4, 16, 64 of the Q4_K block (bf16 x), each forward a CUDA
+    graph, over --layers layers in turn (their touched experts far exceed L2). One JSON line per B: tokens/s, and the
+    HBM roofline of the bytes a forward must read (U touched experts x 2,654,208 B + the fp32 router 1,048,576 B)."""
+    import torch
+    from artlite_b200.moe.block import MoEBlock
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = args.layers
+    block = MoEBlock(hidden=H, n_experts=E, top_k=K, expert_ffn=F, max_tokens=64, n_layers=L, act_dtype="bf16",
+                     device=0, path=args.path)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3000)
+    for layer in range(L):
+        gate, up, down, router = gen_layer_q4k(torch, g, dev)
+        block.set_weights(layer, gate=gate.data_ptr(), up=up.data_ptr(), down=down.data_ptr(),
+                          router=router.data_ptr(), qtype="Q4_K")
+        del gate, up, down, router
+    torch.cuda.empty_cache()
+    peaks, src = measured_peaks()
+    stream = torch.cuda.Stream(device=dev)
+    for B in args.batches:
+        x = torch.randn((B, H), generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+        touched = []
+        for layer in range(L):  # (the routing of each layer: its touched experts)
+            block.forward_ptr(x.data_ptr(), y.data_ptr(), B, layer=layer, stream=stream.cuda_stream)
+            block.sync()
+            touched.append(len(np.unique(block.debug(B)["ids"])))
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                for layer in range(L):
+                    block.forward_graph(x.data_ptr(), y.data_ptr(), B, layer=layer, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            for layer in range(L):
+                block.forward_graph(x.data_ptr(), y.data_ptr(), B, layer=layer, stream=stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_layer = e0.elapsed_time(e1) / (args.steps * L)
+        U = float(np.mean(touched))
+        nbytes = U * 2654208 + E * H * 4
+        gbs = nbytes / (ms_layer / 1000.0) / 1e9
+        print(json.dumps({"workload": f"decode-q4_k-b{B}", "batch": B, "us_per_layer": ms_layer * 1000.0,
+                          "tokens_per_s": B / (ms_layer / 1000.0), "experts_touched": U,
+                          "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                       "frac": gbs / peaks["hbm_gbs"], "peak_source": src, "bytes_per_layer": nbytes},
+                          "path": block.path(0), "layers": L, "steps": args.steps}), flush=True)
+    block.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -181,9 +249,15 @@ def main() -> None:
     ap.add_argument("--cpu-tokens", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--decode", action="store_true", help="BASELINE config 2 (decode batches, Q4_K) instead")
+    ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"], help="expert path of --decode")
+    ap.add_argument("--batches", type=int, nargs="+", default=[1, 4, 16, 64], help="decode batches of --decode")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.decode:
+        run_decode(args)
         return
 
     os.environ["ARTLITE_MOE_TIMING"] = "1"  # per-stage CUDA events between the forward's kernels (no syncs)

@@ -153,6 +153,13 @@ int artlite_moe_set_router_bias(artlite_moe* h, int layer, const float* bias);
  */
 int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64_t T, void* stream);
 
+/*
+ * The same forward as a CUDA graph (device x / y only, no expert parallelism): the first call with a given
+ * (layer, T, x, y) captures one forward and instantiates it, every later call launches the graph on `stream` (NULL:
+ * the handle's). For decode batches, whose kernels are short enough that launch gaps dominate.
+ */
+int artlite_moe_forward_graph(artlite_moe* h, int layer, const void* x, void* y, int64_t T, void* stream);
+
 /* Wait (bounded by timeout_ms; <= 0: 60 s) for the handle's work and report any device-side status. */
 int artlite_moe_sync(artlite_moe* h, int timeout_ms);
 

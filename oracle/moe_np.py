@@ -8,7 +8,9 @@
 - ``rel`` / ``rel_max``: ``tests/numerics.py:24-27,50-53``.
 - Block generators: the synthetic GGUF blocks of the benchmark configurations (fp16 d from |N(0, 0.02)|; Q4_0 nibbles
   uniform 0..15; Q4_K 6-bit scales / mins uniform 0..63 packed as ``gguf_model.py:116-121`` reads them; Q8_0 int8
-  uniform -127..127), drawn from one ``default_rng(seed)`` stream in the order router, x, gate, up, down.
+  uniform -127..127), drawn from one ``default_rng(seed)`` stream in the order router, x, gate, up, down. The other
+  block formats (test cases only): Q4_1 m = -8 d; Q5_K as Q4_K with uniform high bits; Q6_K int8 scales uniform
+  -32..31 with d from |N(0, 0.002)|; all quant bits uniform.
 """
 
 from dataclasses import dataclass
@@ -173,6 +175,19 @@ def random_blocks(rng: np.random.Generator, qtype: str, rows: int, cols: int) ->
         raw[..., 8:12] = (mn[..., :4] & 63) | ((mn[..., 4:] >> 4) << 6)
         raw[..., 12:16] = (sc[..., 4:] & 15) | ((mn[..., 4:] & 15) << 4)
         raw[..., 16:] = rng.integers(0, 256, (rows, n, 128), dtype=np.uint8)
+    elif qtype == "Q4_1":
+        d = _fp16_abs_normal(rng, (rows, n))
+        raw[..., 0:2] = d.view(np.uint8).reshape(rows, n, 2)
+        raw[..., 2:4] = (-8 * d).astype(np.float16).view(np.uint8).reshape(rows, n, 2)
+        raw[..., 4:] = rng.integers(0, 256, (rows, n, 16), dtype=np.uint8)
+    elif qtype == "Q5_K":
+        raw[..., :144] = random_blocks(rng, "Q4_K", rows * n, 256).reshape(rows, n, 144)
+        raw[..., 144:] = rng.integers(0, 256, (rows, n, 32), dtype=np.uint8)
+        raw[..., 16:] = np.concatenate([raw[..., 144:], raw[..., 16:144]], axis=-1)  # d, dmin, scales, qh, qs
+    elif qtype == "Q6_K":
+        raw[..., :192] = rng.integers(0, 256, (rows, n, 192), dtype=np.uint8)
+        raw[..., 192:208] = rng.integers(-32, 32, (rows, n, 16), dtype=np.int8).view(np.uint8)
+        raw[..., 208:] = _fp16_abs_normal(rng, (rows, n), 0.002).view(np.uint8).reshape(rows, n, 2)
     else:
         raise ValueError(qtype)
     return raw.reshape(rows, n * nb)

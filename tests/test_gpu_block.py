@@ -72,6 +72,15 @@ def test_decode_fp32_tight(qtype):
     assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= FP32_TOL
 
 
+@pytest.mark.parametrize("qtype", ["Q4_1", "Q5_K", "Q6_K"])
+def test_decode_generic_formats(qtype):
+    """The formats without a register-decoding GEMV (the generic staged kernel) through the block, fp32 tight."""
+    layer, x, _ = moe_np.make_block(6, 12, qtype=qtype, x_bf16=False, E=16, H=512, F=256)
+    y, dbg = run(layer, x, act="f32", path="gemv", T=12)
+    ids, w = check_routing(dbg, x, layer, 8)
+    assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= FP32_TOL
+
+
 @pytest.mark.parametrize("qtype", ["Q4_0", "Q8_0", "Q4_K"])
 def test_tcgen05_small(qtype):
     """The tcgen05 grouped GEMMs at a small shape: E=16, H=512, F=256, T=200 (ragged expert groups)."""
@@ -155,4 +164,23 @@ def test_zero_tokens_and_errors():
     assert b.forward(x[:0]).shape == (0, 256)
     with pytest.raises(Error, match="max_tokens"):
         b.forward(np.zeros((5, 256), np.uint16))
+    b.close()
+
+
+@pytest.mark.parametrize("path,T", [("gemv", 4), ("tc", 260)])
+def test_forward_graph_matches_forward(path, T):
+    """A forward captured as a CUDA graph (device x / y) gives the eager forward's output bit for bit, on its first
+    (capturing) call and on replays with new input values in the same buffers."""
+    import torch
+    layer, x, _ = moe_np.make_block(40, T, qtype="Q4_K", E=32, H=512, F=256)
+    b = make_block(layer, T, act="bf16", path=path)
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    yd = torch.empty_like(xd)
+    for rep in range(3):
+        if rep:
+            xd.copy_(torch.from_numpy(np.roll(x, rep, axis=0).view(np.int16)))
+        want = b.forward(xd.cpu().numpy().view(np.uint16))
+        b.forward_graph(xd.data_ptr(), yd.data_ptr(), T)
+        b.sync()
+        assert np.array_equal(yd.cpu().numpy().view(np.uint16), want)
     b.close()
