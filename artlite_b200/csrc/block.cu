@@ -82,7 +82,9 @@ int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L) {
   const bool tc = tc_supported(L.qtype, d.hidden, d.expert_ffn) && tc_supported(L.down_qtype, d.expert_ffn, d.hidden);
   if (d.path == 1 || !tc) return 1;
   if (d.path == 2) return 2;
-  // tcgen05 for prefill-sized batches (on average 4 pairs an expert or more), the GEMVs for decode batches
+  // the fused decode kernel where it applies (up to 512 pairs), else tcgen05 for prefill-sized batches (on average 4
+  // pairs an expert or more) and the GEMVs for decode batches
+  if (decode_fused_ok(h, L, P / d.top_k)) return 1;
   return P >= 4 * (int64_t)h.E_local ? 2 : 1;
 }
 

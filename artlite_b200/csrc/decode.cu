@@ -159,9 +159,17 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
   constexpr bool kMs = QG == ARTLITE_Q4_K;  // (then QD == QG)
   ms::Pipe pp{};
   if constexpr (kMs) {
-    pp.bar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sm) + a.stage_bytes - 64);
-    if (threadIdx.x == 0)
-      for (int i = 0; i < ms::kStages; i++) ms::mbar_init(&pp.bar[i], 1);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sm) + a.stage_bytes - 64);
+    pp.full = bars;
+    pp.empty = bars + ms::kStages;
+    pp.failed = reinterpret_cast<int*>(bars + 2 * ms::kStages);
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < ms::kStages; i++) {
+        ms::mbar_init(&pp.full[i], 1);
+        ms::mbar_init(&pp.empty[i], ms::kThreads / 32);
+      }
+      *pp.failed = 0;
+    }
   }
   // ---- 1. router logits (and the tokens' x in fragment order)
   for (int u = blockIdx.x * rq::kWarps + warp; u < a.T * E; u += gridDim.x * rq::kWarps)
@@ -359,7 +367,8 @@ bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t 
     return v && v[0] == '0';
   }();
   const artlite_moe_desc& d = h.d;
-  return !off && T > 0 && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts && h.E_local == d.n_experts &&
+  // (below 8 tokens the separate kernels, whose GEMV spreads finer items over the whole grid, are faster)
+  return !off && T >= 8 && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts && h.E_local == d.n_experts &&
          rq_type(L.qtype) && L.down_qtype == L.qtype && d.hidden % 256 == 0 && d.expert_ffn % 256 == 0 &&
          gemv_rq_rows_per_warp(L.qtype, d.hidden, true) > 0 && gemv_rq_rows_per_warp(L.down_qtype, d.expert_ffn, false) > 0 &&
          (L.qtype != ARTLITE_Q4_K || (d.act_dtype == ARTLITE_BF16 && L.has_dm)) &&

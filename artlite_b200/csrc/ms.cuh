@@ -19,6 +19,7 @@
 // to bf16, as on the tcgen05 path).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -32,7 +33,7 @@ constexpr int kThreads = 256;
 constexpr int kStages = 3;
 constexpr int kRows = 128;                     // raw rows per step (gate 64 + up 64, or 128 down rows)
 constexpr int kStageBytes = kRows * 144;       // 18432 (a multiple of 128: TMA destinations)
-constexpr int kOutBytes = 2 * 64 * 8 * 4;      // gate / up tile outputs of an item (gu)
+constexpr int kOutBytes = 3 * 64 * 8 * 4;      // gate / up tile outputs of an item (gu), and h
 constexpr int kTabBytes = 8 * 16 * 8 * 8;      // per warp: 16 rows x 8 groups x {A, B}
 constexpr long long kWaitCycles = 4000000000LL;  // about 2 s
 
@@ -84,7 +85,7 @@ __device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint
 }
 
 __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -104,11 +105,11 @@ struct Gemv {
   float* y;
 };
 
-struct Pipe {  // the CTA's stages: their mbarriers and the parity each waits for next (bit i: stage i; the same in
-               // every thread)
-  uint64_t* bar;
-  unsigned parity;
-  bool failed;
+struct Pipe {  // the CTA's stages: full (the copies landed: one arrival + bytes) and empty (every warp is done: 8
+               // arrivals) mbarriers, and the parity each thread waits for next (bit i: stage i)
+  uint64_t *full, *empty;
+  unsigned full_parity, empty_parity;
+  int* failed;   // (shared) set once a wait ran out: no more copies are started, no more results written
 };
 
 struct Step {
@@ -178,27 +179,23 @@ __device__ __forceinline__ float f4at(const float4 (&v)[2], int j) {
 
 __device__ __forceinline__ void tile_sb(const uint8_t* rows, const XFrag& x, float* tab, int lane, float (&y)[4]) {
   const int g = lane >> 2, t = lane & 3;
-  // scales of rows (g, g + 8) x groups (2t, 2t + 1) into the warp's table
+  // scales of rows (g, g + 8) x groups (2t, 2t + 1) into the warp's table. The twelve scale bytes q0 .. q11 hold the
+  // six-bit scale / min of group j < 4 in q[j] / q[j + 4] (low six bits) and of j >= 4 in the nibbles of q[j + 4] with
+  // the top two bits of q[j - 4] / q[j]: as packed bytes, sc(0..3) = w1 & 0x3F.., sc(4..7) = (w3 & 0x0F..) |
+  // ((w1 & 0xC0..) >> 2), mn(0..3) = w2 & 0x3F.., mn(4..7) = ((w3 >> 4) & 0x0F..) | ((w2 & 0xC0..) >> 2).
 #pragma unroll
   for (int i = 0; i < 2; i++) {
     const uint4 h = *reinterpret_cast<const uint4*>(rows + (g + 8 * i) * 144);
-    const uint32_t w[4] = {h.x, h.y, h.z, h.w};
-    const float d = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFFu)));
-    const float dmin = __half2float(__ushort_as_half((unsigned short)(w[0] >> 16)));
+    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    const uint32_t sc_w = t < 2 ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y & 0xC0C0C0C0u) >> 2));
+    const uint32_t mn_w = t < 2 ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z & 0xC0C0C0C0u) >> 2));
+    const int sh = 16 * (t & 1);
 #pragma unroll
     for (int jj = 0; jj < 2; jj++) {
-      const int j = 2 * t + jj;
-      auto byte = [&](int b) { return (w[b >> 2] >> ((b & 3) * 8)) & 0xFFu; };
-      int sc, mn;
-      if (j < 4) {
-        sc = byte(4 + j) & 63;
-        mn = byte(8 + j) & 63;
-      } else {
-        sc = (byte(8 + j) & 15) | (byte(j) >> 6) << 4;
-        mn = (byte(8 + j) >> 4) | (byte(4 + j) >> 6) << 4;
-      }
-      const float dsc = __fmul_rn(d, (float)sc), dmn = __fmul_rn(dmin, (float)mn);
-      reinterpret_cast<float2*>(tab)[(g + 8 * i) * 8 + j] = make_float2(dsc, __fmaf_rn(128.0f, dsc, dmn));
+      const float sc = (float)((sc_w >> (sh + 8 * jj)) & 0xFFu), mn = (float)((mn_w >> (sh + 8 * jj)) & 0xFFu);
+      const float dsc = __fmul_rn(d, sc), dmn = __fmul_rn(dmin, mn);
+      reinterpret_cast<float2*>(tab)[(g + 8 * i) * 8 + 2 * t + jj] = make_float2(dsc, __fmaf_rn(128.0f, dsc, dmn));
     }
   }
   __syncwarp();
@@ -230,48 +227,58 @@ __device__ __forceinline__ void tile_sb(const uint8_t* rows, const XFrag& x, flo
 
 // Items [i0, i1) of one GEMV (gu: 64 output rows an item, gate and up; down: 128 rows). Every thread of the CTA calls
 // it; smem (128-byte aligned): the stages, the output tile, the per-warp tables (smem_bytes()). x must be complete in
-// global memory (a grid barrier before).
+// global memory (a grid barrier before). Thread 0 starts the copies: a stage is refilled once its empty barrier shows
+// every warp done with it; the warps otherwise run ahead of one another by up to the stages in flight.
 template <bool GU>
 __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int64_t* offs, const int32_t* perm,
                                    uint8_t* smem, Pipe& pp, int i0, int i1, DevStatus* status) {
   static_assert(kThreads == 256, "8 warps");
-  if ((su32(smem) & 127u) != 0) {  // (TMA destinations: never issued to a misaligned stage)
-    if (threadIdx.x == 0) report(status, ARTLITE_EUNSUPPORTED, 128, 0, 0);
-    pp.failed = true;
-  }
   const int SB = a.K >> 8;
   const int S = (i1 - i0) * SB;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float* out = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [2][64][8]
   float* tab = reinterpret_cast<float*>(smem + kStages * kStageBytes + kOutBytes) + warp * 16 * 8 * 2;
   if (S <= 0) return;
-  // prologue: steps 0 .. kStages - 1 (issued: the steps whose copies were started; after a failure no more are, and
-  // those already started are still waited for, so that none lands after the CTA has moved on)
-  const int pre = pp.failed ? 0 : (S < kStages ? S : kStages);
-  int issued = pre;
-  __syncthreads();  // (the stages are free: nothing of the previous user reads them any more)
-  if (threadIdx.x == 0)
-    for (int s = 0; s < pre; s++) {
-      mbar_expect(&pp.bar[s], kStageBytes);
-      issue<GU>(a, step_of<GU>(a, s, i0, uo, offs), smem + s * kStageBytes, &pp.bar[s]);
+  if ((su32(smem) & 127u) != 0) {  // (TMA destinations: never issued to a misaligned stage)
+    if (threadIdx.x == 0) {
+      report(status, ARTLITE_EUNSUPPORTED, 128, 0, 0);
+      *pp.failed = 1;
+    }
+    __syncthreads();
+    return;
+  }
+  const bool producer = threadIdx.x == 0;
+  // prologue: steps 0 .. kStages - 1 (the stages are free: the previous user waited for every copy it started)
+  int issued = 0;
+  if (producer && !*pp.failed)
+    for (int s = 0; s < kStages && s < S; s++) {
+      mbar_expect(&pp.full[s], kStageBytes);
+      issue<GU>(a, step_of<GU>(a, s, i0, uo, offs), smem + s * kStageBytes, &pp.full[s]);
+      issued = s + 1;
     }
   float y[4] = {0, 0, 0, 0};
   const int tile = GU ? warp >> 1 : warp, mat = GU ? warp & 1 : 0;
+  int waited = 0;  // (producer: steps whose copies are known complete)
   for (int s = 0; s < S; s++) {
     const int b = s % kStages;
     const Step st = step_of<GU>(a, s, i0, uo, offs);
     uint8_t* buf = smem + b * kStageBytes;
     XFrag xf;
     load_x<GU>(a, st, perm, lane, xf);
-    if (s < issued) {
-      if (!mbar_wait(&pp.bar[b], (pp.parity >> b) & 1u, status)) pp.failed = true;
-      pp.parity ^= 1u << b;
+    bool ok = !*(volatile int*)pp.failed;
+    if (ok) {
+      ok = mbar_wait(&pp.full[b], (pp.full_parity >> b) & 1u, status);
+      if (!ok) *(volatile int*)pp.failed = 1;
     }
-    const bool ok = __syncthreads_and(!pp.failed);
-    if (!ok) pp.failed = true;
-    if (!pp.failed) tile_sb(buf + (mat * 64 + tile * 16) * 144, xf, tab, lane, y);
-    if (st.sb == SB - 1) {  // the item's last column: its outputs
+    pp.full_parity ^= 1u << b;
+    ok = __all_sync(0xFFFFFFFFu, ok);
+    if (producer && ok) waited = s + 1;
+    if (ok) tile_sb(buf + (mat * 64 + tile * 16) * 144, xf, tab, lane, y);
+    __syncwarp();
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&pp.empty[b])) : "memory");
+    if (st.sb == SB - 1) {  // the item's last column: its outputs (every warp meets here)
       const int g = lane >> 2, t = lane & 3;
+      const bool good = !*(volatile int*)pp.failed;
       if (GU) {
         float* o = out + mat * 64 * 8;
         o[(tile * 16 + g) * 8 + 2 * t] = y[0];
@@ -279,18 +286,21 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
         o[(tile * 16 + g + 8) * 8 + 2 * t] = y[2];
         o[(tile * 16 + g + 8) * 8 + 2 * t + 1] = y[3];
         __syncthreads();
+        float* hb = out + 2 * 64 * 8;  // [8 tokens][64 rows]: h rounded to bf16
+        for (int v = threadIdx.x; v < 64 * 8; v += kThreads) {
+          const int r = v >> 3, n = v & 7;
+          hb[n * 64 + r] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(silu(out[r * 8 + n]), out[64 * 8 + r * 8 + n])));
+        }
+        __syncthreads();
         if (threadIdx.x < 64) {  // (n, group of 32 rows, t): 8 h values in fragment order, and the group sum
           const int n = threadIdx.x >> 3, grp = (threadIdx.x >> 2) & 1, tq = threadIdx.x & 3;
-          float v[8];
-#pragma unroll
-          for (int j = 0; j < 8; j++) {
-            const int r = grp * 32 + 8 * tq + j;
-            v[j] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(silu(out[r * 8 + n]), out[64 * 8 + r * 8 + n])));
-          }
+          const float4 h0 = *reinterpret_cast<const float4*>(hb + n * 64 + grp * 32 + 8 * tq);
+          const float4 h1 = *reinterpret_cast<const float4*>(hb + n * 64 + grp * 32 + 8 * tq + 4);
+          const float v[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
           float part = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
           part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
           part += __shfl_xor_sync(0xFFFFFFFFu, part, 2);
-          if (n < st.nt && !pp.failed) {
+          if (n < st.nt && good) {
             const int Go = a.N >> 5;
             const int64_t pr = st.d0 + n;
             const int og = st.rt * 2 + grp;
@@ -298,7 +308,8 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
             if (tq == 0) a.hs[pr * Go + og] = part;
           }
         }
-      } else if (!pp.failed) {
+        __syncthreads();  // (out is free again)
+      } else if (good) {
         const int64_t row = (int64_t)st.rt * 128 + tile * 16 + g;
         if (2 * t < st.nt) {
           a.y[(st.d0 + 2 * t) * a.N + row] = y[0];
@@ -311,18 +322,29 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
       }
       y[0] = y[1] = y[2] = y[3] = 0.0f;
     }
-    // refill this stage with step s + kStages
-    const int s2 = s + kStages;
-    const bool more = s2 < S && !pp.failed;  // (uniform: failed is the same in every thread after the vote above)
-    __syncthreads();  // (every warp is done with this stage)
-    if (more) {
-      if (threadIdx.x == 0) {
-        mbar_expect(&pp.bar[b], kStageBytes);
-        issue<GU>(a, step_of<GU>(a, s2, i0, uo, offs), buf, &pp.bar[b]);
+    // the producer refills this stage with step s + kStages once every warp is done with it
+    if (producer) {
+      const int s2 = s + kStages;
+      bool free_ok = true;
+      if (s < issued) {  // (its empty phase for step s completes when all 8 warps arrived)
+        free_ok = !*(volatile int*)pp.failed && mbar_wait(&pp.empty[b], (pp.empty_parity >> b) & 1u, status);
+        pp.empty_parity ^= 1u << b;
+        if (!free_ok) *(volatile int*)pp.failed = 1;
       }
-      issued = s2 + 1;
+      if (s2 < S && free_ok && !*(volatile int*)pp.failed) {
+        mbar_expect(&pp.full[b], kStageBytes);
+        issue<GU>(a, step_of<GU>(a, s2, i0, uo, offs), buf, &pp.full[b]);
+        issued = s2 + 1;
+      }
     }
   }
+  // after a failure: wait (bounded) for the copies already started, so that none lands in a stage after this
+  if (producer)
+    for (int s = waited; s < issued; s++) {
+      const int b = s % kStages;
+      if (!mbar_test(&pp.full[b], (pp.full_parity >> b) & 1u)) mbar_wait(&pp.full[b], (pp.full_parity >> b) & 1u, status);
+    }
+  __syncthreads();
 }
 
 }  // namespace ms
