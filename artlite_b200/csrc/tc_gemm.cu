@@ -313,9 +313,12 @@ struct RawSpan {
 // the kernel's shared-memory pipeline depth: A + B stages and raw weight stages, per format and mode
 __host__ __device__ constexpr int b_stage_bytes(bool pair) { return pair ? B_BYTES / 2 : B_BYTES; }
 __host__ __device__ constexpr int ab_stages(int qt, bool pair) { return pair ? (qt == ARTLITE_Q8_0 ? 4 : 5) : 3; }
+// the epilogue's transpose buffers: per epilogue warp 32 token rows of up to 32 bf16 values, rows 80 bytes apart
+// (16-byte row reads of 8 consecutive lanes fall in distinct banks)
+constexpr int kEpiRow = 80, kEpiWarp = 32 * kEpiRow;
 __host__ __device__ constexpr size_t smem_bytes(int qt, bool pair) {
   return 1024 + (size_t)ab_stages(qt, pair) * (A_BYTES + b_stage_bytes(pair)) +
-         (size_t)raw_stages(qt) * BM * chunk_bytes(qt) + 512;
+         (size_t)raw_stages(qt) * BM * chunk_bytes(qt) + 4 * kEpiWarp + 512;
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -398,7 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
   uint8_t* sA = base;
   uint8_t* sB = sA + SS * A_BYTES;
   uint8_t* sR = sB + SS * BB;
-  Smem* sm = reinterpret_cast<Smem*>(sR + R * BM * CB);
+  uint8_t* sE = sR + R * BM * CB;  // the epilogue warps' transpose buffers
+  Smem* sm = reinterpret_cast<Smem*>(sE + 4 * kEpiWarp);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = p.toff[p.E];
   const uint32_t crank = PAIR ? cluster_rank() : 0;  // 0: the leader
@@ -586,29 +590,44 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
       // 32 columns at a time, the next chunk's TMEM load in flight while this chunk is stored
       const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + acc * BNMAX;
       const int nch = (T.n_mma + 31) / 32;
+      // a 32-token chunk: values into this warp's buffer as [token][column] bf16, then each lane stores its token's
+      // columns with 16-byte stores (gu: 16 features, 32 B; down: 32 rows, 64 B of the output row)
+      uint8_t* eb = sE + q * kEpiWarp;
       auto emit = [&](const uint32_t(&v)[32], int c0) {
         if (GU) {
           const bool gate = lane < 16;
-          const int f = 64 * T.m + 16 * q + (lane & 15);
 #pragma unroll
           for (int j = 0; j < 16; j++) {
             const float mine = __uint_as_float(gate ? v[j] : v[16 + j]);
             const float send = __uint_as_float(gate ? v[16 + j] : v[j]);
             const float other = __shfl_xor_sync(0xFFFFFFFFu, send, 16);
             const float g = gate ? mine : other, u = gate ? other : mine;
-            const int tok = c0 + j + (gate ? 0 : 16);
-            if (tok < T.valid) {
-              const float h = __fdividef(g, 1.0f + __expf(-g)) * u;
-              p.out[(T.row0 + tok) * p.N + f] = __bfloat16_as_ushort(__float2bfloat16_rn(h));
-            }
+            const float h = __fdividef(g, 1.0f + __expf(-g)) * u;
+            const int tok = j + (gate ? 0 : 16);  // (within the chunk)
+            *reinterpret_cast<uint16_t*>(eb + tok * kEpiRow + 2 * (lane & 15)) = __bfloat16_as_ushort(__float2bfloat16_rn(h));
+          }
+          __syncwarp();
+          const int tok = c0 + lane;
+          if (tok < T.valid) {
+            const uint4* src = reinterpret_cast<const uint4*>(eb + lane * kEpiRow);
+            uint4* dst = reinterpret_cast<uint4*>(p.out + (T.row0 + tok) * p.N + 64 * T.m + 16 * q);
+            dst[0] = src[0];
+            dst[1] = src[1];
           }
         } else {
-          const int n = BM * T.m + 32 * q + lane;
 #pragma unroll
           for (int j = 0; j < 32; j++)
-            if (c0 + j < T.valid)
-              p.out[(T.row0 + c0 + j) * p.N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j])));
+            *reinterpret_cast<uint16_t*>(eb + j * kEpiRow + 2 * lane) = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j])));
+          __syncwarp();
+          const int tok = c0 + lane;
+          if (tok < T.valid) {
+            const uint4* src = reinterpret_cast<const uint4*>(eb + lane * kEpiRow);
+            uint4* dst = reinterpret_cast<uint4*>(p.out + (T.row0 + tok) * p.N + BM * T.m + 32 * q);
+#pragma unroll
+            for (int c = 0; c < 4; c++) dst[c] = src[c];
+          }
         }
+        __syncwarp();  // (the buffer is free for the next chunk)
       };
       uint32_t va[32], vb[32];
       tmem_ld32(base, va);
