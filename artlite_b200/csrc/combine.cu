@@ -3,6 +3,8 @@
 // rounding to the output type; and the dispatch-order gather of the token rows for the grouped GEMM.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -70,18 +72,22 @@ int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float*
   return launch_pdl(combine_kernel, dim3((unsigned)T), dim3(256), 0, st, y, y_dtype, slot, w, T, k, H, out, out_dtype);
 }
 
+// a grid-stride loop over 16-byte chunks of the output rows (8 values each): row i of xp = token perm[i] / k of x
 __global__ void __launch_bounds__(256) gather_kernel(const void* x, int x_dtype, const int32_t* perm, int64_t P, int k,
                                                      int H, uint16_t* xp) {
-  const int64_t i = blockIdx.x;
-  const int64_t t = perm[i] / k;
-  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+  const int per_row = H >> 3;
+  const int64_t n = P * per_row;
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < n; c += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = c / per_row;
+    const int col = (int)(c - i * per_row) * 8;
+    const int64_t t = perm[i] / k;
     if (x_dtype == ARTLITE_BF16) {
-      *reinterpret_cast<uint4*>(xp + i * H + c) =
-          *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + t * H + c);
+      *reinterpret_cast<uint4*>(xp + i * H + col) =
+          __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + t * H + col));
     } else {
       float v[8];
-      load8(x, ARTLITE_F32, t * H + c, v);
-      store8(xp, ARTLITE_BF16, i * H + c, v);
+      load8(x, ARTLITE_F32, t * H + col, v);
+      store8(xp, ARTLITE_BF16, i * H + col, v);
     }
   }
 }
@@ -90,7 +96,9 @@ int launch_gather(const void* x, int x_dtype, const int32_t* perm, int64_t P, in
                   cudaStream_t st) {
   AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "gather: H %d (a multiple of 8)", H);
   if (P == 0) return ARTLITE_OK;
-  gather_kernel<<<(unsigned)P, 256, 0, st>>>(x, x_dtype, perm, P, k, H, xp);
+  const int64_t chunks = P * (H / 8);
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(chunks, 256), (int64_t)kNumSMs * 16);
+  gather_kernel<<<grid, 256, 0, st>>>(x, x_dtype, perm, P, k, H, xp);
   AL_LAUNCHED();
   return ARTLITE_OK;
 }
