@@ -144,7 +144,8 @@ void small_plan(const artlite_moe& h, const artlite_moe::Layer& L, int path, int
 
 int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const void* x, int x_dtype, bool gathered,
                 const int32_t* perm, int k, int64_t P, int E_run, const int64_t* offsets, const int32_t* counts,
-                int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk, bool units_ready) {
+                int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk, bool units_ready,
+                const int32_t* wexp, int E_w) {
   const artlite_moe_desc& d = h->d;
   const int H = d.hidden, F = d.expert_ffn;
   *y_rows = h->y.ptr;
@@ -171,6 +172,7 @@ int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const voi
     g.offsets = offsets;
     g.unit_off = h->unit_gu.as<int32_t>();
     g.rt = rt_gu;
+    g.wexp = wexp;
     g.k = k;
     g.out = h->h.as<float>();
     AL_TRY(launch_gemv_gu(g, st));
@@ -212,6 +214,8 @@ int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const voi
   g.P = P;
   g.offsets = offsets;
   g.counts = counts;
+  g.wexp = wexp;
+  g.wE = E_w;
   g.sched = h->tiles.ptr;
   g.out = h->h.as<uint16_t>();
   AL_TRY(launch_tc_gemm(g, /*gu=*/true, st));

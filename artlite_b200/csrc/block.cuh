@@ -47,12 +47,16 @@ struct artlite_moe {
   std::vector<Graph> graphs;
   // expert parallelism (ep.cu): the NCCL communicator, exchange buffers, pinned host copies of the counts
   void* comm = nullptr;                // ncclComm_t
-  artlite::DevBuf ep_rcounts, ep_loff, ep_lcounts, ep_ident, ep_seg, xl, xr, yr, ys;
+  cudaStream_t ep_st = nullptr;        // the exchanges' stream (overlapping the experts)
+  static constexpr int kEpChunks = 4;  // the peers' row groups in up to this many expert chunks (pipelined)
+  int ep_chunks = 1;
+  cudaEvent_t ep_ev[2 + 2 * kEpChunks] = {};  // rows gathered, returns in, per chunk: rows in, outputs ready
+  artlite::DevBuf ep_rcounts, ep_loff, ep_lcounts, ep_wexp, ep_ident, xr, ys;
   int32_t* hb_counts = nullptr;        // pinned: [E] this rank's pairs per expert, then [world x E_local] received
-  int64_t* hb_loff = nullptr;          // pinned: [E_local + 1] offsets of the received rows per local expert
-  int32_t* hb_lcounts = nullptr;       // pinned: [E_local] received rows per local expert
-  int64_t* hb_seg = nullptr;           // pinned: [3][world x E_local] the received segments (from, to, rows)
-  std::vector<int64_t> ep_send_off, ep_recv_pos, ep_send_base, ep_recv_base, ep_send_rows, ep_recv_rows;
+  int64_t* hb_loff = nullptr;          // pinned: [world E_local + 1] the received row groups' offsets
+  int32_t* hb_lcounts = nullptr;       // pinned: [world E_local] their rows
+  std::vector<int64_t> ep_send_base, ep_recv_base, ep_send_rows, ep_recv_rows;  // per peer: blocks sent / received
+  std::vector<int64_t> ep_cs_pos, ep_cs_rows, ep_cr_pos, ep_cr_rows;  // per (peer, chunk): sent / received blocks
   int64_t ep_max_rows = 0;             // rows a rank can receive: max_tokens K world
   bool ep_failed = false;              // an exchange failed: the communicator is aborted, never waited for
 };
@@ -87,13 +91,16 @@ struct Marker {
 int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* x, int64_t T, cudaStream_t st,
                        Marker& mk, int mult_gu = 0, int mult_dn = 0);
 
+// wexp (device, may be null): the weight expert of each of the E_run row groups (expert parallelism: a group is one
+// source rank's rows of one local expert), E_w the experts the weights hold (0: E_run).
 // The experts of a forward over P rows for E_run experts (offsets / counts on the device): rows are the tokens x
 // through perm / k (gathered = false), or already gathered bf16 rows in expert order (gathered = true, perm = the
 // identity, k = 1). Output rows in the same order into *y_rows (the handle's y buffer), fp32 (GEMV path) or bf16
 // (tcgen05 path) in *y_dtype.
 int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const void* x, int x_dtype, bool gathered,
                 const int32_t* perm, int k, int64_t P, int E_run, const int64_t* offsets, const int32_t* counts,
-                int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk, bool units_ready = false);
+                int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk, bool units_ready = false,
+                const int32_t* wexp = nullptr, int E_w = 0);
 
 // which expert path a forward of P pairs takes
 int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L);
@@ -102,8 +109,6 @@ int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L);
 int wait_deadline(cudaStream_t st, int timeout_ms);
 
 // expert parallelism (ep.cu)
-int launch_segment_copy(const void* src, void* dst, const int64_t* s, const int64_t* d, const int64_t* n, int nseg,
-                        int64_t row_bytes, int64_t total_rows, cudaStream_t st);
 int ep_create(artlite_moe* h);
 int ep_forward(artlite_moe* h, int layer, const void* x, void* y, int64_t T, cudaStream_t st, Marker& mk);
 void ep_destroy(artlite_moe* h);

@@ -48,7 +48,7 @@ __device__ __forceinline__ void store8(void* base, int dtype, int64_t i, const f
 
 // one CTA per token row, 8 values per thread (H % 8 == 0)
 __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype, const int32_t* slot, const float* w,
-                                                      int64_t T, int k, int H, void* out, int out_dtype) {
+                                                      int64_t T, int k, int H, void* out, int out_dtype, CombineOwn own) {
   griddep_wait();
   griddep_launch();
   const int64_t t = blockIdx.x;
@@ -56,8 +56,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int i = 0; i < k; i++) {
       const float wi = w[t * k + i];
+      const int64_t sl = slot[t * k + i];
       float v[8];
-      load8(y, y_dtype, (int64_t)slot[t * k + i] * H + c, v);
+      if (own.own && sl >= own.own_lo && sl < own.own_hi)
+        load8(own.own, y_dtype, (sl - own.own_lo) * H + c, v);
+      else
+        load8(y, y_dtype, sl * H + c, v);
 #pragma unroll
       for (int j = 0; j < 8; j++) acc[j] = fmaf(wi, v[j], acc[j]);
     }
@@ -66,39 +70,42 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype
 }
 
 int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float* w, int64_t T, int k, int H, void* out,
-                   int out_dtype, cudaStream_t st) {
+                   int out_dtype, cudaStream_t st, CombineOwn own) {
   AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "combine: H %d (a multiple of 8)", H);
   if (T == 0) return ARTLITE_OK;
-  return launch_pdl(combine_kernel, dim3((unsigned)T), dim3(256), 0, st, y, y_dtype, slot, w, T, k, H, out, out_dtype);
+  return launch_pdl(combine_kernel, dim3((unsigned)T), dim3(256), 0, st, y, y_dtype, slot, w, T, k, H, out, out_dtype,
+                    own);
 }
 
 // a grid-stride loop over 16-byte chunks of the output rows (8 values each): row i of xp = token perm[i] / k of x
 __global__ void __launch_bounds__(256) gather_kernel(const void* x, int x_dtype, const int32_t* perm, int64_t P, int k,
-                                                     int H, uint16_t* xp) {
+                                                     int H, uint16_t* xp, uint16_t* own_dst, int64_t own_lo,
+                                                     int64_t own_hi) {
   const int per_row = H >> 3;
   const int64_t n = P * per_row;
   for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < n; c += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = c / per_row;
     const int col = (int)(c - i * per_row) * 8;
     const int64_t t = perm[i] / k;
+    uint16_t* dst = (own_dst && i >= own_lo && i < own_hi) ? own_dst + (i - own_lo) * H : xp + i * H;
     if (x_dtype == ARTLITE_BF16) {
-      *reinterpret_cast<uint4*>(xp + i * H + col) =
+      *reinterpret_cast<uint4*>(dst + col) =
           __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + t * H + col));
     } else {
       float v[8];
       load8(x, ARTLITE_F32, t * H + col, v);
-      store8(xp, ARTLITE_BF16, i * H + col, v);
+      store8(dst, ARTLITE_BF16, col, v);
     }
   }
 }
 
 int launch_gather(const void* x, int x_dtype, const int32_t* perm, int64_t P, int k, int H, uint16_t* xp,
-                  cudaStream_t st) {
+                  cudaStream_t st, uint16_t* own_dst, int64_t own_lo, int64_t own_hi) {
   AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "gather: H %d (a multiple of 8)", H);
   if (P == 0) return ARTLITE_OK;
   const int64_t chunks = P * (H / 8);
   const unsigned grid = (unsigned)std::min<int64_t>(cdiv(chunks, 256), (int64_t)kNumSMs * 16);
-  gather_kernel<<<grid, 256, 0, st>>>(x, x_dtype, perm, P, k, H, xp);
+  gather_kernel<<<grid, 256, 0, st>>>(x, x_dtype, perm, P, k, H, xp, own_dst, own_lo, own_hi);
   AL_LAUNCHED();
   return ARTLITE_OK;
 }

@@ -1,17 +1,20 @@
 // Expert parallelism across the GPUs of one node: rank r of W owns experts [r E / W, (r + 1) E / W) (their raw GGUF
 // rows only, set_weights) and its own tokens; per layer
-//   1. router, routing and the dispatch over all E experts, on the rank's tokens (block.cu: route_and_dispatch);
-//   2. the token rows gathered into expert order (bf16): contiguous per destination rank;
-//   3. per-expert pair counts exchanged (NCCL send / recv of E / W int32 per peer), read back to the host (the one
-//      host synchronisation of the layer: NCCL message sizes are host values), the exchange plan computed on the host
-//      (artlite_moe_ep_plan);
-//   4. the token rows exchanged with grouped ncclSend / ncclRecv, one message per peer (a rank's rows for a peer's
-//      experts are one contiguous block of its dispatch order), its own block by a device copy; the received blocks
-//      (rank-major, expert-minor) copied into expert-major order by a segment-copy kernel;
-//   5. the local experts on the received rows (block.cu: run_experts; the tcgen05 path or the GEMVs);
-//   6. the outputs copied back into rank-major blocks (the inverse segments), one message per peer, each landing
-//      as the contiguous block of the source rank's dispatch order it came from;
-//   7. the weighted combine of the rank's own tokens (combine.cu).
+//   1. router, routing and the dispatch over all E experts, on the rank's tokens (block.cu: route_and_dispatch); in
+//      dispatch order a rank's pairs for peer q's experts are one contiguous block;
+//   2. per-expert pair counts exchanged (NCCL send / recv of E / W int32 per peer), read back to the host (the one
+//      host synchronisation of the layer: NCCL message sizes are host values); the plan on the host: the send blocks,
+//      and the receive buffer's layout: the peers' blocks (q ascending), then the rank's own, each expert-major as its
+//      source dispatched it;
+//   3. the token rows gathered (bf16): rows for peers into the send buffer at their dispatch positions, the rank's own
+//      rows straight into their place in the receive buffer;
+//   4. the rows exchanged with grouped ncclSend / ncclRecv, one message per peer, on a second stream, while
+//   5. the local experts run on the rank's own row groups; then on the peers' groups: the receive buffer's W x (E / W)
+//      (source, expert) row groups each run in place against their expert's weights (run_experts with a weight-expert
+//      map), no regrouping copy;
+//   6. the outputs returned by one message per peer, each landing as the contiguous block of the source rank's dispatch
+//      order it came from; the rank's own block stays where its experts wrote it;
+//   7. the weighted combine of the rank's own tokens, its own rows read from the expert outputs (combine.cu).
 // NCCL is loaded at run time (dlopen "libnccl.so.2": the one a process that imported torch already holds, or the
 // system's), so the library itself has no link-time NCCL dependency. Waits on the host are bounded: a peer that never
 // sends makes the count exchange's wait run out, the communicator is aborted and the call returns ARTLITE_ETIMEOUT.
@@ -89,36 +92,12 @@ int nccl(Nccl** out) {
     }                                                                                               \
   } while (0)
 
-// rows of `row_bytes` (a multiple of 16) in segments: segment g's n[g] rows from src row s[g] to dst row d[g]
-__global__ void __launch_bounds__(256) segment_copy_kernel(const uint8_t* src, uint8_t* dst, const int64_t* s,
-                                                            const int64_t* d, const int64_t* n, int64_t row_bytes) {
-  const int g = blockIdx.y;
-  const int64_t rows = n[g];
-  const int64_t v16 = row_bytes / 16;
-  for (int64_t i = blockIdx.x; i < rows; i += gridDim.x) {
-    const uint4* a = reinterpret_cast<const uint4*>(src + (s[g] + i) * row_bytes);
-    uint4* b = reinterpret_cast<uint4*>(dst + (d[g] + i) * row_bytes);
-    for (int64_t j = threadIdx.x; j < v16; j += blockDim.x) b[j] = a[j];
-  }
-}
-
 __global__ void iota_kernel(int32_t* p, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = (int32_t)i;
 }
 
 }  // namespace
-
-int launch_segment_copy(const void* src, void* dst, const int64_t* s, const int64_t* d, const int64_t* n, int nseg,
-                        int64_t row_bytes, int64_t total_rows, cudaStream_t st) {
-  if (nseg == 0 || total_rows == 0) return ARTLITE_OK;
-  AL_CHECK(row_bytes % 16 == 0, ARTLITE_EINVAL, "segment copy: rows of %lld bytes", (long long)row_bytes);
-  const unsigned per = (unsigned)std::min<int64_t>(64, std::max<int64_t>(1, total_rows / nseg));
-  segment_copy_kernel<<<dim3(per, (unsigned)nseg), 256, 0, st>>>(static_cast<const uint8_t*>(src),
-                                                                  static_cast<uint8_t*>(dst), s, d, n, row_bytes);
-  AL_LAUNCHED();
-  return ARTLITE_OK;
-}
 
 int ep_create(artlite_moe* h) {
   const artlite_moe_desc& d = h->d;
@@ -127,30 +106,44 @@ int ep_create(artlite_moe* h) {
   const int64_t R = T * K * W;  // the most rows a rank can receive (every rank's pairs all on its experts)
   h->ep_max_rows = R;
   AL_TRY(h->ep_rcounts.reserve(sizeof(int32_t) * E));
-  AL_TRY(h->ep_loff.reserve(sizeof(int64_t) * (El + 1)));
-  AL_TRY(h->ep_lcounts.reserve(sizeof(int32_t) * El));
+  AL_TRY(h->ep_loff.reserve(sizeof(int64_t) * (E + 1)));  // the W El row groups' offsets in the receive buffer
+  AL_TRY(h->ep_lcounts.reserve(sizeof(int32_t) * E));     // their rows
+  AL_TRY(h->ep_wexp.reserve(sizeof(int32_t) * E));        // their weight experts: group q El + e -> e
   AL_TRY(h->ep_ident.reserve(sizeof(int32_t) * R));
-  AL_TRY(h->xl.reserve(sizeof(uint16_t) * (R + 256) * H));
-  AL_TRY(h->xr.reserve(sizeof(uint16_t) * R * H));
-  AL_TRY(h->yr.reserve(sizeof(float) * R * H));
-  AL_TRY(h->ep_seg.reserve(sizeof(int64_t) * 3 * E));
+  AL_TRY(h->xr.reserve(sizeof(uint16_t) * (R + 256) * H));  // (the tcgen05 path reads 256-row boxes)
   AL_TRY(h->ys.reserve(sizeof(float) * T * K * H));
   // the expert workspaces hold the received rows (h: fp32 or bf16 with 256 spare rows; y: fp32 or bf16)
   AL_TRY(h->h.reserve(std::max(sizeof(float) * R * F, sizeof(uint16_t) * (R + 256) * F)));
   AL_TRY(h->y.reserve(sizeof(float) * R * H));
-  AL_TRY(h->tiles.reserve(tc_sched_bytes(El)));
+  AL_TRY(h->tiles.reserve(tc_sched_bytes(E)));
+  AL_TRY(h->unit_gu.reserve(sizeof(int32_t) * (E + 1)));
+  AL_TRY(h->unit_dn.reserve(sizeof(int32_t) * (E + 1)));
   AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_counts), sizeof(int32_t) * 2 * E, cudaHostAllocDefault));
-  AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_loff), sizeof(int64_t) * (El + 1), cudaHostAllocDefault));
-  AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_lcounts), sizeof(int32_t) * El, cudaHostAllocDefault));
-  AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_seg), sizeof(int64_t) * 3 * E, cudaHostAllocDefault));
+  AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_loff), sizeof(int64_t) * (E + 1), cudaHostAllocDefault));
+  AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_lcounts), sizeof(int32_t) * E, cudaHostAllocDefault));
   h->ep_send_base.assign(W, 0);
   h->ep_recv_base.assign(W, 0);
   h->ep_send_rows.assign(W, 0);
   h->ep_recv_rows.assign(W, 0);
+  AL_CUDA(cudaStreamCreateWithFlags(&h->ep_st, cudaStreamNonBlocking));
+  for (cudaEvent_t& e : h->ep_ev) AL_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  h->ep_chunks = El % 4 == 0 ? 4 : El % 2 == 0 ? 2 : 1;
+  h->ep_cs_pos.assign((size_t)W * h->ep_chunks, 0);
+  h->ep_cs_rows.assign((size_t)W * h->ep_chunks, 0);
+  h->ep_cr_pos.assign((size_t)W * h->ep_chunks, 0);
+  h->ep_cr_rows.assign((size_t)W * h->ep_chunks, 0);
   iota_kernel<<<(unsigned)cdiv(R, 256), 256, 0, h->st>>>(h->ep_ident.as<int32_t>(), R);
   AL_LAUNCHED();
-  h->ep_send_off.assign(E, 0);
-  h->ep_recv_pos.assign((size_t)W * El, 0);
+  // the row groups' weight experts: chunk-major for the peers (chunk c, peer place qi, expert e of the chunk), then
+  // the own block's El groups
+  std::vector<int32_t> wexp(E);
+  const int C = h->ep_chunks, Ec = El / C;
+  for (int c = 0; c < C; c++)
+    for (int qi = 0; qi < W - 1; qi++)
+      for (int i = 0; i < Ec; i++) wexp[(c * (W - 1) + qi) * Ec + i] = c * Ec + i;
+  for (int e = 0; e < El; e++) wexp[(W - 1) * El + e] = e;
+  AL_CUDA(cudaMemcpyAsync(h->ep_wexp.ptr, wexp.data(), sizeof(int32_t) * E, cudaMemcpyHostToDevice, h->st));
+  AL_CUDA(cudaStreamSynchronize(h->st));
   return ARTLITE_OK;
 }
 
@@ -164,11 +157,12 @@ void ep_destroy(artlite_moe* h) {
     }
     h->comm = nullptr;
   }
+  for (cudaEvent_t& e : h->ep_ev)
+    if (e) cudaEventDestroy(e), e = nullptr;
+  if (h->ep_st) cudaStreamDestroy(h->ep_st), h->ep_st = nullptr;
   if (h->hb_counts) cudaFreeHost(h->hb_counts);
   if (h->hb_loff) cudaFreeHost(h->hb_loff);
   if (h->hb_lcounts) cudaFreeHost(h->hb_lcounts);
-  if (h->hb_seg) cudaFreeHost(h->hb_seg);
-  h->hb_seg = nullptr;
   h->hb_counts = nullptr;
   h->hb_loff = nullptr;
   h->hb_lcounts = nullptr;
@@ -208,10 +202,9 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   const artlite_moe::Layer& L = h->layers[layer];
   const int W = d.ep_world, r = d.ep_rank, El = h->E_local, E = d.n_experts, H = d.hidden, K = d.top_k;
   const int64_t P = T * K;
-  // 1-2: routing and the dispatch over all experts; the rows in expert order (contiguous per destination rank)
+  // 1: routing and the dispatch over all experts
   AL_TRY(route_and_dispatch(h, L, xd, T, st, mk));
-  if (P) AL_TRY(launch_gather(xd, d.act_dtype, h->perm.as<int32_t>(), P, K, H, h->xp.as<uint16_t>(), st));
-  // 3: counts, then the plan on the host
+  // 2: counts, then the plan on the host
   AL_NCCL(N->groupStart());
   for (int q = 0; q < W; q++) {
     AL_NCCL(N->send(h->counts.as<int32_t>() + q * El, El, ncclInt32, q, comm, st));
@@ -228,86 +221,155 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
     return ARTLITE_ETIMEOUT;
   }
   AL_TRY(rc);
-  AL_TRY(artlite_moe_ep_plan(h->hb_counts, h->hb_counts + E, W, r, E, h->ep_send_off.data(), h->ep_recv_pos.data(),
-                             h->hb_loff, h->hb_lcounts));
-  const int64_t Rl = h->hb_loff[El];
-  AL_CHECK(Rl <= h->ep_max_rows, ARTLITE_EDEVICE, "expert parallelism: %lld rows received, room for %lld",
-           (long long)Rl, (long long)h->ep_max_rows);
-  // per rank q: the block this rank sends (its rows for q's experts, contiguous in dispatch order) and the block it
-  // receives (q's rows for this rank's experts: expert-major inside); the segments (q, e) of the received blocks and
-  // their places in expert-grouped order
-  const int32_t* sc = h->hb_counts;
-  const int32_t* rcv = h->hb_counts + E;
-  int64_t* seg = h->hb_seg;  // [3][W El]: source row, destination row, rows
+  const int32_t* sc = h->hb_counts;      // this rank's pairs per expert (all E)
+  const int32_t* rcv = h->hb_counts + E; // [q][e]: peer q's pairs for local expert e
   std::vector<int64_t>& send_base = h->ep_send_base;
   std::vector<int64_t>& recv_base = h->ep_recv_base;
   std::vector<int64_t>& send_rows = h->ep_send_rows;
   std::vector<int64_t>& recv_rows = h->ep_recv_rows;
-  int64_t rb = 0;
+  // The plan. Sent blocks: in dispatch order, peer q's experts' rows are one block (send_base / send_rows), chunk c of
+  // its experts a contiguous part of it. Receive buffer: chunk-major over the peers' blocks (chunk c: peer q ascending,
+  // its rows of chunk c's experts as it dispatched them), then this rank's own block; the row groups in that same order
+  // (group of (chunk c, peer place qi, expert) = (c (W - 1) + qi) Ec + i), so every chunk is one contiguous range of
+  // groups and of rows.
+  const int C = h->ep_chunks, Ec = El / C;
+  int64_t sb = 0;
   for (int q = 0; q < W; q++) {
-    send_base[q] = h->ep_send_off[(size_t)q * El];
-    int64_t sn = 0, rn = 0;
-    for (int e = 0; e < El; e++) {
-      const int g = q * El + e;
-      sn += sc[g];
-      seg[g] = rb + rn;                                  // where (q, e)'s rows sit in the received block
-      seg[W * El + g] = h->ep_recv_pos[(size_t)q * El + e];  // where they go (expert-grouped)
-      seg[2 * W * El + g] = rcv[g];
-      rn += rcv[g];
+    send_base[q] = sb;
+    int64_t sn = 0;
+    for (int c = 0; c < C; c++) {
+      int64_t n = 0;
+      for (int i = 0; i < Ec; i++) {
+        const int32_t v = sc[q * El + c * Ec + i];
+        AL_CHECK(v >= 0, ARTLITE_EDEVICE, "expert parallelism: count %d", v);
+        n += v;
+      }
+      h->ep_cs_pos[(size_t)q * C + c] = sb + sn;
+      h->ep_cs_rows[(size_t)q * C + c] = n;
+      sn += n;
     }
     send_rows[q] = sn;
-    recv_base[q] = rb;
-    recv_rows[q] = rn;
-    rb += rn;
+    sb += sn;
   }
-  AL_CUDA(cudaMemcpyAsync(h->ep_loff.ptr, h->hb_loff, sizeof(int64_t) * (El + 1), cudaMemcpyHostToDevice, st));
-  AL_CUDA(cudaMemcpyAsync(h->ep_lcounts.ptr, h->hb_lcounts, sizeof(int32_t) * El, cudaMemcpyHostToDevice, st));
-  AL_CUDA(cudaMemcpyAsync(h->ep_seg.ptr, seg, sizeof(int64_t) * 3 * W * El, cudaMemcpyHostToDevice, st));
-  const int64_t* dseg = h->ep_seg.as<int64_t>();
-  // 4: the token rows, one message per peer; this rank's own block by a device copy; then into expert order
-  const uint16_t* xp = h->xp.as<uint16_t>();
+  int64_t rb = 0;
+  for (int q = 0; q < W; q++) recv_rows[q] = 0;
+  for (int c = 0; c < C; c++)
+    for (int qi = 0; qi < W - 1; qi++) {
+      const int q = qi < r ? qi : qi + 1;
+      const int64_t start = rb;
+      for (int i = 0; i < Ec; i++) {
+        const int e = c * Ec + i, j = (c * (W - 1) + qi) * Ec + i;
+        const int32_t v = rcv[q * El + e];
+        AL_CHECK(v >= 0, ARTLITE_EDEVICE, "expert parallelism: count %d from rank %d", v, q);
+        h->hb_loff[j] = rb;
+        h->hb_lcounts[j] = v;
+        rb += v;
+      }
+      h->ep_cr_pos[(size_t)q * C + c] = start;
+      h->ep_cr_rows[(size_t)q * C + c] = rb - start;
+      recv_rows[q] += rb - start;
+    }
+  recv_base[r] = rb;
+  for (int e = 0; e < El; e++) {
+    const int j = (W - 1) * El + e;
+    const int32_t v = rcv[r * El + e];
+    AL_CHECK(v >= 0, ARTLITE_EDEVICE, "expert parallelism: count %d", v);
+    h->hb_loff[j] = rb;
+    h->hb_lcounts[j] = v;
+    rb += v;
+  }
+  recv_rows[r] = rb - recv_base[r];
+  h->hb_loff[E] = rb;
+  const int64_t Rl = rb;
+  AL_CHECK(sb == P && Rl <= h->ep_max_rows, ARTLITE_EDEVICE,
+           "expert parallelism: %lld rows sent of %lld, %lld received, room for %lld", (long long)sb, (long long)P,
+           (long long)Rl, (long long)h->ep_max_rows);
+  AL_CHECK(send_rows[r] == recv_rows[r], ARTLITE_EDEVICE, "expert parallelism: own block %lld / %lld rows",
+           (long long)send_rows[r], (long long)recv_rows[r]);
+  AL_CUDA(cudaMemcpyAsync(h->ep_loff.ptr, h->hb_loff, sizeof(int64_t) * (E + 1), cudaMemcpyHostToDevice, st));
+  AL_CUDA(cudaMemcpyAsync(h->ep_lcounts.ptr, h->hb_lcounts, sizeof(int32_t) * E, cudaMemcpyHostToDevice, st));
+  // 3: the rows in dispatch order: the peers' blocks into the send buffer, this rank's own block into its place in the
+  // receive buffer
+  uint16_t* xp = h->xp.as<uint16_t>();
   uint16_t* xr = h->xr.as<uint16_t>();
-  uint16_t* xl = h->xl.as<uint16_t>();
-  AL_NCCL(N->groupStart());
-  for (int q = 0; q < W; q++) {
-    if (q == r) continue;
-    if (send_rows[q]) AL_NCCL(N->send(xp + send_base[q] * H, (size_t)send_rows[q] * H, ncclBfloat16, q, comm, st));
-    if (recv_rows[q]) AL_NCCL(N->recv(xr + recv_base[q] * H, (size_t)recv_rows[q] * H, ncclBfloat16, q, comm, st));
-  }
-  AL_NCCL(N->groupEnd());
-  if (send_rows[r])
-    AL_CUDA(cudaMemcpyAsync(xr + recv_base[r] * H, xp + send_base[r] * H, sizeof(uint16_t) * send_rows[r] * H,
-                            cudaMemcpyDeviceToDevice, st));
-  AL_TRY(launch_segment_copy(xr, xl, dseg, dseg + W * El, dseg + 2 * W * El, W * El, (int64_t)H * 2, Rl, st));
+  if (P)
+    AL_TRY(launch_gather(xd, d.act_dtype, h->perm.as<int32_t>(), P, K, H, xp, st, xr + recv_base[r] * H, send_base[r],
+                         send_base[r] + send_rows[r]));
+  cudaEvent_t ev_g = h->ep_ev[0], ev_b = h->ep_ev[1];
+  cudaEvent_t* ev_r = h->ep_ev + 2;      // [C] a chunk's rows received
+  cudaEvent_t* ev_y = h->ep_ev + 2 + C;  // [C] a chunk's outputs ready
+  AL_CUDA(cudaEventRecord(ev_g, st));
   AL_TRY(mk.mark());
-  // 5: the local experts
+  // 4: the peers' rows, chunk by chunk, on the exchange stream
+  AL_CUDA(cudaStreamWaitEvent(h->ep_st, ev_g, 0));
+  for (int c = 0; c < C; c++) {
+    AL_NCCL(N->groupStart());
+    for (int q = 0; q < W; q++) {
+      if (q == r) continue;
+      const size_t k = (size_t)q * C + c;
+      if (h->ep_cs_rows[k])
+        AL_NCCL(N->send(xp + h->ep_cs_pos[k] * H, (size_t)h->ep_cs_rows[k] * H, ncclBfloat16, q, comm, h->ep_st));
+      if (h->ep_cr_rows[k])
+        AL_NCCL(N->recv(xr + h->ep_cr_pos[k] * H, (size_t)h->ep_cr_rows[k] * H, ncclBfloat16, q, comm, h->ep_st));
+    }
+    AL_NCCL(N->groupEnd());
+    AL_CUDA(cudaEventRecord(ev_r[c], h->ep_st));
+  }
+  // 5: the local experts in place: the own groups while the rows travel, then each chunk of the peers' groups once its
+  // rows are in, its outputs handed to the exchange stream
   const int path = expert_path(*h, Rl, L);
   h->last_path = path;
   h->paths[layer] = path;
-  void* yrows;
-  int ydt;
-  AL_TRY(run_experts(h, L, path, xl, ARTLITE_BF16, true, h->ep_ident.as<int32_t>(), 1, Rl, El,
-                     h->ep_loff.as<int64_t>(), h->ep_lcounts.as<int32_t>(), (int64_t)(h->xl.bytes / (2 * H)), &yrows,
-                     &ydt, st, mk));
-  // 6: the outputs back: into per-rank blocks (the inverse segments), one message per peer, into dispatch order
+  void* yrows = nullptr;
+  int ydt = 0;
+  const int64_t* goff = h->ep_loff.as<int64_t>();
+  const int32_t* gcnt = h->ep_lcounts.as<int32_t>();
+  const int32_t* gexp = h->ep_wexp.as<int32_t>();
+  const int64_t xr_rows = (int64_t)(h->xr.bytes / (2 * H));
+  const int32_t* ident = h->ep_ident.as<int32_t>();
+  Marker quiet{h, layer, st};
+  quiet.ns = kStages;  // (no stage events inside the expert calls)
+  const int jo = (W - 1) * El;
+  AL_TRY(run_experts(h, L, path, xr, ARTLITE_BF16, true, ident, 1, recv_rows[r], El, goff + jo, gcnt + jo, xr_rows,
+                     &yrows, &ydt, st, quiet, false, gexp + jo, El));
+  AL_TRY(mk.mark());
+  const int Gc = (W - 1) * Ec;  // groups a chunk
+  for (int c = 0; c < C; c++) {
+    AL_CUDA(cudaStreamWaitEvent(st, ev_r[c], 0));
+    int64_t rows = 0;
+    for (int q = 0; q < W; q++)
+      if (q != r) rows += h->ep_cr_rows[(size_t)q * C + c];
+    if (Gc)
+      AL_TRY(run_experts(h, L, path, xr, ARTLITE_BF16, true, ident, 1, rows, Gc, goff + c * Gc, gcnt + c * Gc, xr_rows,
+                         &yrows, &ydt, st, quiet, false, gexp + c * Gc, El));
+    AL_CUDA(cudaEventRecord(ev_y[c], st));
+  }
+  AL_TRY(mk.mark());
+  // 6: the outputs back, chunk by chunk, each landing as the block of the source's dispatch order it came from
   const size_t el = ydt == ARTLITE_BF16 ? 2 : 4;
   const ncclDataType_t dt = ydt == ARTLITE_BF16 ? ncclBfloat16 : ncclFloat32;
-  uint8_t* yr = h->yr.as<uint8_t>();
+  uint8_t* yo = static_cast<uint8_t*>(yrows);
   uint8_t* ys = h->ys.as<uint8_t>();
-  AL_TRY(launch_segment_copy(yrows, yr, dseg + W * El, dseg, dseg + 2 * W * El, W * El, (int64_t)H * el, Rl, st));
-  AL_NCCL(N->groupStart());
-  for (int q = 0; q < W; q++) {
-    if (q == r) continue;
-    if (recv_rows[q]) AL_NCCL(N->send(yr + recv_base[q] * H * el, (size_t)recv_rows[q] * H, dt, q, comm, st));
-    if (send_rows[q]) AL_NCCL(N->recv(ys + send_base[q] * H * el, (size_t)send_rows[q] * H, dt, q, comm, st));
+  for (int c = 0; c < C; c++) {
+    AL_CUDA(cudaStreamWaitEvent(h->ep_st, ev_y[c], 0));
+    AL_NCCL(N->groupStart());
+    for (int q = 0; q < W; q++) {
+      if (q == r) continue;
+      const size_t k = (size_t)q * C + c;
+      if (h->ep_cr_rows[k]) AL_NCCL(N->send(yo + h->ep_cr_pos[k] * H * el, (size_t)h->ep_cr_rows[k] * H, dt, q, comm, h->ep_st));
+      if (h->ep_cs_rows[k]) AL_NCCL(N->recv(ys + h->ep_cs_pos[k] * H * el, (size_t)h->ep_cs_rows[k] * H, dt, q, comm, h->ep_st));
+    }
+    AL_NCCL(N->groupEnd());
   }
-  AL_NCCL(N->groupEnd());
-  if (send_rows[r])
-    AL_CUDA(cudaMemcpyAsync(ys + send_base[r] * H * el, yr + recv_base[r] * H * el, el * send_rows[r] * H,
-                            cudaMemcpyDeviceToDevice, st));
+  AL_CUDA(cudaEventRecord(ev_b, h->ep_st));
+  AL_CUDA(cudaStreamWaitEvent(st, ev_b, 0));
   AL_TRY(mk.mark());
-  // 7: the combine of this rank's tokens
-  if (T) AL_TRY(launch_combine(ys, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st));
+  // 7: the combine of this rank's tokens (its own block read where its experts wrote it)
+  CombineOwn own;
+  own.own = yo + recv_base[r] * H * el;
+  own.own_lo = send_base[r];
+  own.own_hi = send_base[r] + send_rows[r];
+  if (T) AL_TRY(launch_combine(ys, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st, own));
   return ARTLITE_OK;
 }
 }  // namespace

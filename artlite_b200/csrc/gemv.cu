@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(kWarps * 32) expert_gemv(ExpertGemvArgs a, con
   int offs[2][2];  // per stage, per tensor: the first row's offset in the staged bytes
   auto stage = [&](int i, int buf) {
     const Item it = item_of(unit_off, a.E, ntile, i);
-    const int64_t r0 = (int64_t)it.e * a.N + (int64_t)it.rt * RT;
+    const int64_t r0 = (int64_t)(a.wexp ? a.wexp[it.e] : it.e) * a.N + (int64_t)it.rt * RT;
     offs[buf][0] = stage_rows(raw + buf * stage_bytes, a.w0, r0, RT, a.row_bytes);
     if (GU) offs[buf][1] = stage_rows(raw + buf * stage_bytes + raw_bytes, a.w1, r0, RT, a.row_bytes);
     cp_async_commit();

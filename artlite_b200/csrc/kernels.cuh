@@ -99,6 +99,8 @@ struct ExpertGemvArgs {
   const int64_t* offsets;  // [E + 1]
   const int32_t* unit_off; // [E + 1] items per expert, ceil(n_e / 8) * ceil(N / rt), scanned (launch_unit_scan)
   int rt;                  // weight rows per item (gemv_row_tile(N))
+  const int32_t* wexp;     // (may be null) the weight expert of each of the E row groups (expert parallelism: a row
+                           // group is one source rank's rows of one local expert); null: group e uses expert e
   int k;
   float* out;        // gu: h (P x F fp32, dispatch order); down: y (P x H fp32, dispatch order)
 };
@@ -114,11 +116,18 @@ int launch_unit_scan(const int32_t* counts, int E, int unit_rows, int mult, int3
 
 // ---------------------------------------------------------------- combine.cu
 // out[t] = sum_i w[t, i] y[slot[t k + i]] in slot order, fp32; out f32 or bf16. y rows are f32 (y_dtype F32) or bf16.
+// Rows slot in [own_lo, own_hi) come from own + (s - own_lo) rows instead of y + s rows (expert parallelism: the rank's
+// own block stays where its experts wrote it); own = null: every row from y.
+struct CombineOwn {
+  const void* own = nullptr;
+  int64_t own_lo = 0, own_hi = 0;
+};
 int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float* w, int64_t T, int k, int H, void* out,
-                   int out_dtype, cudaStream_t st);
+                   int out_dtype, cudaStream_t st, CombineOwn own = CombineOwn{});
 
-// gather x rows into dispatch order: xp[i] = x[perm[i] / k] (bf16 out; x f32 or bf16)
+// gather x rows into dispatch order: xp[i] = x[perm[i] / k] (bf16 out; x f32 or bf16); rows i in [own_lo, own_hi)
+// go to own_dst + (i - own_lo) rows instead (own_dst null: all to xp)
 int launch_gather(const void* x, int x_dtype, const int32_t* perm, int64_t P, int k, int H, uint16_t* xp,
-                  cudaStream_t st);
+                  cudaStream_t st, uint16_t* own_dst = nullptr, int64_t own_lo = 0, int64_t own_hi = 0);
 
 }  // namespace artlite

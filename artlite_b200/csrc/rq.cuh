@@ -248,7 +248,8 @@ __device__ __forceinline__ void run_items(const ExpertGemvArgs& a, int R, const 
     const bool valid = slot < nslot && row < a.N;
     uint32_t w[Seg<QT>::words];
     if (valid) {  // (issued before the staging below: their latency overlaps it)
-      const uint8_t* p = (mat ? a.w1 : a.w0) + ((int64_t)lo * a.N + row) * a.row_bytes + (int64_t)seg * Seg<QT>::bytes;
+      const int64_t we = a.wexp ? a.wexp[lo] : lo;  // (the row group's weight expert)
+      const uint8_t* p = (mat ? a.w1 : a.w0) + (we * a.N + row) * a.row_bytes + (int64_t)seg * Seg<QT>::bytes;
 #pragma unroll
       for (int v = 0; v < Seg<QT>::v16; v++) {
         const uint4 u = ldg_stream(p + 16 * v);

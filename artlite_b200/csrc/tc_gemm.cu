@@ -48,6 +48,7 @@ __host__ __device__ constexpr int raw_stages(int qt) { return qt == ARTLITE_Q8_0
 struct Params {
   CUtensorMap map_w0, map_w1, map_x;
   const int64_t* offsets;
+  const int32_t* wexp;  // (may be null) the weight expert of each row group
   const int32_t* toff;  // [E + 1] tiles per expert (ceil(n_e / 256) * MT), scanned
   uint16_t* out;
   DevStatus* status;
@@ -151,6 +152,7 @@ __device__ __forceinline__ void tmem_wait32(uint32_t (&v)[32]) {
 
 struct Tile {
   int e, m;
+  int we;        // the weight expert of row group e
   int64_t row0;  // dispatch row of the tile's first token
   int valid;     // tokens in the tile
   int n_mma;     // MMA N: valid rounded up to 16
@@ -166,6 +168,7 @@ __device__ __forceinline__ Tile tile_of(const Params& p, int t) {
   const int j = local / p.MT;
   Tile T;
   T.e = lo;
+  T.we = p.wexp ? p.wexp[lo] : lo;
   T.m = local % p.MT;
   const int64_t o = p.offsets[lo];
   const int n_e = (int)(p.offsets[lo + 1] - o);
@@ -475,11 +478,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
         uint8_t* dst = sR + r * BM * CB;
         mbar_expect_tx(&sm->raw_full[r], BM * CB);
         if (GU) {
-          const int row = T.e * p.N + 64 * m;
+          const int row = T.we * p.N + 64 * m;
           tma_load_2d(dst, &p.map_w0, &sm->raw_full[r], kc * (CB / 2), row);
           tma_load_2d(dst + 64 * CB, &p.map_w1, &sm->raw_full[r], kc * (CB / 2), row);
         } else {
-          tma_load_2d(dst, &p.map_w0, &sm->raw_full[r], kc * (CB / 2), T.e * p.N + BM * m);
+          tma_load_2d(dst, &p.map_w0, &sm->raw_full[r], kc * (CB / 2), T.we * p.N + BM * m);
         }
         if (++r == R) r = 0, rph ^= 1;
       }
@@ -910,13 +913,14 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
   const int MT = (gu ? a.N / 64 : a.N / tc::BM) / (pair ? 2 : 1);  // tiles of weight rows per token tile
   tc::Params p{};
   const int cb = tc::chunk_bytes(a.qtype);
-  const int64_t wrows = (int64_t)a.E * a.N;
+  const int64_t wrows = (int64_t)(a.wE > 0 ? a.wE : a.E) * a.N;
   AL_TRY(make_map(&p.map_w0, a.w0, a.row_bytes / 2, wrows, cb / 2, gu ? 64 : tc::BM, false));
   if (gu) AL_TRY(make_map(&p.map_w1, a.w1, a.row_bytes / 2, wrows, cb / 2, 64, false));
   else p.map_w1 = p.map_w0;
   AL_TRY(make_map(&p.map_x, a.x, a.K, a.x_rows, tc::BK, pair ? tc::BNMAX / 2 : tc::BNMAX, true));
   AL_TRY(launch_unit_scan(a.counts, a.E, tc::BNMAX, MT, static_cast<int32_t*>(a.sched), st));
   p.offsets = a.offsets;
+  p.wexp = a.wexp;
   p.toff = static_cast<const int32_t*>(a.sched);
   p.out = a.out;
   p.status = a.status;

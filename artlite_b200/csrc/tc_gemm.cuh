@@ -20,8 +20,10 @@ struct TcGemmArgs {
   const uint16_t* x;      // bf16 rows in dispatch order (gu: gathered tokens, P x H; down: h, P x F)
   int64_t x_rows;         // rows the x buffer holds (>= P + 256: the token tiles read whole 256-row boxes)
   int64_t P;
-  const int64_t* offsets; // [E + 1]
+  const int64_t* offsets; // [E + 1] the E row groups' first rows in x
   const int32_t* counts;  // [E]
+  const int32_t* wexp;    // (may be null) each row group's weight expert (expert parallelism); null: group e, expert e
+  int wE;                 // experts in the weight tensors (0: E)
   void* sched;            // tc_sched_bytes(E) of device scratch (the tile scan)
   uint16_t* out;          // bf16 rows in dispatch order (gu: h, P x F; down: y, P x H)
   DevStatus* status;

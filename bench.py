@@ -383,20 +383,30 @@ def main() -> None:
     peaks, peak_src = measured_peaks()
     # stages (tc path): router, route+dispatch, gather + gate/up, down, combine
     roof = None
-    if path == "tc" and stages.shape[1] >= 4:
-        gu_ms = float(stages[:, 3 if world > 1 else 2].mean())
+    if path == "tc" and stages.shape[1] >= 4 and world == 1:
+        gu_ms = float(stages[:, 2].mean())
         P = T * K
         flops = 2.0 * P * H * (2 * F)
         achieved = flops / (gu_ms / 1000.0) / 1e12
         peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
-        roof = {"kernel": "tc_expert_gemm<Q4_0, gate/up>" + ("" if world > 1 else " (+ the dispatch gather, same stage)"),
-                "bound": "tensor",
+        roof = {"kernel": "tc_expert_gemm<Q4_0, gate/up> (+ the dispatch gather, same stage)", "bound": "tensor",
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "traffic": traffic_from_profiles(), "peak_source": f"{peak_src} bf16_tflops_sustained",
                 "flops_per_launch": flops, "ms_per_launch": gu_ms}
+    elif path == "tc" and stages.shape[1] >= 5:  # expert parallel: both expert GEMMs, the row exchange overlapped
+        ex_ms = float((stages[:, 3] + stages[:, 4]).mean())
+        P = T * K  # (a rank's experts process about as many rows as it dispatches)
+        flops = 2.0 * P * H * (2 * F) + 2.0 * P * F * H
+        achieved = flops / (ex_ms / 1000.0) / 1e12
+        peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+        roof = {"kernel": "tc_expert_gemm<Q4_0> gate/up + down of a rank (its own rows, then the peers' in chunks, "
+                          "the exchanges overlapped)", "bound": "tensor",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": None, "peak_source": f"{peak_src} bf16_tflops_sustained",
+                "flops_per_launch": flops, "ms_per_launch": ex_ms}
     if world > 1:
-        stage_names = ["router", "route+dispatch", "gather+count/row exchange", "gate_up", "down", "return exchange",
-                       "combine"]
+        stage_names = ["router", "route+dispatch", "count exchange+gather", "own experts (rows in flight)",
+                       "peer experts (chunks, exchanges overlapped)", "return exchange (rest)", "combine"]
     else:
         stage_names = ["router", "route+dispatch", "gather+gate_up", "down", "combine"] if path == "tc" else \
             ["router", "route+dispatch", "gate_up", "down", "combine"]

@@ -202,7 +202,9 @@ int artlite_moe_ep_init(artlite_moe* h, const void* unique_id, int bytes);
  * (world x E / world) the pairs each rank sends for this rank's experts. Out: send_off (E) each expert's first row in
  * this rank's expert-ordered rows; recv_pos (world x E / world) where the rows from rank q for local expert e land in
  * the received rows (grouped by local expert, then by rank); local_off (E / world + 1) / local_counts (E / world) the
- * received rows per local expert.
+ * received rows per local expert. (The block's own forward keeps the received blocks source-major and runs each
+ * (source rank, local expert) row group in place; this plan gives the expert-grouped layout to callers that exchange
+ * rows themselves.)
  */
 int artlite_moe_ep_plan(const int32_t* send_counts, const int32_t* recv_counts, int world, int rank, int E,
                         int64_t* send_off, int64_t* recv_pos, int64_t* local_off, int32_t* local_counts);

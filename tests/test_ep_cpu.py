@@ -2,7 +2,8 @@
 by expert, the ranks exchange counts, the library's host planner (``artlite_moe_ep_plan``) places each rank's rows in
 expert-grouped order on the owner, the owners apply their experts, the outputs return into each rank's dispatch
 order and every rank combines its own tokens. The result must equal the single-process block on the same tokens.
-The data moves by gloo collectives here; on GPUs the same plan drives NCCL send / recv (artlite_b200/csrc/ep.cu).
+The data moves by gloo collectives here; on GPUs the block moves the same blocks by NCCL send / recv and keeps the
+received rows source-major, each (source rank, local expert) group run in place (artlite_b200/csrc/ep.cu).
 
 Also: a rank that never joins the exchange ends the others' collective with an error after a short process-group
 timeout (the host side of the failure detection; no GPU involved)."""
