@@ -2,6 +2,9 @@
 blocks, H=2048, E=128, top-8, F=768, Q4_0 weights, 16384 tokens), and the CPU reference arm.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --decode            BASELINE config 2 (decode batches 1 / 4 / 16 / 64, Q4_K), one line per batch
+    python bench.py --config 3 | 5      BASELINE config 3 (prefill, Q8_0, Zipf-skewed routing) or 5 (Qwen3-235B-A22B
+                                        shape: H 4096, F 1536, Q4_0, 8192-token prefill and a 64-token decode batch)
 
 One step = one forward of every layer of the stack over the step's token batch (the layers are independent blocks,
 each with its own weights, all fed the same batch: the synthetic random weights would overflow bf16 through a chained
@@ -11,8 +14,9 @@ Our arm: weights are generated on the GPU (seeded torch CUDA generator: fp16 d f
 router fp32 N(0, 0.02); x bf16 N(0, 1)) and handed to the library as raw GGUF blocks; inputs resident in HBM before
 the timed region; the weights stream from HBM each layer (340 MB a layer, far above the 126 MB L2, so no L2 flush is
 needed). The timed region: W untimed steps, then K steps between CUDA events on the launching stream, a barrier and
-a synchronize on both sides, the max over ranks. `e2e`: the same steps through the C ABI with pinned HOST x / y buffers
-(the library copies x in and y out on every call, inside the timed region). With N > 1 the block is expert-parallel:
+a synchronize on both sides, the max over ranks. `e2e`: whole steps from pinned host memory to pinned host memory
+(the step's tokens copied in, the layers through the C ABI, the last layer given the host output buffer: the library
+copies the result back inside the call), inside the timed region. With N > 1 the block is expert-parallel:
 rank r owns experts [r E / N, (r + 1) E / N) and T / N of the 16384 tokens; every layer exchanges token rows and
 expert outputs over NCCL (artlite_b200/csrc/ep.cu): strong scaling (the total work is fixed).
 
@@ -60,6 +64,10 @@ REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_c
 
 
 class Clocks:
+    """nvidia-smi samples of the SM clock and throttle reasons every 50 ms, started before the warm-up (so that the
+    sampler runs when the timed region starts); stop(t0, t1) keeps the samples taken within [t0, t1] (host time), or
+    the one nearest to it when the region is shorter than the interval."""
+
     def __init__(self, gpu: int):
         self.gpu, self.proc, self.lines = gpu, None, []
 
@@ -67,7 +75,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
-                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                 text=True)
             threading.Thread(target=self._read, daemon=True).start()
         except OSError:
@@ -75,28 +83,33 @@ class Clocks:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
-    def stop(self) -> dict:
+    def stop(self, t0: float = 0.0, t1: float = float("inf")) -> dict:
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-        sm, mx, reasons = [], 0, set()
-        for ln in self.lines:
+        rows = []
+        for ts, ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 3:
                 continue
             try:
-                s, m, r = float(parts[0]), float(parts[1]), int(parts[2], 16)
+                rows.append((ts, float(parts[0]), float(parts[1]), int(parts[2], 16)))
             except ValueError:
                 continue
-            sm.append(s)
-            mx = max(mx, m)
+        inside = [r for r in rows if t0 <= r[0] <= t1]
+        if not inside and rows:
+            inside = [min(rows, key=lambda r: min(abs(r[0] - t0), abs(r[0] - t1)))]
+        sm = [r[1] for r in inside]
+        mx = max((r[2] for r in inside), default=0)
+        reasons = set()
+        for r in inside:
             for bit, name in REASONS.items():
-                if r & bit and name != "gpu_idle":
+                if r[3] & bit and name != "gpu_idle":
                     reasons.add(name)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None, "reasons": sorted(reasons),
                 "samples": len(sm)}
@@ -185,6 +198,94 @@ def gen_layer_q4k(torch, g, dev):
     return q4k(E * F, H), q4k(E * F, H), q4k(E * H, F), router
 
 
+def gen_q(torch, g, dev, qtype, rows, cols):
+    """Raw GGUF rows of `qtype` on the GPU with BASELINE's distributions (fp16 scales |N(0, 0.02)|; Q4_0 nibbles
+    uniform; Q8_0 int8 uniform -127..127)."""
+    if qtype == "Q4_0":
+        n = cols // 32
+        raw = torch.empty((rows, n, 18), dtype=torch.uint8, device=dev)
+        raw[..., 2:] = torch.randint(0, 256, (rows, n, 16), dtype=torch.uint8, generator=g, device=dev)
+    elif qtype == "Q8_0":
+        n = cols // 32
+        raw = torch.empty((rows, n, 34), dtype=torch.uint8, device=dev)
+        q = torch.randint(-127, 128, (rows, n, 32), dtype=torch.int16, generator=g, device=dev)
+        raw[..., 2:] = q.to(torch.int8).view(torch.uint8)
+    else:
+        raise ValueError(qtype)
+    d = (torch.randn((rows, n), generator=g, device=dev) * 0.02).abs().half()
+    raw[..., 0:2] = d.view(torch.uint8).view(rows, n, 2)
+    return raw.view(rows, -1)
+
+
+def run_config(args) -> None:
+    """BASELINE configs 3 and 5 on one GPU, --layers layers of independent weights in turn (one JSON line per measured
+    shape): tokens x layers / s, ms per layer, and the gate/up GEMM's share of the tensor roofline (tcgen05 path)."""
+    import torch
+    from artlite_b200.moe.block import MoEBlock
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.config == 3:
+        h_, e_, k_, f_, qt, shapes = 2048, 128, 8, 768, "Q8_0", [("config3-prefill-q8_0-t4096-zipf1.1", 4096)]
+    else:
+        h_, e_, k_, f_, qt = 4096, 128, 8, 1536, "Q4_0"
+        shapes = [("config5-prefill-q4_0-h4096-f1536-t8192", 8192), ("config5-decode-q4_0-h4096-f1536-b64", 64)]
+    L = args.layers
+    tmax = max(t for _, t in shapes)
+    block = MoEBlock(hidden=h_, n_experts=e_, top_k=k_, expert_ffn=f_, max_tokens=tmax, n_layers=L, act_dtype="bf16",
+                     device=0, path="auto")
+    g = torch.Generator(device=dev)
+    g.manual_seed(4000 + args.config)
+    for layer in range(L):
+        gate, up, down = gen_q(torch, g, dev, qt, e_ * f_, h_), gen_q(torch, g, dev, qt, e_ * f_, h_), \
+            gen_q(torch, g, dev, qt, e_ * h_, f_)
+        router = torch.randn((e_, h_), generator=g, device=dev) * 0.02
+        block.set_weights(layer, gate=gate.data_ptr(), up=up.data_ptr(), down=down.data_ptr(),
+                          router=router.data_ptr(), qtype=qt)
+        if args.config == 3:  # the Zipf(1.1) expert skew: bias_e = -1.1 ln(rank_e), ranks a seeded permutation
+            rank = torch.randperm(e_, generator=g, device=dev).float() + 1.0
+            block.set_router_bias(layer, (-1.1 * torch.log(rank)).cpu().numpy().astype(np.float32))
+        del gate, up, down, router
+    torch.cuda.empty_cache()
+    peaks, src = measured_peaks()
+    stream = torch.cuda.Stream(device=dev)
+    for name, T in shapes:
+        x = torch.randn((T, h_), generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty((T, h_), dtype=torch.bfloat16, device=dev)
+
+        def step():
+            for layer in range(L):
+                block.forward_ptr(x.data_ptr(), y.data_ptr(), T, layer=layer, stream=stream.cuda_stream)
+
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_layer = e0.elapsed_time(e1) / (args.steps * L)
+        stages = np.array([block.stage_times(layer) for layer in range(L)])
+        path = block.path(0)
+        line = {"workload": name, "tokens": T, "hidden": h_, "experts": e_, "top_k": k_, "expert_ffn": f_, "qtype": qt,
+                "ms_per_layer": ms_layer, "tokens_per_s": T / (ms_layer / 1000.0), "path": path, "layers": L,
+                "steps": args.steps}
+        if path == "tc" and stages.shape[1] >= 3:
+            gu_ms = float(stages[:, 2].mean())
+            flops = 2.0 * T * k_ * h_ * (2 * f_)
+            peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+            line["roofline"] = {"kernel": "tc_expert_gemm gate/up (+ the gather)", "bound": "tensor",
+                                "achieved": flops / (gu_ms / 1000.0) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                                "frac": flops / (gu_ms / 1000.0) / 1e12 / peak, "ms_per_launch": gu_ms,
+                                "peak_source": f"{src} bf16_tflops_sustained"}
+            line["stage_ms_mean"] = dict(zip(["router", "route+dispatch", "gather+gate_up", "down", "combine"],
+                                             [float(v) for v in stages.mean(0)]))
+        print(json.dumps(line), flush=True)
+    block.close()
+
+
 def run_decode(args) -> None:
     """BASELINE config 2 on one GPU: decode batches B = 1, 4, 16, 64 of the Q4_K block (bf16 x), each forward a CUDA
     graph, over --layers layers in turn (their touched experts far exceed L2). One JSON line per B: tokens/s, and the
@@ -250,6 +351,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--decode", action="store_true", help="BASELINE config 2 (decode batches, Q4_K) instead")
+    ap.add_argument("--config", type=int, choices=[3, 5], help="BASELINE config 3 or 5 (one GPU) instead")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"], help="expert path of --decode")
     ap.add_argument("--batches", type=int, nargs="+", default=[1, 4, 16, 64], help="decode batches of --decode")
     args = ap.parse_args()
@@ -258,6 +360,12 @@ def main() -> None:
         return
     if args.decode:
         run_decode(args)
+        return
+    if args.config:
+        if args.layers == LAYERS:
+            args.layers = 4
+        os.environ["ARTLITE_MOE_TIMING"] = "1"
+        run_config(args)
         return
 
     os.environ["ARTLITE_MOE_TIMING"] = "1"  # per-stage CUDA events between the forward's kernels (no syncs)
@@ -307,14 +415,15 @@ def main() -> None:
         if world > 1:
             dist.barrier()
 
+    clocks = Clocks(local)
+    clocks.start()
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             step()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    clocks = Clocks(local)
-    clocks.start()
+    t_host0 = time.time()
     launches0 = _lib.lib().artlite_moe_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -322,6 +431,7 @@ def main() -> None:
         step()
     e1.record(stream)
     torch.cuda.synchronize()
+    t_host1 = time.time()
     launches = _lib.lib().artlite_moe_launch_count() - launches0
     barrier()
     torch.cuda.synchronize()
@@ -329,7 +439,7 @@ def main() -> None:
     # per-stage times of every layer's forward in the last timed step (events on the forward's stream)
     stages = np.array([block.stage_times(layer) for layer in range(L)])
     path = block.path(0)
-    clk = clocks.stop()
+    clk = clocks.stop(t_host0, t_host1)
     t_max = torch.tensor([ms_total], device=dev)
     if world > 1:
         dist.all_reduce(t_max, op=dist.ReduceOp.MAX)

@@ -101,6 +101,15 @@ def test_tcgen05_full_shape(qtype):
     assert moe_np.rel_max(y[tok], oracle_y(layer, x, ids, w, tokens=tok)) <= BF16_TOL
 
 
+@pytest.mark.parametrize("path", ["tc", "gemv"])
+def test_large_expert_shape(path):
+    """Config 5's expert shape (H=4096, F=1536, Q4_0) at E=8, K=2, T=64, on both paths."""
+    layer, x, _ = moe_np.make_block(50, 64, qtype="Q4_0", E=8, H=4096, F=1536)
+    y, dbg = run(layer, x, act="bf16", path=path, T=64, k=2)
+    ids, w = check_routing(dbg, x, layer, 2)
+    assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= BF16_TOL
+
+
 def test_prefill_zipf_q8():
     """Config 3 (T=4096, Q8_0, Zipf(1.1)-skewed routing, bf16): the dispatch in full, outputs on 32 tokens."""
     T = 4096
