@@ -78,7 +78,7 @@ int launch_dequant_rows(int qtype, const uint8_t* raw, int64_t n, int64_t row_by
 // logits (T x E fp32) = x (T x H, f32 or bf16) . W_r^T (E x H, f32 or bf16) (+ bias (E), if not null)
 int launch_router(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H, int E,
                   float* logits, cudaStream_t st);
-// the same for decode-sized batches (T <= kRouterSmallTokens, H % 4 == 0), spread over (E / 2) x (T / 16) CTAs
+// the same for decode-sized batches (T <= kRouterSmallTokens, H % 4 == 0): a warp per (token, expert) over the grid
 constexpr int kRouterSmallTokens = 256;
 bool router_small_ok(int64_t T, int H);
 int launch_router_small(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H,

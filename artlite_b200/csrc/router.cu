@@ -5,6 +5,8 @@
 // per CTA, K in steps of 32 staged in shared memory (transposed, padded), 4 x 4 outputs per thread.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -63,12 +65,10 @@ __global__ void __launch_bounds__(256) router_kernel(const void* x, int x_dtype,
 
 // ---------------------------------------------------------------- decode-sized batches
 //
-// Two experts per CTA, each expert's row split over four warps in 128-column stripes (each lane: 4 consecutive columns
-// per stripe, 16-byte loads of W and x straight from global memory), 16 tokens per CTA; per warp a reduce-scatter of
-// the 16 token sums across its lanes, then the four stripes' partial sums meet in shared memory. Grid (E / 2, T / 16):
-// every W row is read once per 16 tokens by many CTAs at once, where the tiled kernels give one CTA to a small batch.
-constexpr int kRsTok = 16;
-
+// A warp per (token, expert) logit over the whole grid: each lane reads 4 consecutive columns of the W row and of the
+// token row per 128-column stripe with 16-byte loads (all of a 1024-column chunk's loads in flight at once), fp32 FMAs,
+// a warp reduction in fixed order, + bias. Where the tiled kernels give one CTA to a small batch, this spreads the
+// E x H weight read over every SM.
 namespace {
 __device__ __forceinline__ void load4(const void* p, int dtype, int64_t i, float (&v)[4]) {
   if (dtype == ARTLITE_BF16) {
@@ -84,56 +84,36 @@ __device__ __forceinline__ void load4(const void* p, int dtype, int64_t i, float
 
 __global__ void __launch_bounds__(256) router_small_kernel(const void* x, int x_dtype, const void* w, int w_dtype,
                                                            const float* bias, int64_t T, int H, int E, float* logits) {
-  __shared__ float red[8][kRsTok];
   griddep_wait();
   griddep_launch();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * 2 + (warp >> 2), part = warp & 3;
-  const int64_t t0 = (int64_t)blockIdx.y * kRsTok;
-  const int nt = (int)min64(kRsTok, T - t0);
-  float acc[kRsTok];
+  const int lane = threadIdx.x & 31;
+  const int64_t units = T * E;
+  for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < units;
+       u += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t t = u / E;
+    const int e = (int)(u - t * E);
+    float acc = 0.0f;
+    for (int c0 = 0; c0 < H; c0 += 1024) {
+      float wv[8][4], xv[8][4];
 #pragma unroll
-  for (int n = 0; n < kRsTok; n++) acc[n] = 0.0f;
-  if (e < E) {
-#pragma unroll 4
-    for (int c = part * 128 + lane * 4; c < H; c += 512) {
-      float wv[4];
-      load4(w, w_dtype, (int64_t)e * H + c, wv);
+      for (int i = 0; i < 8; i++) {
+        const int c = c0 + 4 * lane + 128 * i;
+        if (c < H) {
+          load4(w, w_dtype, (int64_t)e * H + c, wv[i]);
+          load4(x, x_dtype, t * H + c, xv[i]);
+        } else {
 #pragma unroll
-      for (int n = 0; n < kRsTok; n++) {
-        if (n < nt) {
-          float xv[4];
-          load4(x, x_dtype, (t0 + n) * H + c, xv);
-          acc[n] = fmaf(wv[0], xv[0], acc[n]);
-          acc[n] = fmaf(wv[1], xv[1], acc[n]);
-          acc[n] = fmaf(wv[2], xv[2], acc[n]);
-          acc[n] = fmaf(wv[3], xv[3], acc[n]);
+          for (int j = 0; j < 4; j++) wv[i][j] = xv[i][j] = 0.0f;
         }
       }
-    }
-  }
-  // reduce-scatter over the lanes: afterwards lanes 2j and 2j + 1 hold token j's sum
 #pragma unroll
-  for (int h = 8, o = 16; h >= 1; h >>= 1, o >>= 1) {
-    const bool up = lane & o;
+      for (int i = 0; i < 8; i++)
 #pragma unroll
-    for (int j = 0; j < h; j++) {
-      const float send = up ? acc[j] : acc[j + h];
-      const float keep = up ? acc[j + h] : acc[j];
-      acc[j] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
+        for (int j = 0; j < 4; j++) acc = fmaf(wv[i][j], xv[i][j], acc);
     }
-  }
-  acc[0] += __shfl_xor_sync(0xFFFFFFFFu, acc[0], 1);
-  if (!(lane & 1)) red[warp][lane >> 1] = acc[0];
-  __syncthreads();
-  if (threadIdx.x < 2 * kRsTok) {
-    const int ex = blockIdx.x * 2 + (threadIdx.x >> 4), n = threadIdx.x & 15;
-    const int wb = (threadIdx.x >> 4) * 4;
-    if (ex < E && n < nt) {
-      float v = (red[wb][n] + red[wb + 1][n]) + (red[wb + 2][n] + red[wb + 3][n]);
-      if (bias) v += bias[ex];
-      logits[(t0 + n) * E + ex] = v;
-    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+    if (lane == 0) logits[t * E + e] = bias ? acc + bias[e] : acc;
   }
 }
 
@@ -143,8 +123,9 @@ int launch_router_small(const void* x, int x_dtype, const void* w, int w_dtype, 
                         int E, float* logits, cudaStream_t st) {
   AL_CHECK(router_small_ok(T, H), ARTLITE_EINVAL, "router_small: T %lld H %d", (long long)T, H);
   if (T == 0) return ARTLITE_OK;
-  return launch_pdl(router_small_kernel, dim3((unsigned)cdiv(E, 2), (unsigned)cdiv(T, kRsTok)), dim3(256), 0, st, x,
-                    x_dtype, w, w_dtype, bias, T, H, E, logits);
+  const int64_t warps = T * E;
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(warps, 8), (int64_t)kNumSMs * 8);
+  return launch_pdl(router_small_kernel, dim3(grid), dim3(256), 0, st, x, x_dtype, w, w_dtype, bias, T, H, E, logits);
 }
 
 int launch_router(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H, int E,

@@ -256,22 +256,26 @@ def run_config(args) -> None:
             for layer in range(L):
                 block.forward_ptr(x.data_ptr(), y.data_ptr(), T, layer=layer, stream=stream.cuda_stream)
 
+        clocks = Clocks(0)
+        clocks.start()
         with torch.cuda.stream(stream):
             for _ in range(args.warmup):
                 step()
         torch.cuda.synchronize()
+        t_host0 = time.time()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
             step()
         e1.record(stream)
         torch.cuda.synchronize()
+        clk = clocks.stop(t_host0, time.time())
         ms_layer = e0.elapsed_time(e1) / (args.steps * L)
         stages = np.array([block.stage_times(layer) for layer in range(L)])
         path = block.path(0)
         line = {"workload": name, "tokens": T, "hidden": h_, "experts": e_, "top_k": k_, "expert_ffn": f_, "qtype": qt,
                 "ms_per_layer": ms_layer, "tokens_per_s": T / (ms_layer / 1000.0), "path": path, "layers": L,
-                "steps": args.steps}
+                "steps": args.steps, "clocks": clk}
         if path == "tc" and stages.shape[1] >= 3:
             gu_ms = float(stages[:, 2].mean())
             flops = 2.0 * T * k_ * h_ * (2 * f_)
@@ -315,11 +319,14 @@ def run_decode(args) -> None:
             block.forward_ptr(x.data_ptr(), y.data_ptr(), B, layer=layer, stream=stream.cuda_stream)
             block.sync()
             touched.append(len(np.unique(block.debug(B)["ids"])))
+        clocks = Clocks(0)
+        clocks.start()
         with torch.cuda.stream(stream):
             for _ in range(args.warmup):
                 for layer in range(L):
                     block.forward_graph(x.data_ptr(), y.data_ptr(), B, layer=layer, stream=stream.cuda_stream)
         torch.cuda.synchronize()
+        t_host0 = time.time()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
@@ -327,6 +334,7 @@ def run_decode(args) -> None:
                 block.forward_graph(x.data_ptr(), y.data_ptr(), B, layer=layer, stream=stream.cuda_stream)
         e1.record(stream)
         torch.cuda.synchronize()
+        clk = clocks.stop(t_host0, time.time())
         ms_layer = e0.elapsed_time(e1) / (args.steps * L)
         U = float(np.mean(touched))
         nbytes = U * 2654208 + E * H * 4
@@ -335,7 +343,7 @@ def run_decode(args) -> None:
                           "tokens_per_s": B / (ms_layer / 1000.0), "experts_touched": U,
                           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                        "frac": gbs / peaks["hbm_gbs"], "peak_source": src, "bytes_per_layer": nbytes},
-                          "path": block.path(0), "layers": L, "steps": args.steps}), flush=True)
+                          "path": block.path(0), "layers": L, "steps": args.steps, "clocks": clk}), flush=True)
     block.close()
 
 
