@@ -142,13 +142,13 @@ void small_plan(const artlite_moe& h, const artlite_moe::Layer& L, int path, int
   *mult_dn = (int)cdiv(d.hidden, rt_dn);
 }
 
-int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const void* x, int x_dtype, bool gathered,
+int run_experts(artlite_moe* h, const ExpertWeights& L, int path, const void* x, int x_dtype, bool gathered,
                 const int32_t* perm, int k, int64_t P, int E_run, const int64_t* offsets, const int32_t* counts,
                 int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk, bool units_ready,
-                const int32_t* wexp, int E_w) {
+                const int32_t* wexp, int E_w, int F_run, void* y_out) {
   const artlite_moe_desc& d = h->d;
-  const int H = d.hidden, F = d.expert_ffn;
-  *y_rows = h->y.ptr;
+  const int H = d.hidden, F = F_run > 0 ? F_run : d.expert_ffn;
+  *y_rows = y_out ? y_out : h->y.ptr;
   if (path == 1) {
     *y_dtype = ARTLITE_F32;
     if (P == 0) return ARTLITE_OK;
@@ -160,8 +160,8 @@ int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const voi
     }
     ExpertGemvArgs g{};
     g.qtype = L.qtype;
-    g.w0 = L.gate.as<uint8_t>();
-    g.w1 = L.up.as<uint8_t>();
+    g.w0 = L.gate;
+    g.w1 = L.up;
     g.row_bytes = L.rb_gu;
     g.K = H;
     g.N = F;
@@ -179,7 +179,7 @@ int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const voi
     AL_TRY(mk.mark());
     ExpertGemvArgs dn = g;
     dn.qtype = L.down_qtype;
-    dn.w0 = L.down.as<uint8_t>();
+    dn.w0 = L.down;
     dn.w1 = nullptr;
     dn.row_bytes = L.rb_dn;
     dn.K = F;
@@ -188,7 +188,7 @@ int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const voi
     dn.x_dtype = ARTLITE_F32;
     dn.unit_off = h->unit_dn.as<int32_t>();
     dn.rt = rt_dn;
-    dn.out = h->y.as<float>();
+    dn.out = static_cast<float*>(*y_rows);
     AL_TRY(launch_gemv_down(dn, st));
     return mk.mark();
   }
@@ -202,8 +202,8 @@ int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const voi
   }
   TcGemmArgs g{};
   g.qtype = L.qtype;
-  g.w0 = L.gate.as<uint8_t>();
-  g.w1 = L.up.as<uint8_t>();
+  g.w0 = L.gate;
+  g.w1 = L.up;
   g.row_bytes = L.rb_gu;
   g.K = H;
   g.N = F;
@@ -222,16 +222,45 @@ int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const voi
   AL_TRY(mk.mark());
   TcGemmArgs dn = g;
   dn.qtype = L.down_qtype;
-  dn.w0 = L.down.as<uint8_t>();
+  dn.w0 = L.down;
   dn.w1 = nullptr;
   dn.row_bytes = L.rb_dn;
   dn.K = F;
   dn.N = H;
   dn.x = h->h.as<uint16_t>();
   dn.x_rows = (int64_t)(h->h.bytes / (sizeof(uint16_t) * F));
-  dn.out = h->y.as<uint16_t>();
+  dn.out = static_cast<uint16_t*>(*y_rows);
   AL_TRY(launch_tc_gemm(dn, /*gu=*/false, st));
   return mk.mark();
+}
+
+// the layer's shared expert on all T tokens (one row group, token order) and its gates, for the combine
+// the captured forwards name the weights' and workspaces' addresses: new weights (which may move them) drop them
+void drop_graphs(artlite_moe* h) {
+  for (const artlite_moe::Graph& g : h->graphs) cudaGraphExecDestroy(g.exec);
+  h->graphs.clear();
+}
+
+int run_shared(artlite_moe* h, const artlite_moe::Layer& L, const void* xd, int64_t T, cudaStream_t st,
+               CombineShared* sh) {
+  const artlite_moe_desc& d = h->d;
+  const int H = d.hidden, F = L.sh_F;
+  AL_TRY(launch_shared_gate(xd, d.act_dtype, L.sh_has_gate ? L.sh_ginp.ptr : nullptr, L.sh_gate_dtype, T, H,
+                            h->sh_s.as<float>(), h->sh_off.as<int64_t>(), st));
+  const ExpertWeights W = shared_weights(L);
+  const bool tc = T >= 64 && tc_supported(W.qtype, H, F) && tc_supported(W.down_qtype, F, H);
+  int64_t* off = h->sh_off.as<int64_t>();  // (written by the gate kernel: {0, T} and the count T)
+  int32_t* cnt = reinterpret_cast<int32_t*>(off + 2);
+  Marker quiet{h, 0, st};
+  quiet.ns = kStages;
+  void* yrows;
+  int ydt;
+  AL_TRY(run_experts(h, W, tc ? 2 : 1, xd, d.act_dtype, false, h->sh_iota.as<int32_t>(), 1, T, 1, off, cnt, 0, &yrows,
+                     &ydt, st, quiet, false, nullptr, 0, F, h->sh_y.ptr));
+  sh->y = yrows;
+  sh->y_dtype = ydt;
+  sh->s = h->sh_s.as<float>();
+  return ARTLITE_OK;
 }
 
 }  // namespace artlite
@@ -303,6 +332,7 @@ int artlite_moe_create(const artlite_moe_desc* desc, artlite_moe** out) {
 int artlite_moe_set_weights(artlite_moe* h, int layer, int qtype, const void* gate, const void* up, int down_qtype,
                             const void* down, const void* router, int router_qtype) {
   AL_CHECK(h, ARTLITE_EINVAL, "moe_set_weights: null handle");
+  drop_graphs(h);
   AL_CHECK(layer >= 0 && layer < (int)h->layers.size(), ARTLITE_EINVAL, "moe_set_weights: layer %d of %d", layer,
            (int)h->layers.size());
   AL_CHECK(gate && up && down && router, ARTLITE_EINVAL, "moe_set_weights: null tensor");
@@ -395,9 +425,12 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
       AL_TRY(route_and_dispatch(h, L, xd, T, st, mk, mult_gu, mult_dn));
       void* yrows;
       int ydt;
-      AL_TRY(run_experts(h, L, path, xd, d.act_dtype, false, h->perm.as<int32_t>(), K, P, E, h->offsets.as<int64_t>(),
-                         h->counts.as<int32_t>(), 0, &yrows, &ydt, st, mk, mult_gu > 0));
-      AL_TRY(launch_combine(yrows, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st));
+      AL_TRY(run_experts(h, routed_weights(L), path, xd, d.act_dtype, false, h->perm.as<int32_t>(), K, P, E,
+                         h->offsets.as<int64_t>(), h->counts.as<int32_t>(), 0, &yrows, &ydt, st, mk, mult_gu > 0));
+      CombineShared sh;
+      if (L.has_shared) AL_TRY(run_shared(h, L, xd, T, st, &sh));
+      AL_TRY(launch_combine(yrows, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st,
+                            CombineOwn{}, sh));
     }
   }
   AL_TRY(mk.mark());
@@ -418,6 +451,7 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
 
 int artlite_moe_set_router_bias(artlite_moe* h, int layer, const float* bias) {
   AL_CHECK(h, ARTLITE_EINVAL, "moe_set_router_bias: null handle");
+  drop_graphs(h);
   AL_CHECK(layer >= 0 && layer < (int)h->layers.size(), ARTLITE_EINVAL, "moe_set_router_bias: layer %d of %d", layer,
            (int)h->layers.size());
   AL_CUDA(cudaSetDevice(h->dev));
@@ -429,6 +463,67 @@ int artlite_moe_set_router_bias(artlite_moe* h, int layer, const float* bias) {
   AL_TRY(L.bias.reserve(sizeof(float) * h->d.n_experts));
   AL_CUDA(cudaMemcpyAsync(L.bias.ptr, bias, sizeof(float) * h->d.n_experts, cudaMemcpyDefault, h->st));
   L.has_bias = true;
+  return wait(h->st, 0);
+}
+
+int artlite_moe_set_shared(artlite_moe* h, int layer, int ffn, int qtype, const void* gate, const void* up,
+                           int down_qtype, const void* down, const void* gate_inp, int gate_dtype) {
+  AL_CHECK(h, ARTLITE_EINVAL, "moe_set_shared: null handle");
+  drop_graphs(h);
+  AL_CHECK(layer >= 0 && layer < (int)h->layers.size(), ARTLITE_EINVAL, "moe_set_shared: layer %d of %d", layer,
+           (int)h->layers.size());
+  AL_CUDA(cudaSetDevice(h->dev));
+  artlite_moe::Layer& L = h->layers[layer];
+  if (!gate) {
+    L.has_shared = false;
+    return ARTLITE_OK;
+  }
+  AL_CHECK(h->E_local == h->d.n_experts, ARTLITE_EUNSUPPORTED, "moe_set_shared: not with expert parallelism");
+  AL_CHECK(up && down && ffn > 0, ARTLITE_EINVAL, "moe_set_shared: null up / down or ffn %d", ffn);
+  AL_CHECK(!gate_inp || gate_dtype == ARTLITE_F32 || gate_dtype == ARTLITE_BF16, ARTLITE_EINVAL,
+           "moe_set_shared: gate type %d (F32 or BF16)", gate_dtype);
+  int per, bytes, per_d, bytes_d;
+  AL_TRY(qtype_block(qtype, &per, &bytes));
+  AL_TRY(qtype_block(down_qtype, &per_d, &bytes_d));
+  const artlite_moe_desc& d = h->d;
+  const int64_t H = d.hidden, F = ffn, T = d.max_tokens > 0 ? d.max_tokens : 1;
+  AL_CHECK(H % per == 0 && F % per_d == 0, ARTLITE_EINVAL, "moe_set_shared: H %lld / ffn %lld and blocks of %d / %d",
+           (long long)H, (long long)F, per, per_d);
+  L.sh_F = ffn;
+  L.sh_qtype = qtype;
+  L.sh_down_qtype = down_qtype;
+  L.sh_rb_gu = H / per * bytes;
+  L.sh_rb_dn = F / per_d * bytes_d;
+  const size_t gu_bytes = (size_t)(F * L.sh_rb_gu), dn_bytes = (size_t)(H * L.sh_rb_dn);
+  AL_TRY(L.sh_gate.reserve(gu_bytes + 64));
+  AL_TRY(L.sh_up.reserve(gu_bytes + 64));
+  AL_TRY(L.sh_down.reserve(dn_bytes + 64));
+  AL_CUDA(cudaMemcpyAsync(L.sh_gate.ptr, gate, gu_bytes, cudaMemcpyDefault, h->st));
+  AL_CUDA(cudaMemcpyAsync(L.sh_up.ptr, up, gu_bytes, cudaMemcpyDefault, h->st));
+  AL_CUDA(cudaMemcpyAsync(L.sh_down.ptr, down, dn_bytes, cudaMemcpyDefault, h->st));
+  AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.sh_gate.ptr) + gu_bytes, 0, 64, h->st));
+  AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.sh_up.ptr) + gu_bytes, 0, 64, h->st));
+  AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.sh_down.ptr) + dn_bytes, 0, 64, h->st));
+  L.sh_has_gate = gate_inp != nullptr;
+  if (gate_inp) {
+    const size_t gb = (size_t)H * (gate_dtype == ARTLITE_F32 ? 4 : 2);
+    AL_TRY(L.sh_ginp.reserve(gb));
+    AL_CUDA(cudaMemcpyAsync(L.sh_ginp.ptr, gate_inp, gb, cudaMemcpyDefault, h->st));
+    L.sh_gate_dtype = gate_dtype;
+  }
+  // the shared run's workspaces: all T tokens as one row group (rows 0 .. T - 1 in token order)
+  AL_TRY(h->sh_y.reserve(sizeof(float) * T * H));
+  AL_TRY(h->sh_s.reserve(sizeof(float) * T));
+  AL_TRY(h->sh_off.reserve(sizeof(int64_t) * 2 + sizeof(int32_t)));
+  AL_TRY(h->h.reserve(std::max(h->h.bytes, std::max(sizeof(float) * T * F, sizeof(uint16_t) * (T + 256) * F))));
+  if (h->sh_iota.bytes < sizeof(int32_t) * T) {
+    AL_TRY(h->sh_iota.reserve(sizeof(int32_t) * T));
+    std::vector<int32_t> io(T);
+    for (int64_t i = 0; i < T; i++) io[i] = (int32_t)i;
+    AL_CUDA(cudaMemcpyAsync(h->sh_iota.ptr, io.data(), sizeof(int32_t) * T, cudaMemcpyHostToDevice, h->st));
+    AL_TRY(wait(h->st, 0));
+  }
+  L.has_shared = true;
   return wait(h->st, 0);
 }
 

@@ -24,12 +24,18 @@ struct artlite_moe {
     // one 144-byte super-block wide)
     bool has_dm = false;
     CUtensorMap dm_gate, dm_up, dm_down;
+    // the shared expert (artlite_moe_set_shared): raw rows of one SwiGLU expert of width sh_F, and its gate vector
+    bool has_shared = false, sh_has_gate = false;
+    int sh_F = 0, sh_qtype = -1, sh_down_qtype = -1, sh_gate_dtype = -1;
+    int64_t sh_rb_gu = 0, sh_rb_dn = 0;
+    artlite::DevBuf sh_gate, sh_up, sh_down, sh_ginp;
   };
   std::vector<Layer> layers;
   // workspaces
   artlite::DevBuf xin, yout, logits, ids, w, offsets, perm, slot, counts, blk, unit_gu, unit_dn, status;
   artlite::DevBuf h, y, xp, tiles;
   artlite::DevBuf bar;  // the fused decode kernel's grid barrier (zeroed once; left zeroed by every complete run)
+  artlite::DevBuf sh_y, sh_s, sh_iota, sh_off;  // the shared expert's outputs (T rows), gates (T), 0..T-1, {0, T} / {T}
   int64_t last_T = 0;
   int last_path = 0;
   bool timing = false;
@@ -84,6 +90,20 @@ struct Marker {
   }
 };
 
+// the raw rows one run of the expert GEMMs reads: the routed experts of a layer, or its shared expert
+struct ExpertWeights {
+  int qtype, down_qtype;
+  const uint8_t *gate, *up, *down;
+  int64_t rb_gu, rb_dn;
+};
+inline ExpertWeights routed_weights(const artlite_moe::Layer& L) {
+  return {L.qtype, L.down_qtype, L.gate.as<uint8_t>(), L.up.as<uint8_t>(), L.down.as<uint8_t>(), L.rb_gu, L.rb_dn};
+}
+inline ExpertWeights shared_weights(const artlite_moe::Layer& L) {
+  return {L.sh_qtype, L.sh_down_qtype, L.sh_gate.as<uint8_t>(), L.sh_up.as<uint8_t>(), L.sh_down.as<uint8_t>(),
+          L.sh_rb_gu, L.sh_rb_dn};
+}
+
 // router logits, routing and the dispatch over all E experts of T tokens x (device, act dtype) into the handle's
 // logits / ids / w / offsets / perm / slot / counts
 // mult_gu > 0: the decode-sized path (the small router when it applies, routing and dispatch in one kernel, which also
@@ -91,16 +111,20 @@ struct Marker {
 int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* x, int64_t T, cudaStream_t st,
                        Marker& mk, int mult_gu = 0, int mult_dn = 0);
 
+// F_run (0: the block's expert_ffn) the experts' width; y_out (null: the handle's y buffer) where the output rows go.
 // wexp (device, may be null): the weight expert of each of the E_run row groups (expert parallelism: a group is one
 // source rank's rows of one local expert), E_w the experts the weights hold (0: E_run).
 // The experts of a forward over P rows for E_run experts (offsets / counts on the device): rows are the tokens x
 // through perm / k (gathered = false), or already gathered bf16 rows in expert order (gathered = true, perm = the
 // identity, k = 1). Output rows in the same order into *y_rows (the handle's y buffer), fp32 (GEMV path) or bf16
 // (tcgen05 path) in *y_dtype.
-int run_experts(artlite_moe* h, const artlite_moe::Layer& L, int path, const void* x, int x_dtype, bool gathered,
+int run_experts(artlite_moe* h, const ExpertWeights& W, int path, const void* x, int x_dtype, bool gathered,
                 const int32_t* perm, int k, int64_t P, int E_run, const int64_t* offsets, const int32_t* counts,
                 int64_t x_rows, void** y_rows, int* y_dtype, cudaStream_t st, Marker& mk, bool units_ready = false,
-                const int32_t* wexp = nullptr, int E_w = 0);
+                const int32_t* wexp = nullptr, int E_w = 0, int F_run = 0, void* y_out = nullptr);
+
+// destroys the captured forwards (their addresses may be stale after new weights)
+void drop_graphs(artlite_moe* h);
 
 // which expert path a forward of P pairs takes
 int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L);

@@ -48,7 +48,8 @@ __device__ __forceinline__ void store8(void* base, int dtype, int64_t i, const f
 
 // one CTA per token row, 8 values per thread (H % 8 == 0)
 __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype, const int32_t* slot, const float* w,
-                                                      int64_t T, int k, int H, void* out, int out_dtype, CombineOwn own) {
+                                                      int64_t T, int k, int H, void* out, int out_dtype, CombineOwn own,
+                                                      CombineShared sh) {
   griddep_wait();
   griddep_launch();
   const int64_t t = blockIdx.x;
@@ -65,16 +66,23 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype
 #pragma unroll
       for (int j = 0; j < 8; j++) acc[j] = fmaf(wi, v[j], acc[j]);
     }
+    if (sh.y) {  // the shared expert's gated term, last in the sum
+      const float si = sh.s[t];
+      float v[8];
+      load8(sh.y, sh.y_dtype, t * H + c, v);
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] = fmaf(si, v[j], acc[j]);
+    }
     store8(out, out_dtype, t * H + c, acc);
   }
 }
 
 int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float* w, int64_t T, int k, int H, void* out,
-                   int out_dtype, cudaStream_t st, CombineOwn own) {
+                   int out_dtype, cudaStream_t st, CombineOwn own, CombineShared sh) {
   AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "combine: H %d (a multiple of 8)", H);
   if (T == 0) return ARTLITE_OK;
   return launch_pdl(combine_kernel, dim3((unsigned)T), dim3(256), 0, st, y, y_dtype, slot, w, T, k, H, out, out_dtype,
-                    own);
+                    own, sh);
 }
 
 // a grid-stride loop over 16-byte chunks of the output rows (8 values each): row i of xp = token perm[i] / k of x
@@ -108,6 +116,43 @@ int launch_gather(const void* x, int x_dtype, const int32_t* perm, int64_t P, in
   gather_kernel<<<grid, 256, 0, st>>>(x, x_dtype, perm, P, k, H, xp, own_dst, own_lo, own_hi);
   AL_LAUNCHED();
   return ARTLITE_OK;
+}
+
+// a warp per token: s[t] = sigmoid(x_t . g), fp32 products and a fixed-order fp32 sum (ref.shared_expert's
+// sigmoid(x @ gate_inp), tests/moe/ref.py:55-60, np_ops.sigmoid = 1 / (1 + exp(-z)))
+__global__ void __launch_bounds__(256) shared_gate_kernel(const void* x, int x_dtype, const void* g, int g_dtype,
+                                                          int64_t T, int H, float* s, int64_t* off) {
+  griddep_wait();
+  griddep_launch();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    off[0] = 0;
+    off[1] = T;
+    reinterpret_cast<int32_t*>(off + 2)[0] = (int32_t)T;
+  }
+  const int lane = threadIdx.x & 31;
+  const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t >= T) return;
+  float acc = 0.0f;
+  if (g) {
+    for (int c = lane * 8; c < H; c += 256) {
+      float a[8], b[8];
+      load8(x, x_dtype, t * H + c, a);
+      load8(g, g_dtype, c, b);
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc = fmaf(a[j], b[j], acc);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+  }
+  if (lane == 0) s[t] = g ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-acc))) : 1.0f;
+}
+
+int launch_shared_gate(const void* x, int x_dtype, const void* g, int g_dtype, int64_t T, int H, float* s,
+                       int64_t* off, cudaStream_t st) {
+  AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "shared gate: H %d (a multiple of 8)", H);
+  if (T == 0) return ARTLITE_OK;
+  return launch_pdl(shared_gate_kernel, dim3((unsigned)cdiv(T, 8)), dim3(256), 0, st, x, x_dtype, g, g_dtype, T, H, s,
+                    off);
 }
 
 }  // namespace artlite

@@ -1,6 +1,6 @@
-// The fused decode-batch forward: one cooperative kernel per layer for small batches on the GEMV path (T k <= 512
-// pairs, E <= 256, Q4_0 / Q8_0 / Q4_K weights, the same type for gate / up / down). It runs the same steps as the separate kernels of a forward, in phases
-// separated by grid barriers:
+// The fused decode-batch forward: one cooperative kernel per layer for small batches on the GEMV path (8 <= T,
+// T k <= 512 pairs, E <= 256, Q4_0 / Q8_0 / Q4_K weights, one type for gate / up / down, no shared expert). It runs
+// the same steps as the separate kernels of a forward, in phases separated by grid barriers:
 //   1. router logits (router.cu's semantics: fp32 products, fp32 sums, + bias): a warp per (token, expert), W and x
 //      rows read with 16-byte loads (1024 columns at a time); for Q4_K also the tokens' x in the streaming GEMV's
 //      fragment order (ms.cuh);
@@ -368,7 +368,7 @@ bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t 
   }();
   const artlite_moe_desc& d = h.d;
   // (below 8 tokens the separate kernels, whose GEMV spreads finer items over the whole grid, are faster)
-  return !off && T >= 8 && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts && h.E_local == d.n_experts &&
+  return !off && !L.has_shared && T >= 8 && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts && h.E_local == d.n_experts &&
          rq_type(L.qtype) && L.down_qtype == L.qtype && d.hidden % 256 == 0 && d.expert_ffn % 256 == 0 &&
          gemv_rq_rows_per_warp(L.qtype, d.hidden, true) > 0 && gemv_rq_rows_per_warp(L.down_qtype, d.expert_ffn, false) > 0 &&
          (L.qtype != ARTLITE_Q4_K || (d.act_dtype == ARTLITE_BF16 && L.has_dm)) &&

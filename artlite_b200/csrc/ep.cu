@@ -330,8 +330,8 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   Marker quiet{h, layer, st};
   quiet.ns = kStages;  // (no stage events inside the expert calls)
   const int jo = (W - 1) * El;
-  AL_TRY(run_experts(h, L, path, xr, ARTLITE_BF16, true, ident, 1, recv_rows[r], El, goff + jo, gcnt + jo, xr_rows,
-                     &yrows, &ydt, st, quiet, false, gexp + jo, El));
+  AL_TRY(run_experts(h, routed_weights(L), path, xr, ARTLITE_BF16, true, ident, 1, recv_rows[r], El, goff + jo,
+                     gcnt + jo, xr_rows, &yrows, &ydt, st, quiet, false, gexp + jo, El));
   AL_TRY(mk.mark());
   const int Gc = (W - 1) * Ec;  // groups a chunk
   for (int c = 0; c < C; c++) {
@@ -340,8 +340,8 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
     for (int q = 0; q < W; q++)
       if (q != r) rows += h->ep_cr_rows[(size_t)q * C + c];
     if (Gc)
-      AL_TRY(run_experts(h, L, path, xr, ARTLITE_BF16, true, ident, 1, rows, Gc, goff + c * Gc, gcnt + c * Gc, xr_rows,
-                         &yrows, &ydt, st, quiet, false, gexp + c * Gc, El));
+      AL_TRY(run_experts(h, routed_weights(L), path, xr, ARTLITE_BF16, true, ident, 1, rows, Gc, goff + c * Gc,
+                         gcnt + c * Gc, xr_rows, &yrows, &ydt, st, quiet, false, gexp + c * Gc, El));
     AL_CUDA(cudaEventRecord(ev_y[c], st));
   }
   AL_TRY(mk.mark());
@@ -356,8 +356,10 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
     for (int q = 0; q < W; q++) {
       if (q == r) continue;
       const size_t k = (size_t)q * C + c;
-      if (h->ep_cr_rows[k]) AL_NCCL(N->send(yo + h->ep_cr_pos[k] * H * el, (size_t)h->ep_cr_rows[k] * H, dt, q, comm, h->ep_st));
-      if (h->ep_cs_rows[k]) AL_NCCL(N->recv(ys + h->ep_cs_pos[k] * H * el, (size_t)h->ep_cs_rows[k] * H, dt, q, comm, h->ep_st));
+      if (h->ep_cr_rows[k])
+        AL_NCCL(N->send(yo + h->ep_cr_pos[k] * H * el, (size_t)h->ep_cr_rows[k] * H, dt, q, comm, h->ep_st));
+      if (h->ep_cs_rows[k])
+        AL_NCCL(N->recv(ys + h->ep_cs_pos[k] * H * el, (size_t)h->ep_cs_rows[k] * H, dt, q, comm, h->ep_st));
     }
     AL_NCCL(N->groupEnd());
   }

@@ -122,8 +122,18 @@ struct CombineOwn {
   const void* own = nullptr;
   int64_t own_lo = 0, own_hi = 0;
 };
+// the shared expert's term: out_t += s[t] y[t] in the same fp32 sum (y = null: none)
+struct CombineShared {
+  const void* y = nullptr;
+  int y_dtype = 0;
+  const float* s = nullptr;
+};
 int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float* w, int64_t T, int k, int H, void* out,
-                   int out_dtype, cudaStream_t st, CombineOwn own = CombineOwn{});
+                   int out_dtype, cudaStream_t st, CombineOwn own = CombineOwn{}, CombineShared sh = CombineShared{});
+// the shared expert's gates: s[t] = sigmoid(x_t . g) in fp32 (g: H values of g_dtype F32 / BF16; g = null: 1); also
+// its one row group: off = {0, T}, then the count T (int32) after them
+int launch_shared_gate(const void* x, int x_dtype, const void* g, int g_dtype, int64_t T, int H, float* s,
+                       int64_t* off, cudaStream_t st);
 
 // gather x rows into dispatch order: xp[i] = x[perm[i] / k] (bf16 out; x f32 or bf16); rows i in [own_lo, own_hi)
 // go to own_dst + (i - own_lo) rows instead (own_dst null: all to xp)

@@ -35,8 +35,10 @@ def ep_plan(send_counts: np.ndarray, recv_counts: np.ndarray, world: int, rank: 
     return send_off, recv_pos, local_off, local_counts
 
 
-def _ptr(a) -> int:
-    """A host array's address, or a device address given as an int / an object with ``data_ptr()``."""
+def _ptr(a) -> int | None:
+    """A host array's address, or a device address given as an int / an object with ``data_ptr()`` (None: NULL)."""
+    if a is None:
+        return None
     if isinstance(a, np.ndarray):
         return a.ctypes.data
     if isinstance(a, int):
@@ -83,6 +85,16 @@ class MoEBlock:
         check(lib().artlite_moe_set_weights(self._h, layer, QTYPES[qtype], _ptr(keep[0]), _ptr(keep[1]),
                                             QTYPES[down_qtype or qtype], _ptr(keep[2]), _ptr(keep[3]),
                                             QTYPES[router_qtype]))
+
+    def set_shared(self, layer: int, *, gate, up, down, ffn: int, qtype: str, down_qtype: str | None = None,
+                   gate_inp=None, gate_dtype: str = "F32") -> None:
+        """Layer ``layer``'s shared expert (ref.shared_expert): raw GGUF rows gate / up (ffn x hidden), down (hidden x
+        ffn) (blk.L.ffn_{gate,up,down}_shexp), and the optional gate vector (blk.L.ffn_gate_inp_shexp, hidden values of
+        ``gate_dtype``); numpy arrays or device pointers. ``gate=None`` removes it."""
+        keep = [np.ascontiguousarray(a) if isinstance(a, np.ndarray) else a for a in (gate, up, down, gate_inp)]
+        check(lib().artlite_moe_set_shared(self._h, layer, ffn, QTYPES[qtype], _ptr(keep[0]), _ptr(keep[1]),
+                                            QTYPES[down_qtype or qtype], _ptr(keep[2]), _ptr(keep[3]),
+                                            QTYPES[gate_dtype]))
 
     def set_router_bias(self, layer: int, bias: np.ndarray | None) -> None:
         """A per-expert bias added to the router logits (None: none)."""

@@ -146,6 +146,17 @@ int artlite_moe_set_weights(artlite_moe* h, int layer, int qtype, const void* ga
 int artlite_moe_set_router_bias(artlite_moe* h, int layer, const float* bias);
 
 /*
+ * Layer `layer`'s shared expert (the reference's ref.shared_expert, tests/moe/ref.py:55-60; llama.cpp's
+ * ffn_shexp_gated): raw GGUF rows gate / up = blk.L.ffn_{gate,up}_shexp.weight (ffn rows of H values, qtype), down =
+ * blk.L.ffn_down_shexp.weight (H rows of ffn values, down_qtype), and gate_inp = blk.L.ffn_gate_inp_shexp.weight (H
+ * values of gate_dtype ARTLITE_F32 / ARTLITE_BF16; NULL: no gate). The layer's output becomes the routed sum +
+ * sigmoid(gate_inp . x) swiglu(x), both in one fp32 sum rounded once. Host or device pointers; gate = NULL removes the
+ * shared expert. Not with expert parallelism (ep_world > 1): ARTLITE_EUNSUPPORTED.
+ */
+int artlite_moe_set_shared(artlite_moe* h, int layer, int ffn, int qtype, const void* gate, const void* up,
+                           int down_qtype, const void* down, const void* gate_inp, int gate_dtype);
+
+/*
  * y (T x H) = the block of layer `layer` on x (T x H), act_dtype both: router logits x W_r^T (fp32), routing,
  * dispatch, SwiGLU experts, weighted combine. Host or device x / y; `stream` a cudaStream_t (NULL: the handle's own).
  * With host pointers the call returns when y is back; with device pointers it returns after enqueueing (errors of

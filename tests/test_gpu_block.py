@@ -110,6 +110,35 @@ def test_large_expert_shape(path):
     assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= BF16_TOL
 
 
+@pytest.mark.parametrize("path,T,gated", [("tc", 200, True), ("gemv", 5, True), ("tc", 130, False)])
+def test_shared_expert(path, T, gated):
+    """The shared expert (ref.shared_expert, tests/moe/ref.py:55-60): the routed sum + sigmoid(x . g) swiglu_s(x),
+    in one fp32 sum; gated and ungated, both expert paths; and through a captured graph."""
+    import torch
+    H, Fs = 512, 256
+    layer, x, _ = moe_np.make_block(60, T, qtype="Q4_K", E=16, H=H, F=256)
+    rng = np.random.default_rng(61)
+    sg, su = moe_np.random_blocks(rng, "Q4_K", Fs, H), moe_np.random_blocks(rng, "Q4_K", Fs, H)
+    sd = moe_np.random_blocks(rng, "Q4_K", H, Fs)
+    g = (rng.standard_normal(H) * 0.05).astype(np.float32) if gated else None
+    b = make_block(layer, T, act="bf16", path=path)
+    b.set_shared(0, gate=sg, up=su, down=sd, ffn=Fs, qtype="Q4_K", gate_inp=g)
+    y_raw = b.forward(x)
+    dbg = b.debug(T)
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    yd = torch.empty_like(xd)
+    b.forward_graph(xd.data_ptr(), yd.data_ptr(), T)
+    b.sync()
+    y_graph = yd.cpu().numpy().view(np.uint16)
+    b.close()
+    assert np.array_equal(y_graph, y_raw)
+    ids, w = check_routing(dbg, x, layer, 8)
+    want = oracle_y(layer, x, ids, w) + moe_np.shared_expert(x_f32(x), moe_np.dequant("Q4_K", sg, H),
+                                                             moe_np.dequant("Q4_K", su, H),
+                                                             moe_np.dequant("Q4_K", sd, Fs), g)
+    assert moe_np.rel_max(moe_np.bf16_to_f32(y_raw), want) <= BF16_TOL
+
+
 def test_prefill_zipf_q8():
     """Config 3 (T=4096, Q8_0, Zipf(1.1)-skewed routing, bf16): the dispatch in full, outputs on 32 tokens."""
     T = 4096
