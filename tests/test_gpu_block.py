@@ -139,6 +139,15 @@ def test_shared_expert(path, T, gated):
     assert moe_np.rel_max(moe_np.bf16_to_f32(y_raw), want) <= BF16_TOL
 
 
+@pytest.mark.parametrize("path,T", [("tc", 300), ("gemv", 6), ("gemv", 24)])
+def test_flint_shape_sigmoid_top6(path, T):
+    """The reference's other MoE family's routing shape: E=256 experts, sigmoid gating, top-6, F=512 (Q4_K)."""
+    layer, x, _ = moe_np.make_block(70 + T, T, qtype="Q4_K", E=256, H=512, F=512)
+    y, dbg = run(layer, x, act="bf16", path=path, T=T, gating="sigmoid", k=6)
+    ids, w = check_routing(dbg, x, layer, 6, gating="sigmoid")
+    assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= BF16_TOL
+
+
 def test_prefill_zipf_q8():
     """Config 3 (T=4096, Q8_0, Zipf(1.1)-skewed routing, bf16): the dispatch in full, outputs on 32 tokens."""
     T = 4096
