@@ -9,9 +9,10 @@
 //   3. the token rows gathered (bf16): rows for peers into the send buffer at their dispatch positions, the rank's own
 //      rows straight into their place in the receive buffer;
 //   4. the rows exchanged with grouped ncclSend / ncclRecv, one message per peer, on a second stream, while
-//   5. the local experts run on the rank's own row groups; then on the peers' groups: the receive buffer's W x (E / W)
-//      (source, expert) row groups each run in place against their expert's weights (run_experts with a weight-expert
-//      map), no regrouping copy;
+//   5. the local experts run on the receive buffer's W x (E / W) (source, expert) row groups, each in place against its
+//      expert's weights (run_experts with a weight-expert map), no regrouping copy: at W = 2 the own groups first,
+//      while the rows travel, then the peer's; at W >= 4 (the own block a small share) one run over all groups once
+//      the rows are in; with ARTLITE_EP_CHUNKS > 1 the peers' groups in expert chunks, each run as its rows land;
 //   6. the outputs returned by one message per peer, each landing as the contiguous block of the source rank's dispatch
 //      order it came from; the rank's own block stays where its experts wrote it;
 //   7. the weighted combine of the rank's own tokens, its own rows read from the expert outputs (combine.cu).
@@ -19,6 +20,7 @@
 // system's), so the library itself has no link-time NCCL dependency. Waits on the host are bounded: a peer that never
 // sends makes the count exchange's wait run out, the communicator is aborted and the call returns ARTLITE_ETIMEOUT.
 // Nothing here uses TMA multicast or reads another GPU's memory from a kernel: every byte between GPUs moves by NCCL.
+#include <cstdlib>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
@@ -127,7 +129,13 @@ int ep_create(artlite_moe* h) {
   h->ep_recv_rows.assign(W, 0);
   AL_CUDA(cudaStreamCreateWithFlags(&h->ep_st, cudaStreamNonBlocking));
   for (cudaEvent_t& e : h->ep_ev) AL_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-  h->ep_chunks = El % 4 == 0 ? 4 : El % 2 == 0 ? 2 : 1;
+  // Expert chunks pipeline the exchanges with the peers' GEMMs, but each chunk is another pair of GEMM launches.
+  // ARTLITE_EP_CHUNKS (1, 2 or 4, a divisor of the local experts) sets the count; default 1.
+  h->ep_chunks = 1;
+  if (const char* ev = std::getenv("ARTLITE_EP_CHUNKS")) {
+    const int c = std::atoi(ev);
+    if ((c == 2 || c == 4) && c <= artlite_moe::kEpChunks && El % c == 0) h->ep_chunks = c;
+  }
   h->ep_cs_pos.assign((size_t)W * h->ep_chunks, 0);
   h->ep_cs_rows.assign((size_t)W * h->ep_chunks, 0);
   h->ep_cr_pos.assign((size_t)W * h->ep_chunks, 0);
@@ -330,8 +338,11 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   Marker quiet{h, layer, st};
   quiet.ns = kStages;  // (no stage events inside the expert calls)
   const int jo = (W - 1) * El;
-  AL_TRY(run_experts(h, routed_weights(L), path, xr, ARTLITE_BF16, true, ident, 1, recv_rows[r], El, goff + jo,
-                     gcnt + jo, xr_rows, &yrows, &ydt, st, quiet, false, gexp + jo, El));
+  if (W == 2) {  // the own groups while the rows travel, then the peer's (at N >= 4 the own block is too small a share
+                 // to hide the exchange behind, and one launch over all groups costs less than two)
+    AL_TRY(run_experts(h, routed_weights(L), path, xr, ARTLITE_BF16, true, ident, 1, recv_rows[r], El, goff + jo,
+                       gcnt + jo, xr_rows, &yrows, &ydt, st, quiet, false, gexp + jo, El));
+  }
   AL_TRY(mk.mark());
   const int Gc = (W - 1) * Ec;  // groups a chunk
   for (int c = 0; c < C; c++) {
@@ -339,8 +350,10 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
     int64_t rows = 0;
     for (int q = 0; q < W; q++)
       if (q != r) rows += h->ep_cr_rows[(size_t)q * C + c];
-    if (Gc)
-      AL_TRY(run_experts(h, routed_weights(L), path, xr, ARTLITE_BF16, true, ident, 1, rows, Gc, goff + c * Gc,
+    const int ng = Gc + (W == 2 || c < C - 1 ? 0 : El);  // (N >= 4: the last chunk's run takes the own groups too)
+    if (W != 2 && c == C - 1) rows += recv_rows[r];
+    if (ng)
+      AL_TRY(run_experts(h, routed_weights(L), path, xr, ARTLITE_BF16, true, ident, 1, rows, ng, goff + c * Gc,
                          gcnt + c * Gc, xr_rows, &yrows, &ydt, st, quiet, false, gexp + c * Gc, El));
     AL_CUDA(cudaEventRecord(ev_y[c], st));
   }

@@ -1,6 +1,6 @@
-"""Expert parallelism on 2 GPUs (NCCL, one process per GPU): each rank owns half of the experts and its own tokens;
+"""Expert parallelism on 2 and 4 GPUs (NCCL, one process per GPU): each rank owns 1/N of the experts and its own tokens;
 the EP forward (token rows out by NCCL send / recv, local tcgen05 or GEMV experts, outputs back, local combine) must
-equal, on every rank, the single-GPU block over the same tokens with all experts. Skipped with fewer than 2 GPUs.
+equal, on every rank, the single-GPU block over the same tokens with all experts. Skipped with fewer GPUs than ranks.
 NVLS is off (NCCL_NVLS_ENABLE=0); the ranks are child processes."""
 
 import os
@@ -13,8 +13,9 @@ pytestmark = pytest.mark.gpu
 H, E, K, F = 512, 16, 4, 256
 
 
-def _rank(rank, world, uid, path, T, Tmax, q):
+def _rank(rank, world, uid, path, T, Tmax, chunks, q):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["ARTLITE_EP_CHUNKS"] = str(chunks)
     os.environ["ARTLITE_EP_TIMEOUT_MS"] = "20000"
     import torch
     torch.cuda.set_device(rank)
@@ -39,19 +40,19 @@ def _rank(rank, world, uid, path, T, Tmax, q):
     q.put((rank, float(moe_np.rel_max(a, b)), bool(np.array_equal(y_ep, y_one)), bool(np.array_equal(y_ep, y_ep2))))
 
 
-@pytest.mark.parametrize("path,T", [("tc", 300), ("gemv", 7)])
-def test_ep2_matches_single_gpu(path, T):
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("path,T,chunks", [("tc", 300, 1), ("tc", 300, 4), ("gemv", 7, 1)])
+def test_ep_matches_single_gpu(path, T, chunks, world):
     import torch
     import torch.multiprocessing as mp
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from artlite_b200.moe.block import ep_unique_id
-    world = 2
     uid = ep_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     Tmax = T + 13 * (world - 1)
-    procs = [ctx.Process(target=_rank, args=(r, world, uid, path, T + 13 * r, Tmax, q), daemon=True)
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, path, T + 13 * r, Tmax, chunks, q), daemon=True)
              for r in range(world)]
     for p in procs:
         p.start()
