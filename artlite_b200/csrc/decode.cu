@@ -161,13 +161,15 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
   if constexpr (kMs) {
     uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sm) + a.stage_bytes - 64);
     pp.full = bars;
-    pp.empty = bars + ms::kStages;
-    pp.failed = reinterpret_cast<int*>(bars + 2 * ms::kStages);
+    pp.done = reinterpret_cast<int*>(bars + ms::kStages);
+    pp.issued = pp.done + ms::kStages;
+    pp.failed = pp.issued + 1;
     if (threadIdx.x == 0) {
       for (int i = 0; i < ms::kStages; i++) {
-        ms::mbar_init(&pp.full[i], 1);
-        ms::mbar_init(&pp.empty[i], ms::kThreads / 32);
+        ms::mbar_init(&pp.full[i], ms::kFullArrivals);
+        pp.done[i] = 0;
       }
+      *pp.issued = 0;
       *pp.failed = 0;
     }
   }

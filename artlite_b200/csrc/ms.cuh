@@ -2,17 +2,21 @@
 // (decode.cu).
 //
 // Work: items (expert, group of 8 pairs, tile of rows), split over the CTAs; a CTA walks its items' 256-value
-// super-block columns as steps. Each step's weights arrive in one of three shared-memory stages by TMA (one 2D tile per
-// matrix: 64 gate and 64 up rows, or 128 down rows, one 144-byte super-block wide; completion counted on the stage's
-// mbarrier), two steps in flight while one is computed. The 8 token slots' x for the column (pre-arranged as bf16 in
-// the mma fragment order, with per-group sums) come from global memory (L2) with plain loads issued before the wait.
+// super-block columns as steps. Each step arrives in one of three shared-memory stages, its completion counted on the
+// stage's mbarrier: the weights by TMA (one 2D tile per matrix: 64 gate and 64 up rows, or 128 down rows, one 144-byte
+// super-block wide) and the 8 token slots' x for the column (pre-arranged as bf16 in the mma fragment order, with
+// per-group sums) by the refilling warp's cp.async (16 bytes a lane, their completion arriving on the same mbarrier),
+// so that no warp waits on a global load inside a step and the CTA reads x once, not once per warp. Two steps are in
+// flight while one is computed; the last warp done with a stage refills it.
 //
-// The product: mma.sync m16n8k16 (bf16 x bf16 -> fp32), a warp per 16-row tile (and matrix), the 8 token slots as the
-// n side. Lane (g = lane / 4, t = lane % 4) takes bytes 8t .. 8t + 7 of each 32-byte quant chunk of rows g and g + 8
-// (chunk c: group 2c in the low nibbles, group 2c + 1 in the high ones) straight into A fragments by one LOP3 per two
-// values, (q | 0x4300) = the bf16 value 128 + q exactly; within a 32-value group the k order is permuted (lane t's
-// eight values fill its k slots 2t, 2t + 1, 2t + 8, 2t + 9 of two k16 steps) and x is arranged in the same order, so
-// the dot products are unchanged. A group's scales apply after its two mma steps:
+// The product: mma.sync m16n8k16 (bf16 x bf16 -> fp32), a warp per 16-row tile, the 8 token slots as the n side. For
+// gate / up the tile's rows 0-7 are 8 gate rows and rows 8-15 the same 8 up rows, so that a lane holds gate and up of
+// one output row and applies silu(gate) x up in registers. Lane (g = lane / 4, t = lane % 4) takes bytes 8t .. 8t + 7
+// of each 32-byte quant chunk of its two rows (chunk c: group 2c in the low nibbles, group 2c + 1 in the high ones)
+// straight into A fragments by one LOP3 per two values, (q | 0x4300) = the bf16 value 128 + q exactly; within a
+// 32-value group the k order is permuted (lane t's eight values fill its k slots 2t, 2t + 1, 2t + 8, 2t + 9 of two k16
+// steps) and x is arranged in the same order, so the dot products are unchanged. A group's scales apply after its two
+// mma steps:
 //   sum_j w_j x_j = (d sc) S - (128 d sc + dmin m) X,   S = sum_j (128 + q_j) x_j,   X = sum_j x_j,
 // the reference's dequantised weight being w = (d sc) q - (dmin m) (gguf_model.py:278-330). Products are exact, the
 // sums differ from the reference's fp32 order by rounding; x is the bf16 activation (for the down projection, h rounded
@@ -32,9 +36,15 @@ namespace ms {
 constexpr int kThreads = 256;
 constexpr int kStages = 3;
 constexpr int kRows = 128;                     // raw rows per step (gate 64 + up 64, or 128 down rows)
-constexpr int kStageBytes = kRows * 144;       // 18432 (a multiple of 128: TMA destinations)
-constexpr int kOutBytes = 3 * 64 * 8 * 4;      // gate / up tile outputs of an item (gu), and h
+constexpr int kWBytes = kRows * 144;           // 18432: the step's weights
+constexpr int kXRow = 528;                     // a token slot's x in the stage: 512 bytes + 16 of padding (banks)
+constexpr int kXOff = kWBytes;                 // 8 slots x kXRow
+constexpr int kSOff = kXOff + 8 * kXRow;       // 8 slots x 8 group sums (32 bytes)
+constexpr int kStageBytes = kSOff + 8 * 32;    // 22912 (a multiple of 128: TMA destinations)
+constexpr unsigned kFullArrivals = 33;         // a stage's full barrier: the refiller's expect_tx + 32 lanes' cp.async
+constexpr int kOutBytes = 2 * 64 * 8 * 4;      // h of an item (gu), [8 tokens][64 rows], two buffers
 constexpr int kTabBytes = 8 * 16 * 8 * 8;      // per warp: 16 rows x 8 groups x {A, B}
+static_assert(kStageBytes % 128 == 0, "stages start 128-byte aligned");
 constexpr long long kWaitCycles = 4000000000LL;  // about 2 s
 
 __host__ __device__ constexpr size_t smem_bytes() { return (size_t)kStages * kStageBytes + kOutBytes + kTabBytes + 64; }
@@ -84,6 +94,15 @@ __device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint
                : "memory");
 }
 
+// 16 bytes global -> shared (L2 only), asynchronous
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+// one arrival on b once this thread's earlier cp.async copies have landed (counted in the barrier's init count)
+__device__ __forceinline__ void cp_arrive(uint64_t* b) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(su32(b)) : "memory");
+}
+
 __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
@@ -105,87 +124,111 @@ struct Gemv {
   float* y;
 };
 
-struct Pipe {  // the CTA's stages: full (the copies landed: one arrival + bytes) and empty (every warp is done: 8
-               // arrivals) mbarriers, and the parity each thread waits for next (bit i: stage i)
-  uint64_t *full, *empty;
-  unsigned full_parity, empty_parity;
+struct Pipe {  // the CTA's stages: full mbarriers (the copies landed: one arrival + bytes) and the parity each thread
+               // waits for next (bit i: stage i); per stage a count of the warps done with its current step (shared)
+  uint64_t* full;
+  unsigned full_parity;
+  int* done;     // [kStages]: the warp that makes it 8 resets it and refills the stage
+  int* issued;   // (shared) steps whose copies were started in the current run
   int* failed;   // (shared) set once a wait ran out: no more copies are started, no more results written
 };
 
-struct Step {
-  int e, rt, sb, nt;
+// an item: expert e, row tile rt, its pairs [d0, d0 + nt) in dispatch order (nt <= 8)
+struct Item {
+  int e, rt, nt;
   int64_t d0;
 };
 
+// the item's fields; e is a hint at or below its expert (items ascend, so a forward scan finds it)
 template <bool GU>
-__device__ __forceinline__ Step step_of(const Gemv& a, int s, int i0, const int32_t* uo, const int64_t* offs) {
-  const int SB = a.K >> 8;
-  const int rows_item = GU ? 64 : 128, ntile = a.N / rows_item;
-  const int item = i0 + s / SB;
-  int lo = 0, hi = a.E;
+__device__ __forceinline__ Item item_at(const Gemv& a, int item, int& e, const int32_t* uo, const int64_t* offs) {
+  while (uo[e + 1] <= item) e++;
+  const int ntile = a.N / (GU ? 64 : 128);
+  const int li = item - uo[e], tg = li / ntile;
+  Item it;
+  it.e = e;
+  it.rt = li - tg * ntile;
+  it.d0 = offs[e] + (int64_t)tg * kGemvTokens;
+  it.nt = (int)min64(kGemvTokens, offs[e + 1] - it.d0);
+  return it;
+}
+
+// the expert of item i0 (binary search over the item offsets)
+__device__ __forceinline__ int expert_of(int item, int E, const int32_t* uo) {
+  int lo = 0, hi = E;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (uo[mid] <= item) lo = mid; else hi = mid;
   }
-  const int li = item - uo[lo], tg = li / ntile;
-  Step st;
-  st.e = lo;
-  st.rt = li - tg * ntile;
-  st.sb = s - (s / SB) * SB;
-  st.d0 = offs[lo] + (int64_t)tg * kGemvTokens;
-  st.nt = (int)min64(kGemvTokens, offs[lo + 1] - st.d0);
-  return st;
+  return lo;
 }
 
-// the TMA copies of a step into stage buffer buf (thread 0, after announcing kStageBytes)
+// the copies of step (it, sb) into stage buffer buf, completing on bar; a whole warp calls it: lane 0 announces the
+// weight bytes and starts the weight tiles (TMA), every lane copies 16 bytes of each token slot's 512 bytes of x and
+// lanes 0-15 the slots' 32 bytes of group sums, then arrives once its copies land (slots past nt copy slot 0's row:
+// their products are discarded)
 template <bool GU>
-__device__ __forceinline__ void issue(const Gemv& a, const Step& st, uint8_t* buf, uint64_t* bar) {
-  const int y = st.e * a.N + st.rt * (GU ? 64 : 128);
-  tma_load(buf, a.m0, bar, st.sb * 72, y);
-  if (GU) tma_load(buf + 64 * 144, a.m1, bar, st.sb * 72, y);
+__device__ __forceinline__ void refill(const Gemv& a, const Item& it, int sb, const int32_t* perm, uint8_t* buf,
+                                       uint64_t* bar, int lane) {
+  if (lane == 0) {
+    const int y = it.e * a.N + it.rt * (GU ? 64 : 128);
+    mbar_expect(bar, kWBytes);
+    tma_load(buf, a.m0, bar, sb * 72, y);
+    if (GU) tma_load(buf + 64 * 144, a.m1, bar, sb * 72, y);
+  }
+  const int G = a.K >> 5;
+  const int n = lane & 7;
+  const int64_t d = it.d0 + (n < it.nt ? n : 0);
+  const int64_t my_row = GU ? (int64_t)(perm[d] / a.k) : d;  // (slot lane & 7's x row)
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int64_t row = __shfl_sync(0xFFFFFFFFu, my_row, i);
+    cp16(buf + kXOff + i * kXRow + lane * 16, a.xq + (row * G + sb * 8) * 4 + lane);
+  }
+  const int64_t srow = __shfl_sync(0xFFFFFFFFu, my_row, (lane >> 1) & 7);
+  if (lane < 16) cp16(buf + kSOff + (lane >> 1) * 32 + (lane & 1) * 16, a.xs + srow * G + sb * 8 + (lane & 1) * 4);
+  cp_arrive(bar);
 }
 
-// x of a step for this lane: the B fragments of token slot g for the column's 8 groups, and the group sums of slots
-// 2t, 2t + 1 (slots past nt read slot 0's row: their products are discarded)
+// x of a step for this lane, from the stage: the B fragments of token slot g for the column's 8 groups, and the group
+// sums of slots 2t, 2t + 1
 struct XFrag {
   uint4 b[8];
   float4 s[2][2];
 };
 
-template <bool GU>
-__device__ __forceinline__ void load_x(const Gemv& a, const Step& st, const int32_t* perm, int lane, XFrag& x) {
+__device__ __forceinline__ void load_x(const uint8_t* buf, int lane, XFrag& x) {
   const int g = lane >> 2, t = lane & 3;
-  const int G = a.K >> 5;
-  auto row_of = [&](int n) -> int64_t {
-    n = n < st.nt ? n : 0;
-    return GU ? (int64_t)(perm[st.d0 + n] / a.k) : st.d0 + n;
-  };
-  const uint4* xr = a.xq + (row_of(g) * G + st.sb * 8) * 4 + t;
+  const uint4* xr = reinterpret_cast<const uint4*>(buf + kXOff + g * kXRow) + t;
 #pragma unroll
-  for (int j = 0; j < 8; j++) x.b[j] = __ldcg(xr + 4 * j);
+  for (int j = 0; j < 8; j++) x.b[j] = xr[4 * j];
 #pragma unroll
   for (int i = 0; i < 2; i++) {
-    const float4* sr = reinterpret_cast<const float4*>(a.xs + row_of(2 * t + i) * G + st.sb * 8);
-    x.s[i][0] = __ldcg(sr);
-    x.s[i][1] = __ldcg(sr + 1);
+    const float4* sr = reinterpret_cast<const float4*>(buf + kSOff + (2 * t + i) * 32);
+    x.s[i][0] = sr[0];
+    x.s[i][1] = sr[1];
   }
 }
 
-// this warp's 16-row tile x one super-block column: accumulates y (rows g, g + 8 x tokens 2t, 2t + 1)
+// this warp's 16-row tile x one super-block column: rows 0-7 at lo, rows 8-15 at hi (144-byte rows); accumulates y
+// (rows g, g + 8 x tokens 2t, 2t + 1)
 __device__ __forceinline__ float f4at(const float4 (&v)[2], int j) {
   const float4 q = v[j >> 2];
   return (j & 3) == 0 ? q.x : (j & 3) == 1 ? q.y : (j & 3) == 2 ? q.z : q.w;
 }
 
-__device__ __forceinline__ void tile_sb(const uint8_t* rows, const XFrag& x, float* tab, int lane, float (&y)[4]) {
+__device__ __forceinline__ void tile_sb(const uint8_t* lo, const uint8_t* hi, const XFrag& x, float* tab, int lane,
+                                        float (&y)[4]) {
   const int g = lane >> 2, t = lane & 3;
+  const uint8_t* r0 = lo + g * 144;
+  const uint8_t* r1 = hi + g * 144;
   // scales of rows (g, g + 8) x groups (2t, 2t + 1) into the warp's table. The twelve scale bytes q0 .. q11 hold the
   // six-bit scale / min of group j < 4 in q[j] / q[j + 4] (low six bits) and of j >= 4 in the nibbles of q[j + 4] with
   // the top two bits of q[j - 4] / q[j]: as packed bytes, sc(0..3) = w1 & 0x3F.., sc(4..7) = (w3 & 0x0F..) |
   // ((w1 & 0xC0..) >> 2), mn(0..3) = w2 & 0x3F.., mn(4..7) = ((w3 >> 4) & 0x0F..) | ((w2 & 0xC0..) >> 2).
 #pragma unroll
   for (int i = 0; i < 2; i++) {
-    const uint4 h = *reinterpret_cast<const uint4*>(rows + (g + 8 * i) * 144);
+    const uint4 h = *reinterpret_cast<const uint4*>(i ? r1 : r0);
     const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
     const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
     const uint32_t sc_w = t < 2 ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y & 0xC0C0C0C0u) >> 2));
@@ -201,8 +244,8 @@ __device__ __forceinline__ void tile_sb(const uint8_t* rows, const XFrag& x, flo
   __syncwarp();
 #pragma unroll
   for (int c = 0; c < 4; c++) {
-    const uint2 q0 = *reinterpret_cast<const uint2*>(rows + g * 144 + 16 + 32 * c + 8 * t);
-    const uint2 q1 = *reinterpret_cast<const uint2*>(rows + (g + 8) * 144 + 16 + 32 * c + 8 * t);
+    const uint2 q0 = *reinterpret_cast<const uint2*>(r0 + 16 + 32 * c + 8 * t);
+    const uint2 q1 = *reinterpret_cast<const uint2*>(r1 + 16 + 32 * c + 8 * t);
 #pragma unroll
     for (int p = 0; p < 2; p++) {
       const int j = 2 * c + p, sh = 4 * p;
@@ -226,9 +269,11 @@ __device__ __forceinline__ void tile_sb(const uint8_t* rows, const XFrag& x, flo
 }
 
 // Items [i0, i1) of one GEMV (gu: 64 output rows an item, gate and up; down: 128 rows). Every thread of the CTA calls
-// it; smem (128-byte aligned): the stages, the output tile, the per-warp tables (smem_bytes()). x must be complete in
-// global memory (a grid barrier before). Thread 0 starts the copies: a stage is refilled once its empty barrier shows
-// every warp done with it; the warps otherwise run ahead of one another by up to the stages in flight.
+// it; smem (128-byte aligned): the stages, the h buffers, the per-warp tables (smem_bytes()). x must be complete in
+// global memory (a grid barrier before). Thread 0 starts the first copies; afterwards the last warp to finish with a
+// stage refills it with the step kStages ahead (no waiting producer: the copy starts the moment the stage is free, and
+// no warp both computes and waits for the others); the warps otherwise run ahead of one another by up to the stages in
+// flight.
 template <bool GU>
 __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int64_t* offs, const int32_t* perm,
                                    uint8_t* smem, Pipe& pp, int i0, int i1, DevStatus* status) {
@@ -236,7 +281,7 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
   const int SB = a.K >> 8;
   const int S = (i1 - i0) * SB;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float* out = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [2][64][8]
+  float* out = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [2][8 tokens][64 rows]
   float* tab = reinterpret_cast<float*>(smem + kStages * kStageBytes + kOutBytes) + warp * 16 * 8 * 2;
   if (S <= 0) return;
   if ((su32(smem) & 127u) != 0) {  // (TMA destinations: never issued to a misaligned stage)
@@ -248,23 +293,27 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
     return;
   }
   const bool producer = threadIdx.x == 0;
-  // prologue: steps 0 .. kStages - 1 (the stages are free: the previous user waited for every copy it started)
-  int issued = 0;
-  if (producer && !*pp.failed)
-    for (int s = 0; s < kStages && s < S; s++) {
-      mbar_expect(&pp.full[s], kStageBytes);
-      issue<GU>(a, step_of<GU>(a, s, i0, uo, offs), smem + s * kStageBytes, &pp.full[s]);
-      issued = s + 1;
-    }
+  int e_run = expert_of(i0, a.E, uo);  // (the compute side's expert hint)
+  int e_fill = e_run;                  // (this warp's hint for the refills it issues)
+  // prologue (warp 0): steps 0 .. kStages - 1 (the stages are free: the previous user waited for every copy it started)
+  if (warp == 0) {
+    const bool go = !*(volatile int*)pp.failed;
+    int n = 0;
+    if (go)
+      for (int s = 0; s < kStages && s < S; s++, n++)
+        refill<GU>(a, item_at<GU>(a, i0 + s / SB, e_fill, uo, offs), s % SB, perm, smem + s * kStageBytes, &pp.full[s],
+                   lane);
+    if (lane == 0) *(volatile int*)pp.issued = n;
+  }
   float y[4] = {0, 0, 0, 0};
-  const int tile = GU ? warp >> 1 : warp, mat = GU ? warp & 1 : 0;
+  // gu: this warp's 8 output rows (gate rows at the stage's first 64, up rows at the next 64); down: its 16 rows
+  const int r_lo = GU ? warp * 8 : warp * 16, r_hi = GU ? 64 + warp * 8 : warp * 16 + 8;
   int waited = 0;  // (producer: steps whose copies are known complete)
+  Item it = item_at<GU>(a, i0, e_run, uo, offs);
+  int sb = 0, li = 0;  // (column of the current item, items done)
   for (int s = 0; s < S; s++) {
     const int b = s % kStages;
-    const Step st = step_of<GU>(a, s, i0, uo, offs);
     uint8_t* buf = smem + b * kStageBytes;
-    XFrag xf;
-    load_x<GU>(a, st, perm, lane, xf);
     bool ok = !*(volatile int*)pp.failed;
     if (ok) {
       ok = mbar_wait(&pp.full[b], (pp.full_parity >> b) & 1u, status);
@@ -273,25 +322,35 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
     pp.full_parity ^= 1u << b;
     ok = __all_sync(0xFFFFFFFFu, ok);
     if (producer && ok) waited = s + 1;
-    if (ok) tile_sb(buf + (mat * 64 + tile * 16) * 144, xf, tab, lane, y);
+    if (ok) {
+      XFrag xf;
+      load_x(buf, lane, xf);
+      tile_sb(buf + r_lo * 144, buf + r_hi * 144, xf, tab, lane, y);
+    }
     __syncwarp();
-    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&pp.empty[b])) : "memory");
-    if (st.sb == SB - 1) {  // the item's last column: its outputs (every warp meets here)
+    // done with stage b: the eighth warp to get here refills it with step s + kStages (the count is reset before the
+    // copy starts; no warp counts on stage b again before that copy has landed)
+    int last = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      last = atomicAdd(&pp.done[b], 1) == kThreads / 32 - 1;
+      if (last) atomicExch(&pp.done[b], 0);
+    }
+    const int s2 = s + kStages;
+    if (__shfl_sync(0xFFFFFFFFu, last, 0) && s2 < S && !*(volatile int*)pp.failed) {
+      const int q = s2 / SB;
+      refill<GU>(a, item_at<GU>(a, i0 + q, e_fill, uo, offs), s2 - q * SB, perm, buf, &pp.full[b], lane);
+      if (lane == 0) atomicMax(pp.issued, s2 + 1);
+    }
+    if (++sb == SB) {  // the item's last column: its outputs
       const int g = lane >> 2, t = lane & 3;
       const bool good = !*(volatile int*)pp.failed;
-      if (GU) {
-        float* o = out + mat * 64 * 8;
-        o[(tile * 16 + g) * 8 + 2 * t] = y[0];
-        o[(tile * 16 + g) * 8 + 2 * t + 1] = y[1];
-        o[(tile * 16 + g + 8) * 8 + 2 * t] = y[2];
-        o[(tile * 16 + g + 8) * 8 + 2 * t + 1] = y[3];
-        __syncthreads();
-        float* hb = out + 2 * 64 * 8;  // [8 tokens][64 rows]: h rounded to bf16
-        for (int v = threadIdx.x; v < 64 * 8; v += kThreads) {
-          const int r = v >> 3, n = v & 7;
-          hb[n * 64 + r] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(silu(out[r * 8 + n]), out[64 * 8 + r * 8 + n])));
-        }
-        __syncthreads();
+      if (GU) {  // h = silu(gate) x up, rounded to bf16, into this item's buffer [8 tokens][64 rows]
+        float* hb = out + (li & 1) * 64 * 8;
+        const int r = warp * 8 + g;
+        hb[(2 * t) * 64 + r] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(silu(y[0]), y[2])));
+        hb[(2 * t + 1) * 64 + r] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(silu(y[1]), y[3])));
+        __syncthreads();  // (the other buffer: free since the previous item's barrier)
         if (threadIdx.x < 64) {  // (n, group of 32 rows, t): 8 h values in fragment order, and the group sum
           const int n = threadIdx.x >> 3, grp = (threadIdx.x >> 2) & 1, tq = threadIdx.x & 3;
           const float4 h0 = *reinterpret_cast<const float4*>(hb + n * 64 + grp * 32 + 8 * tq);
@@ -300,45 +359,34 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
           float part = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
           part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
           part += __shfl_xor_sync(0xFFFFFFFFu, part, 2);
-          if (n < st.nt && good) {
+          if (n < it.nt && good) {
             const int Go = a.N >> 5;
-            const int64_t pr = st.d0 + n;
-            const int og = st.rt * 2 + grp;
+            const int64_t pr = it.d0 + n;
+            const int og = it.rt * 2 + grp;
             a.hq[(pr * Go + og) * 4 + tq] = arrange(v);
             if (tq == 0) a.hs[pr * Go + og] = part;
           }
         }
-        __syncthreads();  // (out is free again)
       } else if (good) {
-        const int64_t row = (int64_t)st.rt * 128 + tile * 16 + g;
-        if (2 * t < st.nt) {
-          a.y[(st.d0 + 2 * t) * a.N + row] = y[0];
-          a.y[(st.d0 + 2 * t) * a.N + row + 8] = y[2];
+        const int64_t row = (int64_t)it.rt * 128 + warp * 16 + g;
+        if (2 * t < it.nt) {
+          a.y[(it.d0 + 2 * t) * a.N + row] = y[0];
+          a.y[(it.d0 + 2 * t) * a.N + row + 8] = y[2];
         }
-        if (2 * t + 1 < st.nt) {
-          a.y[(st.d0 + 2 * t + 1) * a.N + row] = y[1];
-          a.y[(st.d0 + 2 * t + 1) * a.N + row + 8] = y[3];
+        if (2 * t + 1 < it.nt) {
+          a.y[(it.d0 + 2 * t + 1) * a.N + row] = y[1];
+          a.y[(it.d0 + 2 * t + 1) * a.N + row + 8] = y[3];
         }
       }
       y[0] = y[1] = y[2] = y[3] = 0.0f;
-    }
-    // the producer refills this stage with step s + kStages once every warp is done with it
-    if (producer) {
-      const int s2 = s + kStages;
-      bool free_ok = true;
-      if (s < issued) {  // (its empty phase for step s completes when all 8 warps arrived)
-        free_ok = !*(volatile int*)pp.failed && mbar_wait(&pp.empty[b], (pp.empty_parity >> b) & 1u, status);
-        pp.empty_parity ^= 1u << b;
-        if (!free_ok) *(volatile int*)pp.failed = 1;
-      }
-      if (s2 < S && free_ok && !*(volatile int*)pp.failed) {
-        mbar_expect(&pp.full[b], kStageBytes);
-        issue<GU>(a, step_of<GU>(a, s2, i0, uo, offs), buf, &pp.full[b]);
-        issued = s2 + 1;
-      }
+      sb = 0;
+      li++;
+      if (i0 + li < i1) it = item_at<GU>(a, i0 + li, e_run, uo, offs);
     }
   }
   // after a failure: wait (bounded) for the copies already started, so that none lands in a stage after this
+  __syncthreads();
+  const int issued = *(volatile int*)pp.issued;
   if (producer)
     for (int s = waited; s < issued; s++) {
       const int b = s % kStages;
