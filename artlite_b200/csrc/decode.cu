@@ -1,9 +1,9 @@
 // The fused decode-batch forward: one cooperative kernel per layer for small batches on the GEMV path (8 <= T,
 // T k <= 512 pairs, E <= 256, Q4_0 / Q8_0 / Q4_K weights, one type for gate / up / down, no shared expert). It runs
 // the same steps as the separate kernels of a forward, in phases separated by grid barriers:
-//   1. router logits (router.cu's semantics: fp32 products, fp32 sums, + bias): a warp per (token, expert), W and x
-//      rows read with 16-byte loads (1024 columns at a time); for Q4_K also the tokens' x in the streaming GEMV's
-//      fragment order (ms.cuh);
+//   1. router logits (router.cu's semantics: fp32 products, fp32 sums, + bias): register-blocked 4 tokens x 4 experts
+//      a warp over a quarter of H (router_tiles), or a warp per (token, expert) for other shapes; for Q4_K also the
+//      tokens' x in the streaming GEMV's fragment order (ms.cuh);
 //   2. routing (route.cuh, the reference's moe_route): when T <= 8 every CTA routes all tokens for its own copy (no
 //      barrier), else CTA c routes tokens 8c .. 8c + 7 and a barrier follows; then every CTA builds the dispatch of the
 //      T k pairs in its shared memory (histogram, scan, stable rank: the order dispatch.cu gives, the same in every
@@ -135,6 +135,71 @@ __device__ __forceinline__ void router_unit(const DecodeArgs& a, int t, int e, i
   if (lane == 0) a.logits[(int64_t)t * a.E + e] = a.bias ? acc + a.bias[e] : acc;
 }
 
+// phase 1 when H % 512 == 0 and E % 4 == 0: register-blocked logits. A CTA takes two (4 tokens x 4 experts) blocks, a
+// warp one block over a quarter of H (each lane 4 consecutive values of every 128), so that a router row and an x row
+// are read 4 times less often than a warp per logit reads them; the quarters' sums meet in shared memory (part: 128
+// floats) and add in a fixed order, + bias
+__device__ __forceinline__ void router_tiles(const DecodeArgs& a, float* part, int warp, int lane) {
+  const int TB = (a.T + 3) >> 2, EB = a.E >> 2, units = TB * EB;
+  const int kq = a.H >> 2;
+  for (int u0 = blockIdx.x * 2; u0 < units; u0 += gridDim.x * 2) {  // (the same trip count for the whole CTA)
+    const int u = u0 + (warp >> 2), kp = warp & 3;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+    if (u < units) {
+      const int t0 = (u / EB) * 4, e0 = (u - (u / EB) * EB) * 4;
+#pragma unroll 2
+      for (int c = kp * kq + lane * 4; c < (kp + 1) * kq; c += 128) {
+        float wv[4][4], xv[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) load4(a.router, a.router_dtype, (int64_t)(e0 + i) * a.H + c, wv[i]);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          if (t0 + i < a.T) {
+            load4(a.x, a.x_dtype, (int64_t)(t0 + i) * a.H + c, xv[i]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) xv[i][j] = 0.0f;
+          }
+        }
+#pragma unroll
+        for (int ti = 0; ti < 4; ti++)
+#pragma unroll
+          for (int ei = 0; ei < 4; ei++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[ti][ei] = fmaf(wv[ei][j], xv[ti][j], acc[ti][ei]);
+      }
+    }
+#pragma unroll
+    for (int ti = 0; ti < 4; ti++)
+#pragma unroll
+      for (int ei = 0; ei < 4; ei++)
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc[ti][ei] += __shfl_xor_sync(0xFFFFFFFFu, acc[ti][ei], o);
+    if (lane == 0)
+#pragma unroll
+      for (int ti = 0; ti < 4; ti++)
+#pragma unroll
+        for (int ei = 0; ei < 4; ei++) part[warp * 16 + ti * 4 + ei] = acc[ti][ei];
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int uu = threadIdx.x >> 4, q = threadIdx.x & 15, u2 = u0 + uu;
+      if (u2 < units) {
+        const int t = (u2 / EB) * 4 + (q >> 2), e = (u2 - (u2 / EB) * EB) * 4 + (q & 3);
+        if (t < a.T) {
+          const float* pp = part + uu * 64 + q;
+          const float v = (pp[0] + pp[16]) + (pp[32] + pp[48]);
+          a.logits[(int64_t)t * a.E + e] = a.bias ? v + a.bias[e] : v;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 template <int QG, int QD, int J>
 __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(128) float sm[];
@@ -174,8 +239,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     }
   }
   // ---- 1. router logits (and the tokens' x in fragment order)
-  for (int u = blockIdx.x * rq::kWarps + warp; u < a.T * E; u += gridDim.x * rq::kWarps)
-    router_unit(a, u / E, u % E, lane);
+  if (a.H % 512 == 0 && E % 4 == 0) {
+    router_tiles(a, sm, warp, lane);  // (the staging area is free until phase 3; its end holds the mbarriers)
+  } else {
+    for (int u = blockIdx.x * rq::kWarps + warp; u < a.T * E; u += gridDim.x * rq::kWarps)
+      router_unit(a, u / E, u % E, lane);
+  }
   if constexpr (kMs) {
     const int G = a.H >> 5;
     for (int u = blockIdx.x * kThreads + threadIdx.x; u < a.T * G * 4; u += gridDim.x * kThreads) {  // (4 | kThreads)

@@ -43,7 +43,8 @@ constexpr int kSOff = kXOff + 8 * kXRow;       // 8 slots x 8 group sums (32 byt
 constexpr int kStageBytes = kSOff + 8 * 32;    // 22912 (a multiple of 128: TMA destinations)
 constexpr unsigned kFullArrivals = 33;         // a stage's full barrier: the refiller's expect_tx + 32 lanes' cp.async
 constexpr int kOutBytes = 2 * 64 * 8 * 4;      // h of an item (gu), [8 tokens][64 rows], two buffers
-constexpr int kTabBytes = 8 * 16 * 8 * 8;      // per warp: 16 rows x 8 groups x {A, B}
+constexpr int kTabRow = 9;                     // a row's {A, B} pairs: 8 groups + 1 of padding (banks)
+constexpr int kTabBytes = 8 * 16 * kTabRow * 8;  // per warp: 16 rows x 8 groups x {A, B}
 static_assert(kStageBytes % 128 == 0, "stages start 128-byte aligned");
 constexpr long long kWaitCycles = 4000000000LL;  // about 2 s
 
@@ -210,8 +211,12 @@ __device__ __forceinline__ void load_x(const uint8_t* buf, int lane, XFrag& x) {
   }
 }
 
-// this warp's 16-row tile x one super-block column: rows 0-7 at lo, rows 8-15 at hi (144-byte rows); accumulates y
-// (rows g, g + 8 x tokens 2t, 2t + 1)
+// the physical row (of 8) that tile row g reads: rows 0-3 of the tile from the even rows, 4-7 from the odd ones, so
+// that each half-warp's 8-byte loads of a 144-byte-stride tile fall on 32 distinct banks
+__device__ __forceinline__ int prow(int g) { return ((g & 3) << 1) | (g >> 2); }
+
+// this warp's 16-row tile x one super-block column: tile rows 0-7 at lo, 8-15 at hi (144-byte rows, tile row g reading
+// physical row prow(g)); accumulates y (tile rows g, g + 8 x tokens 2t, 2t + 1)
 __device__ __forceinline__ float f4at(const float4 (&v)[2], int j) {
   const float4 q = v[j >> 2];
   return (j & 3) == 0 ? q.x : (j & 3) == 1 ? q.y : (j & 3) == 2 ? q.z : q.w;
@@ -220,8 +225,8 @@ __device__ __forceinline__ float f4at(const float4 (&v)[2], int j) {
 __device__ __forceinline__ void tile_sb(const uint8_t* lo, const uint8_t* hi, const XFrag& x, float* tab, int lane,
                                         float (&y)[4]) {
   const int g = lane >> 2, t = lane & 3;
-  const uint8_t* r0 = lo + g * 144;
-  const uint8_t* r1 = hi + g * 144;
+  const uint8_t* r0 = lo + prow(g) * 144;
+  const uint8_t* r1 = hi + prow(g) * 144;
   // scales of rows (g, g + 8) x groups (2t, 2t + 1) into the warp's table. The twelve scale bytes q0 .. q11 hold the
   // six-bit scale / min of group j < 4 in q[j] / q[j + 4] (low six bits) and of j >= 4 in the nibbles of q[j + 4] with
   // the top two bits of q[j - 4] / q[j]: as packed bytes, sc(0..3) = w1 & 0x3F.., sc(4..7) = (w3 & 0x0F..) |
@@ -238,7 +243,7 @@ __device__ __forceinline__ void tile_sb(const uint8_t* lo, const uint8_t* hi, co
     for (int jj = 0; jj < 2; jj++) {
       const float sc = (float)((sc_w >> (sh + 8 * jj)) & 0xFFu), mn = (float)((mn_w >> (sh + 8 * jj)) & 0xFFu);
       const float dsc = __fmul_rn(d, sc), dmn = __fmul_rn(dmin, mn);
-      reinterpret_cast<float2*>(tab)[(g + 8 * i) * 8 + 2 * t + jj] = make_float2(dsc, __fmaf_rn(128.0f, dsc, dmn));
+      reinterpret_cast<float2*>(tab)[(g + 8 * i) * kTabRow + 2 * t + jj] = make_float2(dsc, __fmaf_rn(128.0f, dsc, dmn));
     }
   }
   __syncwarp();
@@ -257,8 +262,8 @@ __device__ __forceinline__ void tile_sb(const uint8_t* lo, const uint8_t* hi, co
       float acc[4] = {0, 0, 0, 0};
       mma_bf16(acc, a0, bx.x, bx.y);
       mma_bf16(acc, a1, bx.z, bx.w);
-      const float2 s0 = reinterpret_cast<const float2*>(tab)[g * 8 + j];
-      const float2 s8 = reinterpret_cast<const float2*>(tab)[(g + 8) * 8 + j];
+      const float2 s0 = reinterpret_cast<const float2*>(tab)[g * kTabRow + j];
+      const float2 s8 = reinterpret_cast<const float2*>(tab)[(g + 8) * kTabRow + j];
       y[0] = fmaf(s0.x, acc[0], fmaf(-s0.y, x0, y[0]));
       y[1] = fmaf(s0.x, acc[1], fmaf(-s0.y, x1, y[1]));
       y[2] = fmaf(s8.x, acc[2], fmaf(-s8.y, x0, y[2]));
@@ -282,7 +287,7 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
   const int S = (i1 - i0) * SB;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float* out = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [2][8 tokens][64 rows]
-  float* tab = reinterpret_cast<float*>(smem + kStages * kStageBytes + kOutBytes) + warp * 16 * 8 * 2;
+  float* tab = reinterpret_cast<float*>(smem + kStages * kStageBytes + kOutBytes) + warp * 16 * kTabRow * 2;
   if (S <= 0) return;
   if ((su32(smem) & 127u) != 0) {  // (TMA destinations: never issued to a misaligned stage)
     if (threadIdx.x == 0) {
@@ -347,7 +352,7 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
       const bool good = !*(volatile int*)pp.failed;
       if (GU) {  // h = silu(gate) x up, rounded to bf16, into this item's buffer [8 tokens][64 rows]
         float* hb = out + (li & 1) * 64 * 8;
-        const int r = warp * 8 + g;
+        const int r = warp * 8 + prow(g);
         hb[(2 * t) * 64 + r] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(silu(y[0]), y[2])));
         hb[(2 * t + 1) * 64 + r] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(silu(y[1]), y[3])));
         __syncthreads();  // (the other buffer: free since the previous item's barrier)
@@ -368,7 +373,7 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
           }
         }
       } else if (good) {
-        const int64_t row = (int64_t)it.rt * 128 + warp * 16 + g;
+        const int64_t row = (int64_t)it.rt * 128 + warp * 16 + prow(g);
         if (2 * t < it.nt) {
           a.y[(it.d0 + 2 * t) * a.N + row] = y[0];
           a.y[(it.d0 + 2 * t) * a.N + row + 8] = y[2];
