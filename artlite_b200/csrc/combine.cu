@@ -55,16 +55,26 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype
   const int64_t t = blockIdx.x;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int i = 0; i < k; i++) {
-      const float wi = w[t * k + i];
-      const int64_t sl = slot[t * k + i];
-      float v[8];
-      if (own.own && sl >= own.own_lo && sl < own.own_hi)
-        load8(own.own, y_dtype, (sl - own.own_lo) * H + c, v);
-      else
-        load8(y, y_dtype, sl * H + c, v);
+    for (int i0 = 0; i0 < k; i0 += 4) {  // (four pairs' loads in flight at once; the sum keeps the pair order)
+      float wi[4], v[4][8];
+      int64_t sl[4];
 #pragma unroll
-      for (int j = 0; j < 8; j++) acc[j] = fmaf(wi, v[j], acc[j]);
+      for (int u = 0; u < 4; u++)
+        if (i0 + u < k) wi[u] = w[t * k + i0 + u], sl[u] = slot[t * k + i0 + u];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        if (i0 + u < k) {
+          if (own.own && sl[u] >= own.own_lo && sl[u] < own.own_hi)
+            load8(own.own, y_dtype, (sl[u] - own.own_lo) * H + c, v[u]);
+          else
+            load8(y, y_dtype, sl[u] * H + c, v[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (i0 + u < k)
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[j] = fmaf(wi[u], v[u][j], acc[j]);
     }
     if (sh.y) {  // the shared expert's gated term, last in the sum
       const float si = sh.s[t];

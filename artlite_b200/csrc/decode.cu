@@ -437,9 +437,14 @@ bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t 
     const char* v = getenv("ARTLITE_DECODE_FUSED");
     return v && v[0] == '0';
   }();
+  static const int64_t t_min = [] {  // (ARTLITE_DECODE_FUSED_MIN: the smallest batch that takes the fused kernel)
+    const char* v = getenv("ARTLITE_DECODE_FUSED_MIN");
+    const int64_t m = v ? atoll(v) : 0;
+    return m >= 1 ? m : (int64_t)8;
+  }();
   const artlite_moe_desc& d = h.d;
   // (below 8 tokens the separate kernels, whose GEMV spreads finer items over the whole grid, are faster)
-  return !off && !L.has_shared && T >= 8 && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts && h.E_local == d.n_experts &&
+  return !off && !L.has_shared && T >= t_min && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts && h.E_local == d.n_experts &&
          rq_type(L.qtype) && L.down_qtype == L.qtype && d.hidden % 256 == 0 && d.expert_ffn % 256 == 0 &&
          gemv_rq_rows_per_warp(L.qtype, d.hidden, true) > 0 && gemv_rq_rows_per_warp(L.down_qtype, d.expert_ffn, false) > 0 &&
          (L.qtype != ARTLITE_Q4_K || (d.act_dtype == ARTLITE_BF16 && L.has_dm)) &&

@@ -130,26 +130,37 @@ int launch_dispatch(const DispatchArgs& a, cudaStream_t st) {
 
 // ---------------------------------------------------------------- decode-sized batches: routing and dispatch in one CTA
 //
-// For n k <= kSmallPairs pairs (and E <= kSmallExperts): one CTA of 1024 threads routes every token (a warp per row,
-// route.cuh), then histograms, scans and ranks the pairs exactly as the three dispatch kernels do for a single block
-// (the same stable order), and writes both expert GEMVs' unit scans. One launch instead of six.
-template <int J>
-__global__ void __launch_bounds__(1024) route_dispatch_small(RouteArgs r, DispatchArgs a, int mult2, int32_t* unit_off2) {
+// For n k <= kSmallPairs pairs (and E <= kSmallExperts): one CTA of NT threads (1024, or 256 for at most 512 pairs
+// and 256 experts) routes every token (a warp per row, route.cuh) into shared memory, copies the ids and weights out
+// for the caller, then histograms, scans and ranks the pairs exactly as the three dispatch kernels do for a single
+// block (the same stable order), and writes both expert GEMVs' unit scans. One launch instead of six.
+template <int J, int NT>
+__global__ void __launch_bounds__(NT) route_dispatch_small(RouteArgs r, DispatchArgs a, int mult2, int32_t* unit_off2) {
   extern __shared__ int32_t sm[];
   __shared__ int64_t s64[32];
   __shared__ int32_t s32[32];
-  int32_t* wc = sm;                 // [32][E] per-warp counts of the current round
-  int32_t* run = sm + 32 * a.E;     // [E] placed so far
+  constexpr int NW = NT / 32;
+  int32_t* wc = sm;                 // [NW][E] per-warp counts of the current round
+  int32_t* run = sm + NW * a.E;     // [E] placed so far
   int32_t* cnt = run + a.E;         // [E] histogram
   int64_t* off = reinterpret_cast<int64_t*>(cnt + a.E + (a.E & 1));  // [E] offsets
+  int32_t* ids_s = reinterpret_cast<int32_t*>(off + a.E);             // [P] the routed ids
+  float* w_s = reinterpret_cast<float*>(ids_s + a.P);                 // [P] and weights
   griddep_wait();
   griddep_launch();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int64_t t = warp; t < r.n; t += 32) route_row<J>(r, t, lane);
-  for (int i = threadIdx.x; i < 34 * a.E; i += blockDim.x) sm[i] = 0;
+  {
+    RouteArgs rl = r;
+    rl.ids = ids_s;
+    rl.w = w_s;
+    for (int64_t t = warp; t < r.n; t += NW) route_row<J>(rl, t, lane);
+  }
+  for (int i = threadIdx.x; i < (NW + 2) * a.E; i += NT) sm[i] = 0;
   __syncthreads();  // (the rows' ids are visible to the block)
-  for (int64_t p = threadIdx.x; p < a.P; p += blockDim.x) {
-    const int32_t x = a.ids[p];
+  for (int64_t p = threadIdx.x; p < a.P; p += NT) {
+    const int32_t x = ids_s[p];
+    r.ids[p] = x;
+    r.w[p] = w_s[p];
     if (x < 0 || x >= a.E)
       report(a.status, ARTLITE_EDEVICE, x, a.E, 1);
     else
@@ -178,9 +189,9 @@ __global__ void __launch_bounds__(1024) route_dispatch_small(RouteArgs r, Dispat
   }
   __syncthreads();
   const unsigned lt = (1u << lane) - 1u;
-  for (int64_t r0 = 0; r0 < a.P; r0 += 1024) {
+  for (int64_t r0 = 0; r0 < a.P; r0 += NT) {
     const int64_t p = r0 + threadIdx.x;
-    int32_t x = p < a.P ? a.ids[p] : -1;
+    int32_t x = p < a.P ? ids_s[p] : -1;
     const bool valid = x >= 0 && x < a.E;
     if (!valid) x = -1 - lane;
     const unsigned peers = __match_any_sync(0xFFFFFFFFu, x);
@@ -210,17 +221,27 @@ int launch_route_dispatch_small(const RouteArgs& r, const DispatchArgs& a, int m
                                 cudaStream_t st) {
   AL_CHECK(small_dispatch_ok(a.P, a.E) && a.P == r.n * r.k, ARTLITE_EINVAL, "route_dispatch_small: P %lld E %d",
            (long long)a.P, a.E);
-  const size_t smem = sizeof(int32_t) * (34 * (size_t)a.E + 1) + sizeof(int64_t) * a.E;
+  AL_CHECK(a.ids == r.ids, ARTLITE_EINVAL, "route_dispatch_small: the dispatch reads the routed ids");
   const int J = (r.E + 31) / 32;
+  const bool narrow = a.P <= 512 && a.E <= 256;  // (256 threads: e = threadIdx.x still covers every expert)
+  const int NT = narrow ? 256 : 1024;
+  const size_t smem = sizeof(int32_t) * ((NT / 32 + 2) * (size_t)a.E + 1) + sizeof(int64_t) * a.E +
+                      (sizeof(int32_t) + sizeof(float)) * (size_t)a.P;
   auto go = [&](auto kern) -> int {
     AL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    return launch_pdl(kern, dim3(1), dim3(1024), smem, st, r, a, mult2, unit_off2);
+    return launch_pdl(kern, dim3(1), dim3(NT), smem, st, r, a, mult2, unit_off2);
   };
-  if (J <= 1) return go(route_dispatch_small<1>);
-  if (J <= 2) return go(route_dispatch_small<2>);
-  if (J <= 4) return go(route_dispatch_small<4>);
-  if (J <= 8) return go(route_dispatch_small<8>);
-  return go(route_dispatch_small<16>);
+  if (narrow) {
+    if (J <= 1) return go(route_dispatch_small<1, 256>);
+    if (J <= 2) return go(route_dispatch_small<2, 256>);
+    if (J <= 4) return go(route_dispatch_small<4, 256>);
+    return go(route_dispatch_small<8, 256>);
+  }
+  if (J <= 1) return go(route_dispatch_small<1, 1024>);
+  if (J <= 2) return go(route_dispatch_small<2, 1024>);
+  if (J <= 4) return go(route_dispatch_small<4, 1024>);
+  if (J <= 8) return go(route_dispatch_small<8, 1024>);
+  return go(route_dispatch_small<16, 1024>);
 }
 
 // ---------------------------------------------------------------- the reference plan's chunk deal

@@ -117,12 +117,74 @@ __global__ void __launch_bounds__(256) router_small_kernel(const void* x, int x_
   }
 }
 
+// 8 consecutive values (p + i is 8-aligned): two 16-byte loads of fp32 or one of bf16
+__device__ __forceinline__ void load8(const void* p, int dtype, int64_t i, float (&v)[8]) {
+  if (dtype == ARTLITE_BF16) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p) + i));
+    const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) v[2 * j] = __uint_as_float(q[j] << 16), v[2 * j + 1] = __uint_as_float(q[j] & 0xFFFF0000u);
+  } else {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i) + 1);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  }
+}
+
+// The same for H % 256 == 0: a CTA per expert, its 8 warps splitting H (each lane 8 consecutive values of every
+// 256-wide slice its warp owns), tokens in chunks of 8. The router row is read once per CTA and every expert's CTA
+// runs at once, so a one-token batch's 1 MB of router weights is read by E SMs in one round of loads; the warps'
+// partial sums meet in shared memory and add in a fixed order, + bias.
+__global__ void __launch_bounds__(256) router_cta_kernel(const void* x, int x_dtype, const void* w, int w_dtype,
+                                                         const float* bias, int64_t T, int H, int E, float* logits) {
+  __shared__ float part[8][8];
+  griddep_wait();
+  griddep_launch();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int e = blockIdx.x; e < E; e += gridDim.x) {
+    for (int64_t t0 = 0; t0 < T; t0 += 8) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int c = warp * 256 + lane * 8; c < H; c += 8 * 256) {
+        float wv[8];
+        load8(w, w_dtype, (int64_t)e * H + c, wv);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          if (t0 + i < T) {
+            float xv[8];
+            load8(x, x_dtype, (t0 + i) * H + c, xv);
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc[i] = fmaf(wv[j], xv[j], acc[i]);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc[i] += __shfl_xor_sync(0xFFFFFFFFu, acc[i], o);
+      if (lane == 0)
+#pragma unroll
+        for (int i = 0; i < 8; i++) part[warp][i] = acc[i];
+      __syncthreads();
+      if (threadIdx.x < 8 && t0 + threadIdx.x < T) {
+        const int i = threadIdx.x;
+        const float v = ((part[0][i] + part[1][i]) + (part[2][i] + part[3][i])) +
+                        ((part[4][i] + part[5][i]) + (part[6][i] + part[7][i]));
+        logits[(t0 + i) * E + e] = bias ? v + bias[e] : v;
+      }
+      __syncthreads();
+    }
+  }
+}
+
 bool router_small_ok(int64_t T, int H) { return T <= kRouterSmallTokens && H % 4 == 0; }
 
 int launch_router_small(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H,
                         int E, float* logits, cudaStream_t st) {
   AL_CHECK(router_small_ok(T, H), ARTLITE_EINVAL, "router_small: T %lld H %d", (long long)T, H);
   if (T == 0) return ARTLITE_OK;
+  if (H % 256 == 0 && T <= 16)
+    return launch_pdl(router_cta_kernel, dim3((unsigned)E), dim3(256), 0, st, x, x_dtype, w, w_dtype, bias, T, H, E,
+                      logits);
   const int64_t warps = T * E;
   const unsigned grid = (unsigned)std::min<int64_t>(cdiv(warps, 8), (int64_t)kNumSMs * 8);
   return launch_pdl(router_small_kernel, dim3(grid), dim3(256), 0, st, x, x_dtype, w, w_dtype, bias, T, H, E, logits);
