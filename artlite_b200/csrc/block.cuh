@@ -58,6 +58,10 @@ struct artlite_moe {
   int ep_chunks = 1;
   cudaEvent_t ep_ev[2 + 2 * kEpChunks] = {};  // rows gathered, returns in, per chunk: rows in, outputs ready
   artlite::DevBuf ep_rcounts, ep_loff, ep_lcounts, ep_wexp, ep_ident, xr, ys;
+  artlite::DevBuf ep_idx, xe;          // the regroup's row maps (2 x ep_max_rows) and expert-major rows
+  int32_t* hb_idx = nullptr;           // pinned: the same maps, built on the host
+  int ep_regroup = -1;                 // rows regrouped expert-major before the experts: -1 from 8 ranks, 0 no, 1 yes
+  std::vector<int64_t> ep_xoff;        // [E_local + 1] the expert-major groups' offsets
   int32_t* hb_counts = nullptr;        // pinned: [E] this rank's pairs per expert, then [world x E_local] received
   int64_t* hb_loff = nullptr;          // pinned: [world E_local + 1] the received row groups' offsets
   int32_t* hb_lcounts = nullptr;       // pinned: [world E_local] their rows

@@ -12,7 +12,11 @@
 //   5. the local experts run on the receive buffer's W x (E / W) (source, expert) row groups, each in place against its
 //      expert's weights (run_experts with a weight-expert map), no regrouping copy: at W = 2 the own groups first,
 //      while the rows travel, then the peer's; at W >= 4 (the own block a small share) one run over all groups once
-//      the rows are in; with ARTLITE_EP_CHUNKS > 1 the peers' groups in expert chunks, each run as its rows land;
+//      the rows are in; with ARTLITE_EP_CHUNKS > 1 the peers' groups in expert chunks, each run as its rows land.
+//      From 8 ranks on the tcgen05 path (ARTLITE_EP_REGROUP=1 / 0 forces it on / off) the received rows are first
+//      gathered into expert-major order (index maps built on the host from the counts), each local expert one row
+//      group, so that its weights are dequantised once per full 256-token tile rather than once per source's half
+//      tile, and the outputs are gathered back into the receive order;
 //   6. the outputs returned by one message per peer, each landing as the contiguous block of the source rank's dispatch
 //      order it came from; the rank's own block stays where its experts wrote it;
 //   7. the weighted combine of the rank's own tokens, its own rows read from the expert outputs (combine.cu).
@@ -113,6 +117,8 @@ int ep_create(artlite_moe* h) {
   AL_TRY(h->ep_wexp.reserve(sizeof(int32_t) * E));        // their weight experts: group q El + e -> e
   AL_TRY(h->ep_ident.reserve(sizeof(int32_t) * R));
   AL_TRY(h->xr.reserve(sizeof(uint16_t) * (R + 256) * H));  // (the tcgen05 path reads 256-row boxes)
+  AL_TRY(h->xe.reserve(sizeof(uint16_t) * (R + 256) * H));
+  AL_TRY(h->ep_idx.reserve(sizeof(int32_t) * 2 * R));
   AL_TRY(h->ys.reserve(sizeof(float) * T * K * H));
   // the expert workspaces hold the received rows (h: fp32 or bf16 with 256 spare rows; y: fp32 or bf16)
   AL_TRY(h->h.reserve(std::max(sizeof(float) * R * F, sizeof(uint16_t) * (R + 256) * F)));
@@ -123,6 +129,9 @@ int ep_create(artlite_moe* h) {
   AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_counts), sizeof(int32_t) * 2 * E, cudaHostAllocDefault));
   AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_loff), sizeof(int64_t) * (E + 1), cudaHostAllocDefault));
   AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_lcounts), sizeof(int32_t) * E, cudaHostAllocDefault));
+  AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_idx), sizeof(int32_t) * 2 * R, cudaHostAllocDefault));
+  h->ep_xoff.assign(El + 1, 0);
+  if (const char* ev = std::getenv("ARTLITE_EP_REGROUP")) h->ep_regroup = ev[0] == '0' ? 0 : 1;
   h->ep_send_base.assign(W, 0);
   h->ep_recv_base.assign(W, 0);
   h->ep_send_rows.assign(W, 0);
@@ -171,6 +180,8 @@ void ep_destroy(artlite_moe* h) {
   if (h->hb_counts) cudaFreeHost(h->hb_counts);
   if (h->hb_loff) cudaFreeHost(h->hb_loff);
   if (h->hb_lcounts) cudaFreeHost(h->hb_lcounts);
+  if (h->hb_idx) cudaFreeHost(h->hb_idx);
+  h->hb_idx = nullptr;
   h->hb_counts = nullptr;
   h->hb_loff = nullptr;
   h->hb_lcounts = nullptr;
@@ -294,6 +305,39 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
            (long long)Rl, (long long)h->ep_max_rows);
   AL_CHECK(send_rows[r] == recv_rows[r], ARTLITE_EDEVICE, "expert parallelism: own block %lld / %lld rows",
            (long long)send_rows[r], (long long)recv_rows[r]);
+  const int path = expert_path(*h, Rl, L);
+  h->last_path = path;
+  h->paths[layer] = path;
+  // Regroup (tcgen05 path, one chunk; by default from 8 ranks, where a (source, expert) group averages about half a
+  // 256-token tile): the received rows gathered into expert-major order, so that each local expert is one row group
+  // and its weights are dequantised once per full tile instead of once per source; the outputs gathered back.
+  const bool regroup = C == 1 && path == 2 && (h->ep_regroup > 0 || (h->ep_regroup < 0 && W >= 8));
+  if (regroup) {
+    int32_t* idx = h->hb_idx;                     // expert-major row -> receive-buffer row
+    int32_t* inv = h->hb_idx + h->ep_max_rows;    // receive-buffer row -> expert-major row
+    int64_t i = 0;
+    for (int e = 0; e < El; e++) {
+      h->ep_xoff[e] = i;
+      for (int qi = 0; qi < W; qi++) {  // (group qi El + e: the peers' (qi < W - 1), then the own block's)
+        const int j = qi * El + e;
+        for (int64_t m = 0; m < h->hb_lcounts[j]; m++, i++) {
+          idx[i] = (int32_t)(h->hb_loff[j] + m);
+          inv[h->hb_loff[j] + m] = (int32_t)i;
+        }
+      }
+    }
+    h->ep_xoff[El] = i;
+    for (int e = 0; e < El; e++) {
+      h->hb_loff[e] = h->ep_xoff[e];
+      h->hb_lcounts[e] = (int32_t)(h->ep_xoff[e + 1] - h->ep_xoff[e]);
+    }
+    h->hb_loff[El] = i;
+    if (Rl) {
+      AL_CUDA(cudaMemcpyAsync(h->ep_idx.ptr, idx, sizeof(int32_t) * Rl, cudaMemcpyHostToDevice, st));
+      AL_CUDA(cudaMemcpyAsync(h->ep_idx.as<int32_t>() + h->ep_max_rows, inv, sizeof(int32_t) * Rl,
+                              cudaMemcpyHostToDevice, st));
+    }
+  }
   AL_CUDA(cudaMemcpyAsync(h->ep_loff.ptr, h->hb_loff, sizeof(int64_t) * (E + 1), cudaMemcpyHostToDevice, st));
   AL_CUDA(cudaMemcpyAsync(h->ep_lcounts.ptr, h->hb_lcounts, sizeof(int32_t) * E, cudaMemcpyHostToDevice, st));
   // 3: the rows in dispatch order: the peers' blocks into the send buffer, this rank's own block into its place in the
@@ -325,9 +369,6 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   }
   // 5: the local experts in place: the own groups while the rows travel, then each chunk of the peers' groups once its
   // rows are in, its outputs handed to the exchange stream
-  const int path = expert_path(*h, Rl, L);
-  h->last_path = path;
-  h->paths[layer] = path;
   void* yrows = nullptr;
   int ydt = 0;
   const int64_t* goff = h->ep_loff.as<int64_t>();
@@ -338,26 +379,41 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   Marker quiet{h, layer, st};
   quiet.ns = kStages;  // (no stage events inside the expert calls)
   const int jo = (W - 1) * El;
-  if (W == 2) {  // the own groups while the rows travel, then the peer's (at N >= 4 the own block is too small a share
-                 // to hide the exchange behind, and one launch over all groups costs less than two)
-    AL_TRY(run_experts(h, routed_weights(L), path, xr, ARTLITE_BF16, true, ident, 1, recv_rows[r], El, goff + jo,
-                       gcnt + jo, xr_rows, &yrows, &ydt, st, quiet, false, gexp + jo, El));
+  if (regroup) {  // every row in: gathered expert-major, the experts, the outputs gathered back into xr's order
+    AL_CUDA(cudaStreamWaitEvent(st, ev_r[0], 0));
+    uint16_t* xe = h->xe.as<uint16_t>();
+    const int32_t* idx = h->ep_idx.as<int32_t>();
+    if (Rl) AL_TRY(launch_gather(xr, ARTLITE_BF16, idx, Rl, 1, H, xe, st, nullptr, 0, 0));
+    AL_TRY(mk.mark());
+    AL_TRY(run_experts(h, routed_weights(L), path, xe, ARTLITE_BF16, true, ident, 1, Rl, El, goff, gcnt,
+                       (int64_t)(h->xe.bytes / (2 * H)), &yrows, &ydt, st, quiet, false, gexp + jo, El));
+    AL_CHECK(ydt == ARTLITE_BF16, ARTLITE_EUNSUPPORTED, "expert parallelism: regrouped outputs of type %d", ydt);
+    if (Rl) AL_TRY(launch_gather(yrows, ARTLITE_BF16, idx + h->ep_max_rows, Rl, 1, H, xr, st, nullptr, 0, 0));
+    yrows = xr;
+    AL_CUDA(cudaEventRecord(ev_y[0], st));
+    AL_TRY(mk.mark());
+  } else {
+    if (W == 2) {  // the own groups while the rows travel, then the peer's (at N >= 4 the own block is too small a
+                   // share to hide the exchange behind, and one launch over all groups costs less than two)
+      AL_TRY(run_experts(h, routed_weights(L), path, xr, ARTLITE_BF16, true, ident, 1, recv_rows[r], El, goff + jo,
+                         gcnt + jo, xr_rows, &yrows, &ydt, st, quiet, false, gexp + jo, El));
+    }
+    AL_TRY(mk.mark());
+    const int Gc = (W - 1) * Ec;  // groups a chunk
+    for (int c = 0; c < C; c++) {
+      AL_CUDA(cudaStreamWaitEvent(st, ev_r[c], 0));
+      int64_t rows = 0;
+      for (int q = 0; q < W; q++)
+        if (q != r) rows += h->ep_cr_rows[(size_t)q * C + c];
+      const int ng = Gc + (W == 2 || c < C - 1 ? 0 : El);  // (N >= 4: the last chunk's run takes the own groups too)
+      if (W != 2 && c == C - 1) rows += recv_rows[r];
+      if (ng)
+        AL_TRY(run_experts(h, routed_weights(L), path, xr, ARTLITE_BF16, true, ident, 1, rows, ng, goff + c * Gc,
+                           gcnt + c * Gc, xr_rows, &yrows, &ydt, st, quiet, false, gexp + c * Gc, El));
+      AL_CUDA(cudaEventRecord(ev_y[c], st));
+    }
+    AL_TRY(mk.mark());
   }
-  AL_TRY(mk.mark());
-  const int Gc = (W - 1) * Ec;  // groups a chunk
-  for (int c = 0; c < C; c++) {
-    AL_CUDA(cudaStreamWaitEvent(st, ev_r[c], 0));
-    int64_t rows = 0;
-    for (int q = 0; q < W; q++)
-      if (q != r) rows += h->ep_cr_rows[(size_t)q * C + c];
-    const int ng = Gc + (W == 2 || c < C - 1 ? 0 : El);  // (N >= 4: the last chunk's run takes the own groups too)
-    if (W != 2 && c == C - 1) rows += recv_rows[r];
-    if (ng)
-      AL_TRY(run_experts(h, routed_weights(L), path, xr, ARTLITE_BF16, true, ident, 1, rows, ng, goff + c * Gc,
-                         gcnt + c * Gc, xr_rows, &yrows, &ydt, st, quiet, false, gexp + c * Gc, El));
-    AL_CUDA(cudaEventRecord(ev_y[c], st));
-  }
-  AL_TRY(mk.mark());
   // 6: the outputs back, chunk by chunk, each landing as the block of the source's dispatch order it came from
   const size_t el = ydt == ARTLITE_BF16 ? 2 : 4;
   const ncclDataType_t dt = ydt == ARTLITE_BF16 ? ncclBfloat16 : ncclFloat32;

@@ -1,6 +1,8 @@
 """Expert parallelism on 2 and 4 GPUs (NCCL, one process per GPU): each rank owns 1/N of the experts and its own tokens;
 the EP forward (token rows out by NCCL send / recv, local tcgen05 or GEMV experts, outputs back, local combine) must
-equal, on every rank, the single-GPU block over the same tokens with all experts. Skipped with fewer GPUs than ranks.
+equal, on every rank, the single-GPU block over the same tokens with all experts, with one or four expert chunks and
+with the rows regrouped expert-major before the experts (the default from 8 ranks, forced here). Skipped with fewer
+GPUs than ranks.
 NVLS is off (NCCL_NVLS_ENABLE=0); the ranks are child processes."""
 
 import os
@@ -13,9 +15,10 @@ pytestmark = pytest.mark.gpu
 H, E, K, F = 512, 16, 4, 256
 
 
-def _rank(rank, world, uid, path, T, Tmax, chunks, q):
+def _rank(rank, world, uid, path, T, Tmax, chunks, regroup, q):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     os.environ["ARTLITE_EP_CHUNKS"] = str(chunks)
+    os.environ["ARTLITE_EP_REGROUP"] = regroup
     os.environ["ARTLITE_EP_TIMEOUT_MS"] = "20000"
     import torch
     torch.cuda.set_device(rank)
@@ -41,8 +44,9 @@ def _rank(rank, world, uid, path, T, Tmax, chunks, q):
 
 
 @pytest.mark.parametrize("world", [2, 4])
-@pytest.mark.parametrize("path,T,chunks", [("tc", 300, 1), ("tc", 300, 4), ("gemv", 7, 1)])
-def test_ep_matches_single_gpu(path, T, chunks, world):
+@pytest.mark.parametrize("path,T,chunks,regroup", [("tc", 300, 1, "0"), ("tc", 300, 4, "0"), ("tc", 300, 1, "1"),
+                                                   ("gemv", 7, 1, "0")])
+def test_ep_matches_single_gpu(path, T, chunks, regroup, world):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < world:
@@ -52,7 +56,7 @@ def test_ep_matches_single_gpu(path, T, chunks, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     Tmax = T + 13 * (world - 1)
-    procs = [ctx.Process(target=_rank, args=(r, world, uid, path, T + 13 * r, Tmax, chunks, q), daemon=True)
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, path, T + 13 * r, Tmax, chunks, regroup, q), daemon=True)
              for r in range(world)]
     for p in procs:
         p.start()
