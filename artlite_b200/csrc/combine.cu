@@ -47,6 +47,9 @@ __device__ __forceinline__ void store8(void* base, int dtype, int64_t i, const f
 }  // namespace
 
 // one CTA per token row, 8 values per thread (H % 8 == 0)
+// kGrouped: four pairs' loads in flight at once (decode-sized batches, where latency dominates; it takes more
+// registers, which costs a large batch its occupancy: the per-pair loop there)
+template <bool kGrouped>
 __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype, const int32_t* slot, const float* w,
                                                       int64_t T, int k, int H, void* out, int out_dtype, CombineOwn own,
                                                       CombineShared sh) {
@@ -55,7 +58,20 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype
   const int64_t t = blockIdx.x;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int i0 = 0; i0 < k; i0 += 4) {  // (four pairs' loads in flight at once; the sum keeps the pair order)
+    if (!kGrouped) {
+      for (int i = 0; i < k; i++) {
+        const float wi = w[t * k + i];
+        const int64_t sl = slot[t * k + i];
+        float v[8];
+        if (own.own && sl >= own.own_lo && sl < own.own_hi)
+          load8(own.own, y_dtype, (sl - own.own_lo) * H + c, v);
+        else
+          load8(y, y_dtype, sl * H + c, v);
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[j] = fmaf(wi, v[j], acc[j]);
+      }
+    }
+    for (int i0 = 0; kGrouped && i0 < k; i0 += 4) {  // (four pairs' loads in flight at once; the sum keeps the pair order)
       float wi[4], v[4][8];
       int64_t sl[4];
 #pragma unroll
@@ -91,8 +107,11 @@ int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float*
                    int out_dtype, cudaStream_t st, CombineOwn own, CombineShared sh) {
   AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "combine: H %d (a multiple of 8)", H);
   if (T == 0) return ARTLITE_OK;
-  return launch_pdl(combine_kernel, dim3((unsigned)T), dim3(256), 0, st, y, y_dtype, slot, w, T, k, H, out, out_dtype,
-                    own, sh);
+  if (T <= 64)
+    return launch_pdl(combine_kernel<true>, dim3((unsigned)T), dim3(256), 0, st, y, y_dtype, slot, w, T, k, H, out,
+                      out_dtype, own, sh);
+  return launch_pdl(combine_kernel<false>, dim3((unsigned)T), dim3(256), 0, st, y, y_dtype, slot, w, T, k, H, out,
+                    out_dtype, own, sh);
 }
 
 // a grid-stride loop over 16-byte chunks of the output rows (8 values each): row i of xp = token perm[i] / k of x
