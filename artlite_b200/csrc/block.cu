@@ -131,10 +131,23 @@ int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* 
 
 // The decode-sized plan of a forward: both GEMVs' items per expert and token group (0, 0 when the fused routing /
 // dispatch kernel does not apply).
+bool mss_use(const artlite_moe& h, const ExpertWeights& W, int path, int x_dtype, int F) {
+  static const bool off = [] {
+    const char* v = getenv("ARTLITE_DECODE_MSS");
+    return v && v[0] == '0';
+  }();
+  return !off && path == 1 && W.ss_gate && mss_ok(W.qtype, W.down_qtype, x_dtype, h.d.hidden, F, true);
+}
+
 void small_plan(const artlite_moe& h, const artlite_moe::Layer& L, int path, int64_t T, int* mult_gu, int* mult_dn) {
   const artlite_moe_desc& d = h.d;
   *mult_gu = *mult_dn = 0;
   if (path != 1 || T <= 0 || !small_dispatch_ok(T * d.top_k, d.n_experts) || !router_small_ok(T, d.hidden)) return;
+  if (mss_use(h, routed_weights(L), path, d.act_dtype, d.expert_ffn)) {
+    *mult_gu = mss_mult_gu(d.expert_ffn);
+    *mult_dn = mss_mult_dn(d.hidden);
+    return;
+  }
   const int rt_gu = gemv_row_tile(L.qtype, d.hidden, d.expert_ffn, true);
   const int rt_dn = gemv_row_tile(L.down_qtype, d.expert_ffn, d.hidden, false);
   if (rt_gu <= 0 || rt_dn <= 0) return;
@@ -149,6 +162,36 @@ int run_experts(artlite_moe* h, const ExpertWeights& L, int path, const void* x,
   const artlite_moe_desc& d = h->d;
   const int H = d.hidden, F = F_run > 0 ? F_run : d.expert_ffn;
   *y_rows = y_out ? y_out : h->y.ptr;
+  if (path == 1 && !wexp && mss_use(*h, L, path, x_dtype, F)) {  // the small-batch tensor-core GEMVs (no row-group map)
+    *y_dtype = ARTLITE_F32;
+    if (P == 0) return ARTLITE_OK;
+    if (!units_ready) {
+      AL_TRY(launch_unit_scan(counts, E_run, kGemvTokens, mss_mult_gu(F), h->unit_gu.as<int32_t>(), st));
+      AL_TRY(launch_unit_scan(counts, E_run, kGemvTokens, mss_mult_dn(H), h->unit_dn.as<int32_t>(), st));
+    }
+    MssLaunch s{};
+    s.gate_map = L.ss_gate;
+    s.up_map = L.ss_up;
+    s.down_map = L.ss_down;
+    s.H = H;
+    s.F = F;
+    s.E = E_run;
+    s.k = k;
+    s.x = x;
+    s.hq = h->h.as<uint4>();
+    s.hs = reinterpret_cast<float*>(h->h.as<uint8_t>() + sizeof(uint16_t) * P * F);
+    s.y = static_cast<float*>(*y_rows);
+    s.unit_gu = h->unit_gu.as<int32_t>();
+    s.unit_dn = h->unit_dn.as<int32_t>();
+    s.offsets = offsets;
+    s.perm = perm;
+    s.slots = (int)std::min<int64_t>(kGemvTokens, k > 1 ? P / k : P);  // (a token's k pairs go to distinct experts)
+    s.status = h->status.as<DevStatus>();
+    AL_TRY(launch_mss(s, true, st));
+    AL_TRY(mk.mark());
+    AL_TRY(launch_mss(s, false, st));
+    return mk.mark();
+  }
   if (path == 1) {
     *y_dtype = ARTLITE_F32;
     if (P == 0) return ARTLITE_OK;
@@ -375,6 +418,12 @@ int artlite_moe_set_weights(artlite_moe* h, int layer, int qtype, const void* ga
     AL_TRY(make_raw_map(&L.dm_up, L.up.ptr, L.rb_gu, h->E_local * F, 144, 64));
     AL_TRY(make_raw_map(&L.dm_down, L.down.ptr, L.rb_dn, h->E_local * H, 144, 128));
     L.has_dm = true;
+  }
+  L.has_ss = false;
+  if (L.has_dm && F % 32 == 0) {
+    AL_TRY(make_raw_map(&L.ss_gate, L.gate.ptr, L.rb_gu, h->E_local * F, 144, 32));
+    AL_TRY(make_raw_map(&L.ss_up, L.up.ptr, L.rb_gu, h->E_local * F, 144, 32));
+    L.has_ss = true;
   }
   L.n_planes = 0;
   if (router_tc_supported(d.n_experts, d.hidden, d.act_dtype)) {

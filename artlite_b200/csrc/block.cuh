@@ -24,6 +24,9 @@ struct artlite_moe {
     // one 144-byte super-block wide)
     bool has_dm = false;
     CUtensorMap dm_gate, dm_up, dm_down;
+    // and for the small-batch GEMVs (mss.cu): gate / up boxes of 32 rows (down: dm_down)
+    bool has_ss = false;
+    CUtensorMap ss_gate, ss_up;
     // the shared expert (artlite_moe_set_shared): raw rows of one SwiGLU expert of width sh_F, and its gate vector
     bool has_shared = false, sh_has_gate = false;
     int sh_F = 0, sh_qtype = -1, sh_down_qtype = -1, sh_gate_dtype = -1;
@@ -99,14 +102,19 @@ struct ExpertWeights {
   int qtype, down_qtype;
   const uint8_t *gate, *up, *down;
   int64_t rb_gu, rb_dn;
+  const CUtensorMap *ss_gate, *ss_up, *ss_down;  // the small-batch GEMVs' maps (null: none)
 };
 inline ExpertWeights routed_weights(const artlite_moe::Layer& L) {
-  return {L.qtype, L.down_qtype, L.gate.as<uint8_t>(), L.up.as<uint8_t>(), L.down.as<uint8_t>(), L.rb_gu, L.rb_dn};
+  const bool ss = L.has_ss && L.has_dm;
+  return {L.qtype, L.down_qtype, L.gate.as<uint8_t>(), L.up.as<uint8_t>(), L.down.as<uint8_t>(), L.rb_gu, L.rb_dn,
+          ss ? &L.ss_gate : nullptr, ss ? &L.ss_up : nullptr, ss ? &L.dm_down : nullptr};
 }
 inline ExpertWeights shared_weights(const artlite_moe::Layer& L) {
   return {L.sh_qtype, L.sh_down_qtype, L.sh_gate.as<uint8_t>(), L.sh_up.as<uint8_t>(), L.sh_down.as<uint8_t>(),
-          L.sh_rb_gu, L.sh_rb_dn};
+          L.sh_rb_gu, L.sh_rb_dn, nullptr, nullptr, nullptr};
 }
+// the small-batch tensor-core GEMVs apply (GEMV path, Q4_K with maps, bf16 x; ARTLITE_DECODE_MSS=0 turns them off)
+bool mss_use(const artlite_moe& h, const ExpertWeights& W, int path, int x_dtype, int F);
 
 // router logits, routing and the dispatch over all E experts of T tokens x (device, act dtype) into the handle's
 // logits / ids / w / offsets / perm / slot / counts

@@ -1,6 +1,7 @@
 // Kernel argument blocks and launchers of libartlite_moe_cuda.so (one definition per .cu file).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -139,5 +140,26 @@ int launch_shared_gate(const void* x, int x_dtype, const void* g, int g_dtype, i
 // go to own_dst + (i - own_lo) rows instead (own_dst null: all to xp)
 int launch_gather(const void* x, int x_dtype, const int32_t* perm, int64_t P, int k, int H, uint16_t* xp,
                   cudaStream_t st, uint16_t* own_dst = nullptr, int64_t own_lo = 0, int64_t own_hi = 0);
+
+// ---------------------------------------------------------------- mss.cu
+// The small-batch tensor-core GEMVs (Q4_K, bf16 x): gate / up items of 32 output rows into h (fragment order + group
+// sums: hq, hs), down items of 128 output rows into fp32 y, both over the dispatch's pair groups of <= 8.
+struct MssLaunch {
+  const CUtensorMap *gate_map, *up_map, *down_map;  // raw rows: gate / up boxes of 32 rows, down boxes of 128 rows
+  int H, F, E, k;
+  const void* x;  // bf16 token rows; pair d's row is perm[d] / k
+  uint4* hq;      // h of the pairs in fragment order (F / 32 groups a row), then
+  float* hs;      // their group sums
+  float* y;       // fp32 output rows (pairs x H)
+  const int32_t *unit_gu, *unit_dn;  // items per expert (exclusive scans: mss_mult_* x ceil(pairs / 8))
+  const int64_t* offsets;
+  const int32_t* perm;
+  int slots;  // token slots to stage: min(8, the most pairs an expert can get)
+  DevStatus* status;
+};
+bool mss_ok(int qtype, int down_qtype, int x_dtype, int H, int F, bool has_maps);
+int mss_mult_gu(int F);
+int mss_mult_dn(int H);
+int launch_mss(const MssLaunch& s, bool gu, cudaStream_t st);
 
 }  // namespace artlite
