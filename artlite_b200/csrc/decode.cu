@@ -1,5 +1,5 @@
-// The fused decode-batch forward: one cooperative kernel per layer for small batches on the GEMV path (8 <= T,
-// T k <= 512 pairs, E <= 256, Q4_0 / Q8_0 / Q4_K weights, one type for gate / up / down, no shared expert). It runs
+// The fused decode-batch forward: one cooperative kernel per layer for small batches on the GEMV path (8 <= T, or
+// 16 <= T where the small-batch tensor-core GEMVs of mss.cu apply; T k <= 512 pairs, E <= 256, Q4_0 / Q8_0 / Q4_K weights, one type for gate / up / down, no shared expert). It runs
 // the same steps as the separate kernels of a forward, in phases separated by grid barriers:
 //   1. router logits (router.cu's semantics: fp32 products, fp32 sums, + bias): register-blocked 4 tokens x 4 experts
 //      a warp over a quarter of H (router_tiles), or a warp per (token, expert) for other shapes; for Q4_K also the
@@ -437,13 +437,16 @@ bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t 
     const char* v = getenv("ARTLITE_DECODE_FUSED");
     return v && v[0] == '0';
   }();
-  static const int64_t t_min = [] {  // (ARTLITE_DECODE_FUSED_MIN: the smallest batch that takes the fused kernel)
+  static const int64_t t_set = [] {  // (ARTLITE_DECODE_FUSED_MIN: the smallest batch that takes the fused kernel)
     const char* v = getenv("ARTLITE_DECODE_FUSED_MIN");
     const int64_t m = v ? atoll(v) : 0;
-    return m >= 1 ? m : (int64_t)8;
+    return m >= 1 ? m : (int64_t)0;
   }();
   const artlite_moe_desc& d = h.d;
-  // (below 8 tokens the separate kernels, whose GEMV spreads finer items over the whole grid, are faster)
+  // below the threshold the separate kernels, whose GEMVs spread finer items over the whole grid, are faster: below 8
+  // tokens with the register-decoding GEMVs, below 16 with the small-batch tensor-core ones (measured at B = 8: 110 us
+  // against the fused kernel's 117; at B = 16: 170 against 161)
+  const int64_t t_min = t_set ? t_set : mss_use(h, routed_weights(L), 1, d.act_dtype, d.expert_ffn) ? 16 : 8;
   return !off && !L.has_shared && T >= t_min && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts && h.E_local == d.n_experts &&
          rq_type(L.qtype) && L.down_qtype == L.qtype && d.hidden % 256 == 0 && d.expert_ffn % 256 == 0 &&
          gemv_rq_rows_per_warp(L.qtype, d.hidden, true) > 0 && gemv_rq_rows_per_warp(L.down_qtype, d.expert_ffn, false) > 0 &&

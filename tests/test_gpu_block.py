@@ -54,9 +54,10 @@ def test_config1_fp32(golden):
     assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= FP32_TOL
 
 
-@pytest.mark.parametrize("B", [1, 4, 16, 64])
+@pytest.mark.parametrize("B", [1, 4, 12, 16, 64])
 def test_decode_q4k(B):
-    """Config 2's decode batches (Q4_K, bf16 x) on the dequant-GEMV path."""
+    """Config 2's decode batches (Q4_K, bf16 x) on the dequant-GEMV path: below 16 tokens the small-batch tensor-core
+    GEMVs (12: every token slot staged), from 16 the fused decode kernel."""
     layer, x, _ = moe_np.make_block(B, B, qtype="Q4_K")
     y, dbg = run(layer, x, act="bf16", path="gemv", T=B)
     ids, w = check_routing(dbg, x, layer, 8)
