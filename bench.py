@@ -1,9 +1,9 @@
-"""MoE-layer tokens/s of the GGUF MoE block on B200 (a 48-layer stack of Qwen3-30B-A3B-shape
+"""MoE-layer tokens/s of the GGUF MoE block on B200 (benchmark config 4: a 48-layer stack of Qwen3-30B-A3B-shape
 blocks, H=2048, E=128, top-8, F=768, Q4_0 weights, 16384 tokens), and the CPU reference arm.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-    python bench.py --decode            BASELINE config 2 (decode batches 1 / 4 / 16 / 64, Q4_K), one line per batch
-    python bench.py --config 3 | 5      BASELINE config 3 (prefill, Q8_0, Zipf-skewed routing) or 5 (Qwen3-235B-A22B
+    python bench.py --decode            benchmark config 2 (decode batches 1 / 4 / 16 / 64, Q4_K), one line per batch
+    python bench.py --config 3 | 5      benchmark config 3 (prefill, Q8_0, Zipf-skewed routing) or 5 (Qwen3-235B-A22B
                                         shape: H 4096, F 1536, Q4_0, 8192-token prefill and a 64-token decode batch)
 
 One step = one forward of every layer of the stack over the step's token batch (the layers are independent blocks,
@@ -199,7 +199,7 @@ def gen_layer_q4k(torch, g, dev):
 
 
 def gen_q(torch, g, dev, qtype, rows, cols):
-    """Raw GGUF rows of `qtype` on the GPU with BASELINE's distributions (fp16 scales |N(0, 0.02)|; Q4_0 nibbles
+    """Raw GGUF rows of `qtype` on the GPU with the benchmark's distributions (fp16 scales |N(0, 0.02)|; Q4_0 nibbles
     uniform; Q8_0 int8 uniform -127..127)."""
     if qtype == "Q4_0":
         n = cols // 32
@@ -218,7 +218,7 @@ def gen_q(torch, g, dev, qtype, rows, cols):
 
 
 def run_config(args) -> None:
-    """BASELINE configs 3 and 5 on one GPU, --layers layers of independent weights in turn (one JSON line per measured
+    """benchmark configs 3 and 5 on one GPU, --layers layers of independent weights in turn (one JSON line per measured
     shape): tokens x layers / s, ms per layer, and the gate/up GEMM's share of the tensor roofline (tcgen05 path)."""
     import torch
     from artlite_b200.moe.block import MoEBlock
@@ -291,7 +291,7 @@ def run_config(args) -> None:
 
 
 def run_decode(args) -> None:
-    """BASELINE config 2 on one GPU: decode batches B = 1, 4, 16, 64 of the Q4_K block (bf16 x), each forward a CUDA
+    """benchmark config 2 on one GPU: decode batches B = 1, 4, 16, 64 of the Q4_K block (bf16 x), each forward a CUDA
     graph, over --layers layers in turn (their touched experts far exceed L2). One JSON line per B: tokens/s, and the
     HBM roofline of the bytes a forward must read (U touched experts x 2,654,208 B + the fp32 router 1,048,576 B)."""
     import torch
@@ -358,8 +358,8 @@ def main() -> None:
     ap.add_argument("--cpu-tokens", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--decode", action="store_true", help="BASELINE config 2 (decode batches, Q4_K) instead")
-    ap.add_argument("--config", type=int, choices=[3, 5], help="BASELINE config 3 or 5 (one GPU) instead")
+    ap.add_argument("--decode", action="store_true", help="benchmark config 2 (decode batches, Q4_K) instead")
+    ap.add_argument("--config", type=int, choices=[3, 5], help="benchmark config 3 or 5 (one GPU) instead")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"], help="expert path of --decode")
     ap.add_argument("--batches", type=int, nargs="+", default=[1, 4, 16, 64], help="decode batches of --decode")
     args = ap.parse_args()

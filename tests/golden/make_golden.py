@@ -8,9 +8,9 @@ tree; the vectors are committed, so the tests need neither the reference nor thi
   dequant of the same blocks.
 
 Inputs follow the reference's own seeded fixtures (``tests/moe/test_plan.py:18-57``, ``tests/moe/test_route.py:16-26``)
-with BASELINE's E=128 added, and the seeded synthetic blocks of ``oracle.moe_np``.
+with the benchmark's E=128 added, and the seeded synthetic blocks of ``oracle.moe_np``.
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref <the reference's source tree>]
 """
 
 import argparse

@@ -44,7 +44,7 @@ def check_routing(dbg, x, layer, k, gating="softmax", bias=None):
 
 
 def test_config1_fp32(golden):
-    """BASELINE config 1 (T=16, H=2048, E=128, K=8, F=768, Q4_0, fp32 x) against the reference's own moe_ffn output
+    """benchmark config 1 (T=16, H=2048, E=128, K=8, F=768, Q4_0, fp32 x) against the reference's own moe_ffn output
     (tests/golden: ref.moe_route + ref.moe_ffn with gguf-py's dequant)."""
     layer, x, _ = moe_np.make_block(0, 16, qtype="Q4_0", x_bf16=False)
     y, dbg = run(layer, x, act="f32", path="gemv", T=16)
