@@ -17,7 +17,8 @@ QTYPES = {"F32": 0, "F16": 1, "Q4_0": 2, "Q4_1": 3, "Q8_0": 8, "Q4_K": 12, "Q5_K
 # every entry point include/artlite_moe.h declares (tests check the library exports each of them)
 EXPORTS = ("artlite_moe_last_error", "artlite_moe_version", "artlite_moe_route", "artlite_moe_plan",
            "artlite_moe_dispatch", "artlite_moe_dispatch_noalloc", "artlite_dequant_supported", "artlite_dequant_rows", "artlite_moe_create",
-           "artlite_moe_set_weights", "artlite_moe_set_router_bias", "artlite_moe_set_shared", "artlite_moe_forward",
+           "artlite_moe_set_weights", "artlite_moe_set_router_bias", "artlite_moe_set_shared", "artlite_moe_set_norm",
+           "artlite_moe_forward",
            "artlite_moe_forward_graph", "artlite_moe_sync", "artlite_moe_debug",
            "artlite_moe_stage_times", "artlite_moe_path", "artlite_moe_launch_count", "artlite_moe_destroy",
            "artlite_moe_ep_unique_id", "artlite_moe_ep_init", "artlite_moe_ep_plan")
@@ -54,6 +55,7 @@ _SIGS = {
     "artlite_moe_set_weights": ([_P, _I, _I, _P, _P, _I, _P, _P, _I], _I),
     "artlite_moe_set_router_bias": ([_P, _I, _P], _I),
     "artlite_moe_set_shared": ([_P, _I, _I, _I, _P, _P, _I, _P, _P, _I], _I),
+    "artlite_moe_set_norm": ([_P, _I, _P, _I, ctypes.c_double], _I),
     "artlite_moe_forward": ([_P, _I, _P, _P, _I64, _P], _I),
     "artlite_moe_forward_graph": ([_P, _I, _P, _P, _I64, _P], _I),
     "artlite_moe_sync": ([_P, _I], _I),

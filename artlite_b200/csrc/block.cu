@@ -460,14 +460,20 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
   void* yd = y_dev ? y : h->yout.ptr;
   Marker mk{h, layer, st};
   AL_TRY(mk.mark());
+  const void* res = nullptr;  // (a layer with a norm: its input, added back to the output)
+  if (L.has_norm && T > 0) {
+    AL_TRY(launch_norm(xd, d.act_dtype, L.norm_w.ptr, L.norm_dtype, L.norm_eps, T, H, h->xn.ptr, st));
+    res = xd;
+    xd = h->xn.ptr;
+  }
   if (h->E_local < E) {
-    AL_TRY(ep_forward(h, layer, xd, yd, T, st, mk));
+    AL_TRY(ep_forward(h, layer, xd, yd, T, st, mk, res));
   } else {
     const int path = expert_path(*h, P, L);
     h->last_path = path;
     h->paths[layer] = path;
     if (path == 1 && decode_fused_ok(*h, L, T)) {
-      AL_TRY(launch_decode(h, L, xd, yd, T, st));
+      AL_TRY(launch_decode(h, L, xd, yd, T, st, res));
     } else {
       int mult_gu, mult_dn;
       small_plan(*h, L, path, T, &mult_gu, &mult_dn);
@@ -479,7 +485,7 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
       CombineShared sh;
       if (L.has_shared) AL_TRY(run_shared(h, L, xd, T, st, &sh));
       AL_TRY(launch_combine(yrows, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st,
-                            CombineOwn{}, sh));
+                            CombineOwn{}, sh, res));
     }
   }
   AL_TRY(mk.mark());
@@ -512,6 +518,32 @@ int artlite_moe_set_router_bias(artlite_moe* h, int layer, const float* bias) {
   AL_TRY(L.bias.reserve(sizeof(float) * h->d.n_experts));
   AL_CUDA(cudaMemcpyAsync(L.bias.ptr, bias, sizeof(float) * h->d.n_experts, cudaMemcpyDefault, h->st));
   L.has_bias = true;
+  return wait(h->st, 0);
+}
+
+int artlite_moe_set_norm(artlite_moe* h, int layer, const void* w, int w_dtype, double eps) {
+  AL_CHECK(h, ARTLITE_EINVAL, "moe_set_norm: null handle");
+  drop_graphs(h);
+  AL_CHECK(layer >= 0 && layer < (int)h->layers.size(), ARTLITE_EINVAL, "moe_set_norm: layer %d of %d", layer,
+           (int)h->layers.size());
+  AL_CUDA(cudaSetDevice(h->dev));
+  artlite_moe::Layer& L = h->layers[layer];
+  if (!w) {
+    L.has_norm = false;
+    return ARTLITE_OK;
+  }
+  AL_CHECK(w_dtype == ARTLITE_F32 || w_dtype == ARTLITE_BF16, ARTLITE_EINVAL, "moe_set_norm: weight type %d", w_dtype);
+  AL_CHECK(eps >= 0.0, ARTLITE_EINVAL, "moe_set_norm: eps %g", eps);
+  AL_CHECK(h->d.hidden % 8 == 0, ARTLITE_EUNSUPPORTED, "moe_set_norm: H %d (a multiple of 8)", h->d.hidden);
+  const size_t wb = (w_dtype == ARTLITE_F32 ? 4 : 2) * (size_t)h->d.hidden;
+  const size_t act = h->d.act_dtype == ARTLITE_BF16 ? 2 : 4;
+  const int64_t T = h->d.max_tokens > 0 ? h->d.max_tokens : 1;
+  AL_TRY(L.norm_w.reserve(wb));
+  AL_TRY(h->xn.reserve(act * T * h->d.hidden));
+  AL_CUDA(cudaMemcpyAsync(L.norm_w.ptr, w, wb, cudaMemcpyDefault, h->st));
+  L.norm_dtype = w_dtype;
+  L.norm_eps = eps;
+  L.has_norm = true;
   return wait(h->st, 0);
 }
 

@@ -27,6 +27,12 @@ struct artlite_moe {
     // and for the small-batch GEMVs (mss.cu): gate / up boxes of 32 rows (down: dm_down)
     bool has_ss = false;
     CUtensorMap ss_gate, ss_up;
+    // RMSNorm of the input before the router and the experts, and the input added back to the output as the residual
+    // (artlite_moe_set_norm): the norm weight (H values of norm_dtype) and eps
+    bool has_norm = false;
+    int norm_dtype = -1;
+    double norm_eps = 0;
+    artlite::DevBuf norm_w;
     // the shared expert (artlite_moe_set_shared): raw rows of one SwiGLU expert of width sh_F, and its gate vector
     bool has_shared = false, sh_has_gate = false;
     int sh_F = 0, sh_qtype = -1, sh_down_qtype = -1, sh_gate_dtype = -1;
@@ -37,6 +43,7 @@ struct artlite_moe {
   // workspaces
   artlite::DevBuf xin, yout, logits, ids, w, offsets, perm, slot, counts, blk, unit_gu, unit_dn, status;
   artlite::DevBuf h, y, xp, tiles;
+  artlite::DevBuf xn;  // the normed input rows (layers with artlite_moe_set_norm)
   artlite::DevBuf bar;  // the fused decode kernel's grid barrier (zeroed once; left zeroed by every complete run)
   artlite::DevBuf sh_y, sh_s, sh_iota, sh_off;  // the shared expert's outputs (T rows), gates (T), 0..T-1, {0, T} / {T}
   int64_t last_T = 0;
@@ -146,11 +153,13 @@ int wait_deadline(cudaStream_t st, int timeout_ms);
 
 // expert parallelism (ep.cu)
 int ep_create(artlite_moe* h);
-int ep_forward(artlite_moe* h, int layer, const void* x, void* y, int64_t T, cudaStream_t st, Marker& mk);
+int ep_forward(artlite_moe* h, int layer, const void* x, void* y, int64_t T, cudaStream_t st, Marker& mk,
+               const void* res = nullptr);
 void ep_destroy(artlite_moe* h);
 
 // the fused decode-batch forward (decode.cu): whether it applies, and the launch (x, y device, act dtype)
 bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t T);
-int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, void* y, int64_t T, cudaStream_t st);
+int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, void* y, int64_t T, cudaStream_t st,
+                  const void* res = nullptr);
 
 }  // namespace artlite

@@ -49,10 +49,19 @@ __device__ __forceinline__ void store8(void* base, int dtype, int64_t i, const f
 // one CTA per token row, 8 values per thread (H % 8 == 0)
 // kGrouped: four pairs' loads in flight at once (decode-sized batches, where latency dominates; it takes more
 // registers, which costs a large batch its occupancy: the per-pair loop there)
+// the residual's row t, columns c .. c + 7, added last to the fp32 sum (res null: nothing)
+__device__ __forceinline__ void add_res(const void* res, int dtype, int64_t i, float (&acc)[8]) {
+  if (!res) return;
+  float v[8];
+  load8(res, dtype, i, v);
+#pragma unroll
+  for (int j = 0; j < 8; j++) acc[j] = __fadd_rn(acc[j], v[j]);
+}
+
 template <bool kGrouped>
 __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype, const int32_t* slot, const float* w,
                                                       int64_t T, int k, int H, void* out, int out_dtype, CombineOwn own,
-                                                      CombineShared sh) {
+                                                      CombineShared sh, const void* res) {
   griddep_wait();
   griddep_launch();
   const int64_t t = blockIdx.x;
@@ -96,6 +105,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype
 #pragma unroll
         for (int j = 0; j < 8; j++) acc[j] = fmaf(si, v[j], acc[j]);
       }
+      add_res(res, out_dtype, t * H + c, acc);
       store8(out, out_dtype, t * H + c, acc);
     }
     return;
@@ -143,19 +153,65 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype
 #pragma unroll
       for (int j = 0; j < 8; j++) acc[j] = fmaf(si, v[j], acc[j]);
     }
+    add_res(res, out_dtype, t * H + c, acc);
     store8(out, out_dtype, t * H + c, acc);
   }
 }
 
 int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float* w, int64_t T, int k, int H, void* out,
-                   int out_dtype, cudaStream_t st, CombineOwn own, CombineShared sh) {
+                   int out_dtype, cudaStream_t st, CombineOwn own, CombineShared sh, const void* res) {
   AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "combine: H %d (a multiple of 8)", H);
   if (T == 0) return ARTLITE_OK;
   if (T <= 64)
     return launch_pdl(combine_kernel<true>, dim3((unsigned)T), dim3(256), 0, st, y, y_dtype, slot, w, T, k, H, out,
-                      out_dtype, own, sh);
+                      out_dtype, own, sh, res);
   return launch_pdl(combine_kernel<false>, dim3((unsigned)T), dim3(256), 0, st, y, y_dtype, slot, w, T, k, H, out,
-                    out_dtype, own, sh);
+                    out_dtype, own, sh, res);
+}
+
+// RMSNorm as the reference's float32 numpy (tests/np_ops.py:27-32): the mean of the squares in float64, x over
+// sqrt(mean + eps) in float64 rounded to float32, times w in float32; a CTA per row, stored in x's dtype
+__global__ void __launch_bounds__(256) norm_kernel(const void* x, int x_dtype, const void* w, int w_dtype, double eps,
+                                                   int H, void* out) {
+  __shared__ double part[8];
+  __shared__ double den;
+  griddep_wait();
+  griddep_launch();
+  const int64_t t = blockIdx.x;
+  double s = 0.0;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    float v[8];
+    load8(x, x_dtype, t * H + c, v);
+#pragma unroll
+    for (int j = 0; j < 8; j++) s = fma((double)v[j], (double)v[j], s);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double tot = 0.0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += part[i];
+    den = sqrt(tot / H + eps);
+  }
+  __syncthreads();
+  const double d = den;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    float v[8], g[8];
+    load8(x, x_dtype, t * H + c, v);
+    load8(w, w_dtype, c, g);
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = __fmul_rn((float)((double)v[j] / d), g[j]);
+    store8(out, x_dtype, t * H + c, v);
+  }
+}
+
+int launch_norm(const void* x, int x_dtype, const void* w, int w_dtype, double eps, int64_t T, int H, void* out,
+                cudaStream_t st) {
+  AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "norm: H %d (a multiple of 8)", H);
+  AL_CHECK(w_dtype == ARTLITE_F32 || w_dtype == ARTLITE_BF16, ARTLITE_EINVAL, "norm: weight type %d", w_dtype);
+  if (T == 0) return ARTLITE_OK;
+  return launch_pdl(norm_kernel, dim3((unsigned)T), dim3(256), 0, st, x, x_dtype, w, w_dtype, eps, H, out);
 }
 
 // a grid-stride loop over 16-byte chunks of the output rows (8 values each): row i of xp = token perm[i] / k of x

@@ -93,6 +93,7 @@ struct DecodeArgs {
   int64_t* offsets;
   int32_t *counts, *perm, *slot;
   float *h, *y;
+  const void* res;  // rows added last to the output (the residual of a layer with a norm), or null
   void* out;
   GridBar* bar;
   DevStatus* status;
@@ -399,6 +400,21 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
         acc[6] = fmaf(wi, y1.z, acc[6]), acc[7] = fmaf(wi, y1.w, acc[7]);
       }
       const int64_t o = (int64_t)t * a.H + c;
+      if (a.res) {  // (the residual, last in the fp32 sum)
+        float r[8];
+        if (a.x_dtype == ARTLITE_BF16) {
+          const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.res) + o));
+          const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; j++) r[2 * j] = __uint_as_float(q[j] << 16), r[2 * j + 1] = __uint_as_float(q[j] & 0xFFFF0000u);
+        } else {
+          const float4* f = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + o);
+          const float4 f0 = __ldg(f), f1 = __ldg(f + 1);
+          r[0] = f0.x, r[1] = f0.y, r[2] = f0.z, r[3] = f0.w, r[4] = f1.x, r[5] = f1.y, r[6] = f1.z, r[7] = f1.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[j] = __fadd_rn(acc[j], r[j]);
+      }
       if (a.x_dtype == ARTLITE_BF16) {
         uint32_t q[4];
 #pragma unroll
@@ -454,7 +470,8 @@ bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t 
          decode_smem(L.qtype, d.hidden, d.expert_ffn) <= 113 * 1024;
 }
 
-int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, void* y, int64_t T, cudaStream_t st) {
+int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, void* y, int64_t T, cudaStream_t st,
+                  const void* res) {
   const artlite_moe_desc& d = h->d;
   if (!h->bar.ptr) {
     AL_TRY(h->bar.reserve(sizeof(GridBar)));
@@ -504,6 +521,7 @@ int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, vo
   a.h = h->h.as<float>();
   a.y = h->y.as<float>();
   a.out = y;
+  a.res = res;
   a.bar = h->bar.as<GridBar>();
   a.status = h->status.as<DevStatus>();
   const size_t smem = decode_smem(L.qtype, d.hidden, d.expert_ffn);

@@ -188,7 +188,8 @@ void ep_destroy(artlite_moe* h) {
 }
 
 namespace {
-int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t T, cudaStream_t st, Marker& mk);
+int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t T, cudaStream_t st, Marker& mk,
+                    const void* res);
 
 int ep_timeout_ms() {
   const char* v = getenv("ARTLITE_EP_TIMEOUT_MS");
@@ -199,10 +200,11 @@ int ep_timeout_ms() {
 
 // The EP forward; any failure once the exchanges have begun aborts the communicator (the peers' next bounded wait
 // then fails too) and leaves the handle unusable for expert parallelism, instead of a rank blocking on a peer forever.
-int ep_forward(artlite_moe* h, int layer, const void* xd, void* yd, int64_t T, cudaStream_t st, Marker& mk) {
+int ep_forward(artlite_moe* h, int layer, const void* xd, void* yd, int64_t T, cudaStream_t st, Marker& mk,
+               const void* res) {
   AL_CHECK(h->comm && !h->ep_failed, ARTLITE_EINVAL,
            "moe_forward: expert parallelism needs artlite_moe_ep_init first (or a previous exchange failed)");
-  const int rc = ep_forward_impl(h, layer, xd, yd, T, st, mk);
+  const int rc = ep_forward_impl(h, layer, xd, yd, T, st, mk, res);
   if (rc != ARTLITE_OK && h->comm) {
     Nccl* N;
     if (nccl(&N) == ARTLITE_OK) N->commAbort(static_cast<ncclComm_t>(h->comm));
@@ -213,7 +215,8 @@ int ep_forward(artlite_moe* h, int layer, const void* xd, void* yd, int64_t T, c
 }
 
 namespace {
-int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t T, cudaStream_t st, Marker& mk) {
+int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t T, cudaStream_t st, Marker& mk,
+                    const void* res) {
   Nccl* N;
   AL_TRY(nccl(&N));
   ncclComm_t comm = static_cast<ncclComm_t>(h->comm);
@@ -440,7 +443,8 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   own.own = yo + recv_base[r] * H * el;
   own.own_lo = send_base[r];
   own.own_hi = send_base[r] + send_rows[r];
-  if (T) AL_TRY(launch_combine(ys, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st, own));
+  if (T) AL_TRY(launch_combine(ys, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st, own,
+                               CombineShared{}, res));
   return ARTLITE_OK;
 }
 }  // namespace

@@ -130,7 +130,11 @@ struct CombineShared {
   const float* s = nullptr;
 };
 int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float* w, int64_t T, int k, int H, void* out,
-                   int out_dtype, cudaStream_t st, CombineOwn own = CombineOwn{}, CombineShared sh = CombineShared{});
+                   int out_dtype, cudaStream_t st, CombineOwn own = CombineOwn{}, CombineShared sh = CombineShared{},
+                   const void* res = nullptr);  // res: rows of out_dtype added last (the residual), or null
+// out = rms_norm(x, w, eps) row by row (T rows of H, x and out of x_dtype; w: H values of w_dtype F32 / BF16)
+int launch_norm(const void* x, int x_dtype, const void* w, int w_dtype, double eps, int64_t T, int H, void* out,
+                cudaStream_t st);
 // the shared expert's gates: s[t] = sigmoid(x_t . g) in fp32 (g: H values of g_dtype F32 / BF16; g = null: 1); also
 // its one row group: off = {0, T}, then the count T (int32) after them
 int launch_shared_gate(const void* x, int x_dtype, const void* g, int g_dtype, int64_t T, int H, float* s,

@@ -96,6 +96,13 @@ class MoEBlock:
                                             QTYPES[down_qtype or qtype], _ptr(keep[2]), _ptr(keep[3]),
                                             QTYPES[gate_dtype]))
 
+    def set_norm(self, layer: int, w, *, eps: float = 1e-6, dtype: str = "F32") -> None:
+        """RMSNorm of layer ``layer``'s input before the router and the experts (np_ops.rms_norm: the mean of the
+        squares in float64), and the input added back to the output as the residual: y = x + moe(rms_norm(x, w, eps)).
+        ``w``: hidden values of ``dtype`` (F32 or BF16), a numpy array or a device pointer; None removes it."""
+        keep = np.ascontiguousarray(w) if isinstance(w, np.ndarray) else w
+        check(lib().artlite_moe_set_norm(self._h, layer, _ptr(keep), QTYPES[dtype], float(eps)))
+
     def set_router_bias(self, layer: int, bias: np.ndarray | None) -> None:
         """A per-expert bias added to the router logits (None: none)."""
         b = None if bias is None else np.ascontiguousarray(bias, np.float32)

@@ -146,6 +146,17 @@ int artlite_moe_set_weights(artlite_moe* h, int layer, int qtype, const void* ga
 int artlite_moe_set_router_bias(artlite_moe* h, int layer, const float* bias);
 
 /*
+ * Layer `layer`'s input norm and residual (the MoE layer's place in the reference's decoder: the post-attention
+ * RMSNorm feeds the router and the experts, GatherNormOperator, src/artlite/moe/gather.py:142-289, and the combined
+ * delta is added back to the residual stream, moe/gather.py:11-17): with a norm weight w (H values of w_dtype
+ * ARTLITE_F32 or ARTLITE_BF16, host or device; NULL removes it) every forward computes
+ *   x_n = rms_norm(x, w, eps) = float32(x / sqrt(mean(x^2) + eps)) * w   (tests/np_ops.py:27-32: the mean in float64)
+ * in the activation dtype, routes and runs the experts on x_n, and returns y = x + the routed (and shared) sum, one
+ * fp32 sum rounded once. Without this call the block has neither (the benchmark's configs have none).
+ */
+int artlite_moe_set_norm(artlite_moe* h, int layer, const void* w, int w_dtype, double eps);
+
+/*
  * Layer `layer`'s shared expert (the reference's ref.shared_expert, tests/moe/ref.py:55-60; llama.cpp's
  * ffn_shexp_gated): raw GGUF rows gate / up = blk.L.ffn_{gate,up}_shexp.weight (ffn rows of H values, qtype), down =
  * blk.L.ffn_down_shexp.weight (H rows of ffn values, down_qtype), and gate_inp = blk.L.ffn_gate_inp_shexp.weight (H

@@ -44,6 +44,15 @@ def sigmoid(x: np.ndarray) -> np.ndarray:
     return np.float32(1) / (np.float32(1) + np.exp(-x))
 
 
+def rms_norm(x: np.ndarray, w: np.ndarray | None, eps: float) -> np.ndarray:
+    """tests/np_ops.py:27-32: x / sqrt(mean(x^2) + eps) * w over the last axis, the mean of the squares in float64,
+    the quotient rounded to float32, then times w in float32."""
+    x = f32(x)
+    ms = np.mean(x.astype(np.float64) ** 2, axis=-1, keepdims=True)
+    y = (x / np.sqrt(ms + eps)).astype(np.float32)
+    return y if w is None else y * f32(w)
+
+
 def softmax(x: np.ndarray) -> np.ndarray:
     x = f32(x)
     e = np.exp(x - x.max(-1, keepdims=True))

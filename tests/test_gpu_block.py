@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from oracle import moe_np
-from tests.moe_helpers import make_block, oracle_y, orc, x_f32
+from tests.moe_helpers import expert_fn, make_block, oracle_y, orc, x_f32
 
 pytestmark = pytest.mark.gpu
 
@@ -232,3 +232,29 @@ def test_forward_graph_matches_forward(path, T):
         b.sync()
         assert np.array_equal(yd.cpu().numpy().view(np.uint16), want)
     b.close()
+
+
+@pytest.mark.parametrize("path,T,act", [("tc", 300, "bf16"), ("gemv", 5, "bf16"), ("gemv", 24, "bf16"), ("gemv", 16, "f32")])
+def test_norm_and_residual(path, T, act):
+    """A layer with its input norm and residual (artlite_moe_set_norm): y = x + moe(rms_norm(x, w, eps)), against
+    np_ops.rms_norm restated and ref.moe_ffn on the normed rows (rounded to the activation dtype, as the block routes
+    and computes on them); the separate kernels, the small-batch and fused decode kernels and the tcgen05 path."""
+    qtype = "Q4_K" if act == "bf16" else "Q4_0"
+    layer, x, _ = moe_np.make_block(80 + T, T, qtype=qtype, E=16, H=512, F=256, x_bf16=act == "bf16")
+    wn = (1.0 + 0.1 * np.random.default_rng(5).standard_normal(layer.H)).astype(np.float32)
+    eps = 1e-6
+    b = make_block(layer, T, act=act, path=path)
+    b.set_norm(0, wn, eps=eps)
+    y = b.forward(x)
+    dbg = b.debug(T)
+    b.close()
+    xf = x_f32(x)
+    xn = moe_np.rms_norm(xf, wn, eps)
+    if act == "bf16":
+        xn = moe_np.bf16_to_f32(moe_np.to_bf16_bits(xn))
+    assert moe_np.rel_max(dbg["logits"], xn @ layer.router.T) < 1e-5
+    ids, w = orc().route(dbg["logits"], 8)
+    assert np.array_equal(dbg["ids"], ids)
+    want = xf + moe_np.moe_ffn(xn, ids, w, expert_fn(layer))
+    got = moe_np.bf16_to_f32(y) if act == "bf16" else y
+    assert moe_np.rel_max(got, want) <= (BF16_TOL if act == "bf16" or path == "tc" else FP32_TOL)
