@@ -559,7 +559,6 @@ int artlite_moe_set_shared(artlite_moe* h, int layer, int ffn, int qtype, const 
     L.has_shared = false;
     return ARTLITE_OK;
   }
-  AL_CHECK(h->E_local == h->d.n_experts, ARTLITE_EUNSUPPORTED, "moe_set_shared: not with expert parallelism");
   AL_CHECK(up && down && ffn > 0, ARTLITE_EINVAL, "moe_set_shared: null up / down or ffn %d", ffn);
   AL_CHECK(!gate_inp || gate_dtype == ARTLITE_F32 || gate_dtype == ARTLITE_BF16, ARTLITE_EINVAL,
            "moe_set_shared: gate type %d (F32 or BF16)", gate_dtype);

@@ -155,6 +155,11 @@ int wait_deadline(cudaStream_t st, int timeout_ms);
 int ep_create(artlite_moe* h);
 int ep_forward(artlite_moe* h, int layer, const void* x, void* y, int64_t T, cudaStream_t st, Marker& mk,
                const void* res = nullptr);
+// the layer's shared expert over all T tokens (its gated rows for the combine); with expert parallelism every rank
+// holds the whole shared expert and runs it on its own tokens
+struct CombineShared;
+int run_shared(artlite_moe* h, const artlite_moe::Layer& L, const void* xd, int64_t T, cudaStream_t st,
+               CombineShared* sh);
 void ep_destroy(artlite_moe* h);
 
 // the fused decode-batch forward (decode.cu): whether it applies, and the launch (x, y device, act dtype)

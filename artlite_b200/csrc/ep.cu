@@ -417,6 +417,10 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
     }
     AL_TRY(mk.mark());
   }
+  // the shared expert on this rank's own tokens (every rank holds all of it), on the main stream while the outputs
+  // travel back
+  CombineShared sh;
+  if (L.has_shared && T > 0) AL_TRY(run_shared(h, L, xd, T, st, &sh));
   // 6: the outputs back, chunk by chunk, each landing as the block of the source's dispatch order it came from
   const size_t el = ydt == ARTLITE_BF16 ? 2 : 4;
   const ncclDataType_t dt = ydt == ARTLITE_BF16 ? ncclBfloat16 : ncclFloat32;
@@ -444,7 +448,7 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   own.own_lo = send_base[r];
   own.own_hi = send_base[r] + send_rows[r];
   if (T) AL_TRY(launch_combine(ys, ydt, h->slot.as<int32_t>(), h->w.as<float>(), T, K, H, yd, d.act_dtype, st, own,
-                               CombineShared{}, res));
+                               sh, res));
   return ARTLITE_OK;
 }
 }  // namespace
