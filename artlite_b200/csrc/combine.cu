@@ -65,51 +65,6 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* y, int y_dtype
   griddep_wait();
   griddep_launch();
   const int64_t t = blockIdx.x;
-  if (!kGrouped && y_dtype == ARTLITE_BF16 && k <= 32) {
-    // bf16 rows (the tensor-core path): the token's pair weights and row addresses staged once for the CTA, then four
-    // pairs' 16-byte loads in flight at a time, kept as raw bf16 words until their FMAs (the same pair order)
-    __shared__ float s_w[32];
-    __shared__ const uint16_t* s_src[32];
-    if (threadIdx.x < k) {
-      const int64_t sl = slot[t * k + threadIdx.x];
-      s_w[threadIdx.x] = w[t * k + threadIdx.x];
-      s_src[threadIdx.x] = (own.own && sl >= own.own_lo && sl < own.own_hi)
-                               ? static_cast<const uint16_t*>(own.own) + (sl - own.own_lo) * H
-                               : static_cast<const uint16_t*>(y) + sl * H;
-    }
-    __syncthreads();
-    for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int i0 = 0; i0 < k; i0 += 4) {
-        uint4 q[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++)
-          if (i0 + u < k) q[u] = __ldcg(reinterpret_cast<const uint4*>(s_src[i0 + u] + c));
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          if (i0 + u < k) {
-            const float wi = s_w[i0 + u];
-            const uint32_t qw[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-              acc[2 * j] = fmaf(wi, __uint_as_float(qw[j] << 16), acc[2 * j]);
-              acc[2 * j + 1] = fmaf(wi, __uint_as_float(qw[j] & 0xFFFF0000u), acc[2 * j + 1]);
-            }
-          }
-        }
-      }
-      if (sh.y) {
-        const float si = sh.s[t];
-        float v[8];
-        load8(sh.y, sh.y_dtype, t * H + c, v);
-#pragma unroll
-        for (int j = 0; j < 8; j++) acc[j] = fmaf(si, v[j], acc[j]);
-      }
-      add_res(res, out_dtype, t * H + c, acc);
-      store8(out, out_dtype, t * H + c, acc);
-    }
-    return;
-  }
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (!kGrouped) {
