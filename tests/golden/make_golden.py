@@ -5,7 +5,8 @@ tree; the vectors are committed, so the tests need neither the reference nor thi
 - the reference's compiled host code ``csrc/artlite/moe_host.cpp`` / ``dequant.cpp`` (``oracle/_ref``, built by
   ``make -C oracle ref``): routing ids / weights, the plan, row dequant;
 - gguf-py (``gguf.quants.dequantize``, the reference's pinned ``gguf>=0.19.0``, pyproject.toml:23) as an independent
-  dequant of the same blocks.
+  dequant of the same blocks;
+- the reference's ``tests/np_ops.py`` ``rms_norm`` (the block's optional input norm).
 
 Inputs follow the reference's own seeded fixtures (``tests/moe/test_plan.py:18-57``, ``tests/moe/test_route.py:16-26``)
 with the benchmark's E=128 added, and the seeded synthetic blocks of ``oracle.moe_np``.
@@ -120,6 +121,13 @@ def main() -> None:
     for arr in (layer.router, x, layer.gate, layer.up, layer.down):
         h.update(np.ascontiguousarray(arr).tobytes())
     g["block_c1_sha256"] = np.frombuffer(h.digest(), np.uint8)
+
+    # --- the block's input norm: the reference's np_ops.rms_norm (tests/np_ops.py:27-32) on seeded rows
+    from tests import np_ops  # noqa: E402
+    rng = np.random.default_rng(11)
+    g["norm_x"] = (3 * rng.standard_normal((16, 2048))).astype(np.float32)
+    g["norm_w"] = (1 + 0.1 * rng.standard_normal(2048)).astype(np.float32)
+    g["norm_y"] = np_ops.rms_norm(g["norm_x"], g["norm_w"], 1e-6)
 
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **g)
     print("wrote", os.path.join(HERE, "golden.npz"), len(g), "arrays")

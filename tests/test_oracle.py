@@ -116,6 +116,13 @@ def test_block_config1(golden, orc):
     assert moe_np.rel_max(y, golden["block_c1_y"]) < 1e-5
 
 
+def test_rms_norm_restatement(golden):
+    """moe_np.rms_norm (the block's optional input norm) equals the reference's np_ops.rms_norm bit for bit on the
+    golden rows (tests/golden/make_golden.py ran the reference's own function)."""
+    y = moe_np.rms_norm(golden["norm_x"], golden["norm_w"], 1e-6)
+    assert y.dtype == np.float32 and np.array_equal(y.view(np.uint32), golden["norm_y"].view(np.uint32))
+
+
 def test_against_compiled_reference_when_present(golden, orc):
     """Directly against oracle/_ref (the reference's compiled host code), on fresh random inputs: routing of
     256 x 128 logits with ties and NaNs, the plan of its ids."""
