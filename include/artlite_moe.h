@@ -198,7 +198,8 @@ int artlite_moe_debug(artlite_moe* h, float* logits, int32_t* ids, float* weight
  */
 int artlite_moe_stage_times(artlite_moe* h, int layer, float* ms, int* n_out);
 
-/* The expert path layer `layer`'s last forward took: 1 dequant-GEMV, 2 tcgen05 grouped GEMM (0: none yet). */
+/* The expert path layer `layer`'s last forward took: 1 the GEMV path (the fused decode kernel, the small-batch
+ * tensor-core GEMVs or the register-decoding GEMVs), 2 the tcgen05 grouped GEMM (0: none yet). */
 int artlite_moe_path(artlite_moe* h, int layer);
 
 /* Kernels this library has launched in this process so far (all handles and entry points). */
@@ -225,8 +226,8 @@ int artlite_moe_ep_init(artlite_moe* h, const void* unique_id, int bytes);
  * this rank's expert-ordered rows; recv_pos (world x E / world) where the rows from rank q for local expert e land in
  * the received rows (grouped by local expert, then by rank); local_off (E / world + 1) / local_counts (E / world) the
  * received rows per local expert. (The block's own forward keeps the received blocks source-major and runs each
- * (source rank, local expert) row group in place; this plan gives the expert-grouped layout to callers that exchange
- * rows themselves.)
+ * (source rank, local expert) row group in place, or from 8 ranks gathers them into this expert-grouped layout first;
+ * the plan gives the layout to callers that exchange rows themselves.)
  */
 int artlite_moe_ep_plan(const int32_t* send_counts, const int32_t* recv_counts, int world, int rank, int E,
                         int64_t* send_off, int64_t* recv_pos, int64_t* local_off, int32_t* local_counts);
