@@ -117,52 +117,85 @@ class Clocks:
 
 # ---------------------------------------------------------------- the CPU reference path
 
-def cpu_reference_sample(T: int, seed: int = 0) -> dict:
-    """The reference's CPU path on T tokens of one layer: (routing, moe_ffn) timed; returns tokens/s and what ran."""
-    from oracle import lib as olib
-    from oracle import moe_np
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    ref = olib.reference()
-    impl = ref if ref is not None else olib.oracle()
-    kind = "reference" if ref is not None else "port"
-    layer, x, _ = moe_np.make_block(seed, T, qtype=QTYPE, H=H, E=E, F=F)
-    xf = moe_np.bf16_to_f32(x)
 
-    def expert(e: int):
-        return (impl.dequant_rows(QTYPE, layer.gate[e * F:(e + 1) * F], H),
-                impl.dequant_rows(QTYPE, layer.up[e * F:(e + 1) * F], H),
-                impl.dequant_rows(QTYPE, layer.down[e * H:(e + 1) * H], F))
+class CpuReference:
+    """The reference's CPU path on one layer of the workload (T tokens): the router product, its routing (the
+    reference's compiled moe_route from oracle/_ref when it loads here, else the C restatement), and ref.moe_ffn
+    (restated in oracle/moe_np.py) with the compiled dequant_rows of the experts the tokens touch. The layer and the
+    tokens are generated once; run() times one pass."""
 
-    t0 = time.perf_counter()
-    logits = xf @ layer.router.T
-    ids, w = impl.route(logits, K)
-    moe_np.moe_ffn(xf, ids, w, expert)
-    dt = time.perf_counter() - t0
-    return {"seconds": dt, "tokens": T, "kind": kind, "cores": os.cpu_count()}
+    def __init__(self, T: int, seed: int = 0):
+        from oracle import lib as olib
+        from oracle import moe_np
+
+        self.moe_np = moe_np
+        ref = olib.reference()
+        self.impl = ref if ref is not None else olib.oracle()
+        self.kind = "reference" if ref is not None else "port"
+        self.T = T
+        self.layer, x, _ = moe_np.make_block(seed, T, qtype=QTYPE, H=H, E=E, F=F)
+        self.xf = moe_np.bf16_to_f32(x)
+
+    def run(self, blas_threads: int | None = None) -> float:
+        from contextlib import nullcontext
+
+        from threadpoolctl import threadpool_limits
+        layer, impl = self.layer, self.impl
+
+        def expert(e: int):
+            return (impl.dequant_rows(QTYPE, layer.gate[e * F:(e + 1) * F], H),
+                    impl.dequant_rows(QTYPE, layer.up[e * F:(e + 1) * F], H),
+                    impl.dequant_rows(QTYPE, layer.down[e * H:(e + 1) * H], F))
+
+        with threadpool_limits(blas_threads) if blas_threads else nullcontext():
+            t0 = time.perf_counter()
+            logits = self.xf @ layer.router.T
+            ids, w = impl.route(logits, K)
+            self.moe_np.moe_ffn(self.xf, ids, w, expert)
+            return time.perf_counter() - t0
+
+
+def blas_info() -> str:
+    try:
+        from threadpoolctl import threadpool_info
+        return ", ".join(f"{i.get('internal_api')} {i.get('num_threads')} threads" for i in threadpool_info()) or "?"
+    except ImportError:
+        return "?"
 
 
 def run_reference(args) -> None:
+    """The reference arm: the reference's CPU path on the workload's own per-layer batch (T = --cpu-tokens, default
+    the 16384 tokens of a layer of the stack), one layer per step, with all host cores; value = tokens x layers / s."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    T = args.cpu_tokens
+    ref = CpuReference(args.cpu_tokens, seed=1)
     for _ in range(args.warmup):
-        cpu_reference_sample(T, seed=1)
-    times = []
-    for s in range(args.steps):
-        r = cpu_reference_sample(T, seed=2 + s)
-        times.append(r["seconds"])
+        ref.run()
+    times = [ref.run() for _ in range(args.steps)]
     ms = 1000.0 * float(np.mean(times))
-    value = T / (ms / 1000.0)  # one layer per step
-    sample = f"{T} tokens x 1 layer of the workload per step (router, routing, moe_ffn with the dequant of the " \
-             f"experts they touch); numpy BLAS and the reference's dequant threads on all host cores"
+    value = ref.T / (ms / 1000.0)  # one layer per step
+    sample = (f"{ref.T} tokens x 1 layer of the workload per step (router, routing, moe_ffn with the dequant of the "
+              f"experts they touch); numpy BLAS ({blas_info()}) and the reference's dequant threads on all "
+              f"{os.cpu_count()} host cores ({cpu_model()}); median step {1000.0 * float(np.median(times)):.1f} ms")
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy: oracle.moe_np.make_block)",
-            "config": {"workload": WORKLOAD, "tokens_per_step": T, "layers_per_step": 1, "hidden": H, "experts": E,
-                       "top_k": K, "expert_ffn": F, "qtype": QTYPE},
+            "config": {"workload": WORKLOAD, "tokens_per_step": ref.T, "layers_per_step": 1, "hidden": H,
+                       "experts": E, "top_k": K, "expert_ffn": F, "qtype": QTYPE},
             "impl": "reference",
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": r["cores"], "kind": r["kind"], "sample": sample},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": ref.kind,
+                             "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -217,37 +250,40 @@ def gen_q(torch, g, dev, qtype, rows, cols):
     return raw.view(rows, -1)
 
 
-def run_config(args) -> None:
-    """benchmark configs 3 and 5 on one GPU, --layers layers of independent weights in turn (one JSON line per measured
-    shape): tokens x layers / s, ms per layer, and the gate/up GEMM's share of the tensor roofline (tcgen05 path)."""
+def measure_config(config: int, layers: int, steps: int, warmup: int) -> list[dict]:
+    """benchmark configs 3 and 5 on one GPU, `layers` layers of independent weights in turn (one dict per measured
+    shape): tokens x layers / s, ms per layer, and the gate/up GEMM's share of the tensor roofline (tcgen05 path).
+    The block's device status word is read after the timed steps (a bounded wait that ran out, or a bad expert id,
+    raises)."""
     import torch
     from artlite_b200.moe.block import MoEBlock
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    if args.config == 3:
+    if config == 3:
         h_, e_, k_, f_, qt, shapes = 2048, 128, 8, 768, "Q8_0", [("config3-prefill-q8_0-t4096-zipf1.1", 4096)]
     else:
         h_, e_, k_, f_, qt = 4096, 128, 8, 1536, "Q4_0"
         shapes = [("config5-prefill-q4_0-h4096-f1536-t8192", 8192), ("config5-decode-q4_0-h4096-f1536-b64", 64)]
-    L = args.layers
+    L = layers
     tmax = max(t for _, t in shapes)
     block = MoEBlock(hidden=h_, n_experts=e_, top_k=k_, expert_ffn=f_, max_tokens=tmax, n_layers=L, act_dtype="bf16",
                      device=0, path="auto")
     g = torch.Generator(device=dev)
-    g.manual_seed(4000 + args.config)
+    g.manual_seed(4000 + config)
     for layer in range(L):
         gate, up, down = gen_q(torch, g, dev, qt, e_ * f_, h_), gen_q(torch, g, dev, qt, e_ * f_, h_), \
             gen_q(torch, g, dev, qt, e_ * h_, f_)
         router = torch.randn((e_, h_), generator=g, device=dev) * 0.02
         block.set_weights(layer, gate=gate.data_ptr(), up=up.data_ptr(), down=down.data_ptr(),
                           router=router.data_ptr(), qtype=qt)
-        if args.config == 3:  # the Zipf(1.1) expert skew: bias_e = -1.1 ln(rank_e), ranks a seeded permutation
+        if config == 3:  # the Zipf(1.1) expert skew: bias_e = -1.1 ln(rank_e), ranks a seeded permutation
             rank = torch.randperm(e_, generator=g, device=dev).float() + 1.0
             block.set_router_bias(layer, (-1.1 * torch.log(rank)).cpu().numpy().astype(np.float32))
         del gate, up, down, router
     torch.cuda.empty_cache()
     peaks, src = measured_peaks()
     stream = torch.cuda.Stream(device=dev)
+    out = []
     for name, T in shapes:
         x = torch.randn((T, h_), generator=g, device=dev).to(torch.bfloat16)
         y = torch.empty((T, h_), dtype=torch.bfloat16, device=dev)
@@ -259,23 +295,24 @@ def run_config(args) -> None:
         clocks = Clocks(0)
         clocks.start()
         with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
+            for _ in range(warmup):
                 step()
         torch.cuda.synchronize()
         t_host0 = time.time()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         e1.record(stream)
         torch.cuda.synchronize()
         clk = clocks.stop(t_host0, time.time())
-        ms_layer = e0.elapsed_time(e1) / (args.steps * L)
+        block.sync()  # (the device status word: raises if a kernel reported an error)
+        ms_layer = e0.elapsed_time(e1) / (steps * L)
         stages = np.array([block.stage_times(layer) for layer in range(L)])
         path = block.path(0)
         line = {"workload": name, "tokens": T, "hidden": h_, "experts": e_, "top_k": k_, "expert_ffn": f_, "qtype": qt,
                 "ms_per_layer": ms_layer, "tokens_per_s": T / (ms_layer / 1000.0), "path": path, "layers": L,
-                "steps": args.steps, "clocks": clk}
+                "steps": steps, "clocks": clk}
         if path == "tc" and stages.shape[1] >= 3:
             gu_ms = float(stages[:, 2].mean())
             flops = 2.0 * T * k_ * h_ * (2 * f_)
@@ -284,23 +321,38 @@ def run_config(args) -> None:
                                 "achieved": flops / (gu_ms / 1000.0) / 1e12, "peak": peak, "unit": "TFLOP/s",
                                 "frac": flops / (gu_ms / 1000.0) / 1e12 / peak, "ms_per_launch": gu_ms,
                                 "peak_source": f"{src} bf16_tflops_sustained"}
+            down_ms = float(stages[:, 3].mean())
+            layer_flops = flops * 1.5
+            line["layer_roofline"] = {"bound": "tensor", "achieved": layer_flops / (ms_layer / 1000.0) / 1e12,
+                                      "peak": peak, "unit": "TFLOP/s",
+                                      "frac": layer_flops / (ms_layer / 1000.0) / 1e12 / peak,
+                                      "down_frac": flops * 0.5 / (down_ms / 1000.0) / 1e12 / peak}
             line["stage_ms_mean"] = dict(zip(["router", "route+dispatch", "gather+gate_up", "down", "combine"],
                                              [float(v) for v in stages.mean(0)]))
-        print(json.dumps(line), flush=True)
+        out.append(line)
     block.close()
+    del block
+    torch.cuda.empty_cache()
+    return out
 
 
-def run_decode(args) -> None:
+def run_config(args) -> None:
+    for line in measure_config(args.config, args.layers, args.steps, args.warmup):
+        print(json.dumps(line), flush=True)
+
+
+def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "auto") -> list[dict]:
     """benchmark config 2 on one GPU: decode batches B = 1, 4, 16, 64 of the Q4_K block (bf16 x), each forward a CUDA
-    graph, over --layers layers in turn (their touched experts far exceed L2). One JSON line per B: tokens/s, and the
-    HBM roofline of the bytes a forward must read (U touched experts x 2,654,208 B + the fp32 router 1,048,576 B)."""
+    graph, over `layers` layers in turn (their touched experts far exceed L2). One dict per B: tokens/s, and the
+    HBM roofline of the bytes a forward must read (U touched experts x 2,654,208 B + the fp32 router 1,048,576 B).
+    The block's device status word is read after the timed steps (raises on a kernel-reported error)."""
     import torch
     from artlite_b200.moe.block import MoEBlock
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    L = args.layers
-    block = MoEBlock(hidden=H, n_experts=E, top_k=K, expert_ffn=F, max_tokens=64, n_layers=L, act_dtype="bf16",
-                     device=0, path=args.path)
+    L = layers
+    block = MoEBlock(hidden=H, n_experts=E, top_k=K, expert_ffn=F, max_tokens=max(batches), n_layers=L,
+                     act_dtype="bf16", device=0, path=path)
     g = torch.Generator(device=dev)
     g.manual_seed(3000)
     for layer in range(L):
@@ -311,7 +363,8 @@ def run_decode(args) -> None:
     torch.cuda.empty_cache()
     peaks, src = measured_peaks()
     stream = torch.cuda.Stream(device=dev)
-    for B in args.batches:
+    out = []
+    for B in batches:
         x = torch.randn((B, H), generator=g, device=dev).to(torch.bfloat16)
         y = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
         touched = []
@@ -322,29 +375,39 @@ def run_decode(args) -> None:
         clocks = Clocks(0)
         clocks.start()
         with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
+            for _ in range(warmup):
                 for layer in range(L):
                     block.forward_graph(x.data_ptr(), y.data_ptr(), B, layer=layer, stream=stream.cuda_stream)
         torch.cuda.synchronize()
         t_host0 = time.time()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             for layer in range(L):
                 block.forward_graph(x.data_ptr(), y.data_ptr(), B, layer=layer, stream=stream.cuda_stream)
         e1.record(stream)
         torch.cuda.synchronize()
         clk = clocks.stop(t_host0, time.time())
-        ms_layer = e0.elapsed_time(e1) / (args.steps * L)
+        block.sync()  # (the device status word: raises if a kernel reported an error)
+        ms_layer = e0.elapsed_time(e1) / (steps * L)
         U = float(np.mean(touched))
         nbytes = U * 2654208 + E * H * 4
         gbs = nbytes / (ms_layer / 1000.0) / 1e9
-        print(json.dumps({"workload": f"decode-q4_k-b{B}", "batch": B, "us_per_layer": ms_layer * 1000.0,
-                          "tokens_per_s": B / (ms_layer / 1000.0), "experts_touched": U,
-                          "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                                       "frac": gbs / peaks["hbm_gbs"], "peak_source": src, "bytes_per_layer": nbytes},
-                          "path": block.path(0), "layers": L, "steps": args.steps, "clocks": clk}), flush=True)
+        out.append({"workload": f"decode-q4_k-b{B}", "batch": B, "us_per_layer": ms_layer * 1000.0,
+                    "tokens_per_s": B / (ms_layer / 1000.0), "experts_touched": U,
+                    "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                 "frac": gbs / peaks["hbm_gbs"], "peak_source": f"{src} hbm_gbs",
+                                 "bytes_per_layer": nbytes},
+                    "path": block.path(0), "layers": L, "steps": steps, "clocks": clk})
     block.close()
+    del block
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_decode(args) -> None:
+    for line in measure_decode(args.batches, args.layers, args.steps, args.warmup, args.path):
+        print(json.dumps(line), flush=True)
 
 
 def main() -> None:
@@ -355,9 +418,10 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--tokens", type=int, default=TOKENS)
-    ap.add_argument("--cpu-tokens", type=int, default=32)
+    ap.add_argument("--cpu-tokens", type=int, default=TOKENS, help="tokens of a CPU reference pass (one layer)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the decode sweep and config 3 of the default line")
     ap.add_argument("--decode", action="store_true", help="benchmark config 2 (decode batches, Q4_K) instead")
     ap.add_argument("--config", type=int, choices=[3, 5], help="benchmark config 3 or 5 (one GPU) instead")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"], help="expert path of --decode")
@@ -441,6 +505,7 @@ def main() -> None:
     torch.cuda.synchronize()
     t_host1 = time.time()
     launches = _lib.lib().artlite_moe_launch_count() - launches0
+    block.sync()  # (the device status word of the timed steps: raises if a kernel reported an error)
     barrier()
     torch.cuda.synchronize()
     ms_total = e0.elapsed_time(e1)
@@ -493,11 +558,24 @@ def main() -> None:
 
     # (every rank closes its block, then leaves the process group together)
     block.close()
+    del block
+    torch.cuda.empty_cache()
     barrier()
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return
+    # the north star's other two targets, timed in the same run on one GPU: the decode batches (HBM roofline) and
+    # the 4096-token Q8_0 prefill with Zipf-skewed routing (tensor roofline)
+    extras = {}
+    if world == 1 and not args.no_extras:
+        extras["decode_sweep"] = {f"B{d['batch']}": {k: d[k] for k in ("us_per_layer", "tokens_per_s",
+                                                                        "experts_touched", "roofline", "path",
+                                                                        "layers", "steps", "clocks")}
+                                  for d in measure_decode([1, 4, 16, 64], 8, 20, 3)}
+        c3 = measure_config(3, 4, 10, 3)[0]
+        extras["config3"] = {k: c3.get(k) for k in ("workload", "ms_per_layer", "tokens_per_s", "path", "roofline",
+                                                    "layer_roofline", "stage_ms_mean", "layers", "steps", "clocks")}
     peaks, peak_src = measured_peaks()
     # stages (tc path): router, route+dispatch, gather + gate/up, down, combine
     roof = None
@@ -541,6 +619,7 @@ def main() -> None:
                        "l2": "inputs larger than L2 (340 MB of weights streamed per layer)"},
             "stage_ms_mean": dict(zip(stage_names, [float(v) for v in stages.mean(0)])),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clk}
+    line.update(extras)
     print(json.dumps(line), flush=True)
 
 
@@ -559,21 +638,25 @@ def traffic_from_profiles():
 
 
 def cpu_baseline(T: int) -> dict:
-    """The reference's CPU path on a bounded sample (about 10-30 s of CPU work)."""
-    t0 = time.perf_counter()
-    secs, toks, r = 0.0, 0, None
-    i = 0
-    while time.perf_counter() - t0 < 10.0 or i < 2:
-        r = cpu_reference_sample(T, seed=50 + i)
-        if i > 0:  # (the first sample warms the caches)
-            secs += r["seconds"]
-            toks += r["tokens"]
-        i += 1
-        if time.perf_counter() - t0 > 30.0:
-            break
-    return {"value": toks / secs, "unit": UNIT, "cores": r["cores"], "kind": r["kind"],
-            "sample": f"{i - 1} samples of {T} tokens x 1 layer (router, routing, moe_ffn with the dequant of the "
-                      f"experts they touch), numpy BLAS on all cores, the reference's dequant threads"}
+    """The reference's CPU path on bounded samples (about 20-40 s of CPU work): the value is the median of three
+    passes over one layer of the workload's own batch (T tokens) with all host cores; beside it, a 1024-token layer
+    with all cores and with one BLAS thread (median of five each), where the dequant of the touched experts weighs
+    more."""
+    big = CpuReference(T, seed=50)
+    big.run()  # (warm)
+    t_big = [big.run() for _ in range(3)]
+    small = CpuReference(1024, seed=51)
+    small.run()
+    t_all = [small.run() for _ in range(5)]
+    t_one = [small.run(blas_threads=1) for _ in range(5)]
+    value = T / float(np.median(t_big))
+    return {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": big.kind,
+            "sample": f"median of 3 passes of {T} tokens x 1 layer (router, routing, moe_ffn with the dequant of the "
+                      f"experts they touch), numpy BLAS on all cores ({blas_info()}), the reference's dequant "
+                      f"threads; host {cpu_model()}",
+            "cpu_model": cpu_model(),
+            "t1024_all_cores_tokens_per_s": 1024 / float(np.median(t_all)),
+            "t1024_one_blas_thread_tokens_per_s": 1024 / float(np.median(t_one))}
 
 
 if __name__ == "__main__":

@@ -47,3 +47,30 @@ def make_block(layer: moe_np.Layer, T: int, *, act: str, path: str, gating: str 
     for L in range(n_layers):
         b.set_weights(L, gate=layer.gate, up=layer.up, down=layer.down, router=layer.router, qtype=layer.qtype)
     return b
+
+
+def torch_moe_ffn(layer: moe_np.Layer, x: np.ndarray, ids: np.ndarray, w: np.ndarray, device: int = 0) -> np.ndarray:
+    """ref.moe_ffn (tests/moe/ref.py:43-52) as a plain PyTorch fp32 computation on the GPU, for every token of a
+    full-size batch: each expert's weights dequantised exactly on the CPU by the C oracle (bit-identical to the
+    reference's dequant_rows), its rows' SwiGLU in fp32 (no TF32), the weighted rows added into y in expert order.
+    It differs from the NumPy oracle only in the fp32 summation order (tests pin the two against each other)."""
+    import torch
+    prev = torch.backends.cuda.matmul.fp32_precision
+    torch.backends.cuda.matmul.fp32_precision = "ieee"
+    try:
+        dev = torch.device("cuda", device)
+        xf = torch.from_numpy(x_f32(x)).to(dev)
+        y = torch.zeros_like(xf)
+        get = expert_fn(layer)
+        ids_t = torch.from_numpy(np.ascontiguousarray(ids, np.int64)).to(dev)
+        w_t = torch.from_numpy(np.ascontiguousarray(w, np.float32)).to(dev)
+        for e in np.unique(ids):
+            t, i = torch.nonzero(ids_t == int(e), as_tuple=True)
+            g, u, d = (torch.from_numpy(a).to(dev) for a in get(int(e)))
+            xe = xf[t]
+            h = torch.nn.functional.silu(xe @ g.T) * (xe @ u.T)
+            y.index_add_(0, t, w_t[t, i][:, None] * (h @ d.T))
+        out = y.cpu().numpy()
+    finally:
+        torch.backends.cuda.matmul.fp32_precision = prev
+    return out
