@@ -50,13 +50,15 @@ int scratch_address(int dev, uint8_t** out) {
   return ARTLITE_OK;
 }
 
-bool on_device(const void* p) {
+// device memory of device `dev` (not host, pinned, managed or another GPU's memory: the kernels would fault on a
+// buffer of another device without peer access, and host memory is not reachable at these addresses)
+bool on_device(const void* p, int dev) {
   cudaPointerAttributes at;
   if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
-  return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+  return at.type == cudaMemoryTypeDevice && at.device == dev;
 }
 
 }  // namespace
@@ -71,17 +73,21 @@ int artlite_moe_dispatch_noalloc(const int32_t* ids, int64_t n, int k, int E, in
                                  int32_t* slot, void* stream) {
   AL_CHECK(n >= 0 && k >= 1 && E >= 1, ARTLITE_EINVAL, "dispatch_noalloc: n %lld k %d E %d", (long long)n, k, E);
   AL_CHECK(E <= 1024, ARTLITE_EUNSUPPORTED, "dispatch_noalloc: E %d (this build: E <= 1024)", E);
+  // (the pair count is bounded before it is formed: n k must not wrap)
+  AL_CHECK(n <= kNoAllocMaxCounts * (int64_t)kDispatchBlockPairs / k, ARTLITE_EINVAL,
+           "dispatch_noalloc: %lld tokens x %d slots exceed the static scratch (at most %lld pairs)", (long long)n, k,
+           (long long)(kNoAllocMaxCounts / E * kDispatchBlockPairs));
   const int64_t P = n * k;
   const int64_t nblk = P ? cdiv(P, kDispatchBlockPairs) : 0;
   AL_CHECK(nblk * E <= kNoAllocMaxCounts, ARTLITE_EINVAL,
            "dispatch_noalloc: %lld pairs of %d experts need %lld block counts; the static scratch holds %lld (at most "
            "%lld pairs at this E)", (long long)P, E, (long long)(nblk * E), (long long)kNoAllocMaxCounts,
            (long long)(kNoAllocMaxCounts / E * kDispatchBlockPairs));
-  AL_CHECK(offsets && on_device(offsets) && (P == 0 || (ids && perm && slot && on_device(ids) && on_device(perm) &&
-                                                         on_device(slot))),
-           ARTLITE_EINVAL, "dispatch_noalloc: ids / offsets / perm / slot must be device memory of the current device");
   int dev;
   AL_CUDA(cudaGetDevice(&dev));
+  AL_CHECK(offsets && on_device(offsets, dev) && (P == 0 || (ids && perm && slot && on_device(ids, dev) &&
+                                                              on_device(perm, dev) && on_device(slot, dev))),
+           ARTLITE_EINVAL, "dispatch_noalloc: ids / offsets / perm / slot must be device memory of the current device");
   uint8_t* scratch;
   AL_TRY(scratch_address(dev, &scratch));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -97,8 +103,8 @@ int artlite_moe_dispatch_noalloc(const int32_t* ids, int64_t n, int k, int E, in
   d.slot = slot;
   d.status = status;
   AL_TRY(launch_dispatch(d, st));
-  DevStatus s{};
-  AL_CUDA(cudaMemcpyAsync(&s, status, sizeof s, cudaMemcpyDeviceToHost, st));
+  // the call returns when its kernels are done: the stream is polled against a deadline, and the status word is read
+  // only once the stream is idle (a copy that has nothing to wait for)
   const auto t0 = std::chrono::steady_clock::now();
   for (;;) {
     const cudaError_t q = cudaStreamQuery(st);
@@ -108,7 +114,9 @@ int artlite_moe_dispatch_noalloc(const int32_t* ids, int64_t n, int k, int E, in
              "dispatch_noalloc: no completion within 60 s");
     std::this_thread::yield();
   }
-  AL_CHECK(s.code != ARTLITE_EDEVICE, ARTLITE_EINVAL, "moe_plan: expert id %d of %d", s.a, E);
+  DevStatus s{};
+  AL_CUDA(cudaMemcpy(&s, status, sizeof s, cudaMemcpyDeviceToHost));
+  AL_CHECK(s.code != ARTLITE_EDEVICE, ARTLITE_EINVAL, "dispatch_noalloc: expert id %d of %d", s.a, E);
   AL_CHECK(s.code == 0, s.code, "dispatch_noalloc: device status %d", s.code);
   return ARTLITE_OK;
 }

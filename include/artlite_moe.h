@@ -87,12 +87,14 @@ int artlite_moe_dispatch(const int32_t* ids, int64_t n, int k, int E, int64_t* o
 /*
  * The same dispatch for callers that must not allocate device memory while they run (a serving loop that reserves its
  * memory budget at start-up, code whose device memory a framework's caching allocator owns): it allocates nothing.
- * No counterpart in the reference. ids, offsets, perm and slot must be device memory of the current device; the
+ * No counterpart in the reference. ids, offsets, perm and slot must be device memory of the current device (host,
+ * pinned, managed and other GPUs' buffers are rejected with ARTLITE_EINVAL before anything is launched); the
  * scratch is a 1 MiB static device array of this library (held on every GPU that loads it until exit), so a call
  * takes at most ceil(n k / 4096) E <= 262144 block counts (n k <= 8,388,608 pairs at E = 128) and rejects more with
  * ARTLITE_EINVAL. The first call on a device looks the array's address up (cudaGetSymbolAddress) for that device; make
- * it before any stream capture. Enqueued on `stream` (NULL: the default stream), then waited for; every call shares
- * the array, so calls that overlap on the GPU race.
+ * it before any stream capture. Enqueued on `stream` (NULL: the default stream), then waited for (at most 60 s:
+ * ARTLITE_ETIMEOUT); an expert id outside [0, E) returns ARTLITE_EINVAL. Every call shares the array, so calls that
+ * overlap on the GPU race.
  */
 int artlite_moe_dispatch_noalloc(const int32_t* ids, int64_t n, int k, int E, int64_t* offsets, int32_t* perm,
                                  int32_t* slot, void* stream);
