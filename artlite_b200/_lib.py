@@ -20,7 +20,7 @@ EXPORTS = ("artlite_moe_last_error", "artlite_moe_version", "artlite_moe_route",
            "artlite_moe_set_weights", "artlite_moe_set_router_bias", "artlite_moe_set_shared", "artlite_moe_set_norm",
            "artlite_moe_forward",
            "artlite_moe_forward_graph", "artlite_moe_sync", "artlite_moe_debug",
-           "artlite_moe_stage_times", "artlite_moe_path", "artlite_moe_launch_count", "artlite_moe_destroy",
+           "artlite_moe_stage_times", "artlite_moe_path", "artlite_moe_weights", "artlite_moe_launch_count", "artlite_moe_destroy",
            "artlite_moe_ep_unique_id", "artlite_moe_ep_init", "artlite_moe_ep_plan")
 
 
@@ -33,7 +33,7 @@ class Error(RuntimeError):
 
 
 class CapacityError(Error):
-    """``moe_plan``: a column needs more than ``cap`` chunks (moe_host.cpp:263)."""
+    """``moe_plan``: a column needs more than ``cap`` chunks (moe_host.cpp:223)."""
 
 
 class MoeDesc(ctypes.Structure):
@@ -62,6 +62,7 @@ _SIGS = {
     "artlite_moe_debug": ([_P, _P, _P, _P, _P, _P], _I),
     "artlite_moe_stage_times": ([_P, _I, _P, ctypes.POINTER(_I)], _I),
     "artlite_moe_path": ([_P, _I], _I),
+    "artlite_moe_weights": ([_P, _I, _I, ctypes.POINTER(_P), ctypes.POINTER(_I64)], _I),
     "artlite_moe_launch_count": ([], _I64),
     "artlite_moe_destroy": ([_P], _I),
     "artlite_moe_ep_unique_id": ([_P, _I], _I),

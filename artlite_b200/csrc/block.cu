@@ -44,6 +44,25 @@ int status_error(const DevStatus& s, int E) {
   return ARTLITE_OK;
 }
 
+// a bounded wait for an event recorded earlier
+int wait_event(cudaEvent_t e, int timeout_ms) {
+  if (timeout_ms <= 0) timeout_ms = 60000;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(e);
+    if (q == cudaSuccess) return ARTLITE_OK;
+    if (q != cudaErrorNotReady) {
+      set_error("moe: %s", cudaGetErrorString(q));
+      return ARTLITE_ECUDA;
+    }
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+      set_error("moe: no completion within %d ms", timeout_ms);
+      return ARTLITE_ETIMEOUT;
+    }
+    std::this_thread::yield();
+  }
+}
+
 int wait(cudaStream_t st, int timeout_ms) {
   if (timeout_ms <= 0) timeout_ms = 60000;
   cudaEvent_t e;
@@ -333,6 +352,7 @@ int artlite_moe_create(const artlite_moe_desc* desc, artlite_moe** out) {
   if (d.device >= 0) AL_CUDA(cudaSetDevice(d.device));
   AL_CUDA(cudaGetDevice(&h->dev));
   AL_CUDA(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking));
+  AL_CUDA(cudaEventCreateWithFlags(&h->done, cudaEventDisableTiming));
   h->E_local = d.n_experts / world;
   h->e0 = d.ep_rank * h->E_local;
   h->layers.resize(d.n_layers);
@@ -490,6 +510,9 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
   }
   AL_TRY(mk.mark());
   h->n_stages[layer] = mk.ns;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  AL_CUDA(cudaStreamIsCapturing(st, &cs));
+  if (cs == cudaStreamCaptureStatusNone) AL_CUDA(cudaEventRecord(h->done, st));
   if (T > 0 && !y_dev) {
     AL_CUDA(cudaMemcpyAsync(y, yd, act * T * H, cudaMemcpyDefault, st));
     AL_TRY(wait_deadline(st, 0));
@@ -618,6 +641,7 @@ int artlite_moe_forward_graph(artlite_moe* h, int layer, const void* x, void* y,
   for (const artlite_moe::Graph& g : h->graphs)
     if (g.layer == layer && g.T == T && g.x == x && g.y == y) {
       AL_CUDA(cudaGraphLaunch(g.exec, st));
+      AL_CUDA(cudaEventRecord(h->done, st));
       h->last_T = T;
       return ARTLITE_OK;
     }
@@ -652,6 +676,7 @@ int artlite_moe_forward_graph(artlite_moe* h, int layer, const void* x, void* y,
   AL_CHECK(ie == cudaSuccess, ARTLITE_ECUDA, "moe_forward_graph: instantiate: %s", cudaGetErrorString(ie));
   h->graphs.push_back({layer, T, x, y, exec});
   AL_CUDA(cudaGraphLaunch(exec, st));
+  AL_CUDA(cudaEventRecord(h->done, st));
   return ARTLITE_OK;
 }
 
@@ -659,6 +684,7 @@ int artlite_moe_sync(artlite_moe* h, int timeout_ms) {
   AL_CHECK(h, ARTLITE_EINVAL, "moe_sync: null handle");
   AL_CUDA(cudaSetDevice(h->dev));
   AL_TRY(wait(h->st, timeout_ms));
+  AL_TRY(wait_event(h->done, timeout_ms));  // (the last forward, on whichever stream it was enqueued)
   DevStatus s;
   AL_CUDA(cudaMemcpy(&s, h->status.ptr, sizeof s, cudaMemcpyDeviceToHost));
   if (s.code) {
@@ -701,6 +727,22 @@ int artlite_moe_path(artlite_moe* h, int layer) {
   return h->paths[layer];
 }
 
+int artlite_moe_weights(artlite_moe* h, int layer, int which, const void** ptr, int64_t* bytes) {
+  AL_CHECK(h && ptr && bytes, ARTLITE_EINVAL, "moe_weights: null argument");
+  AL_CHECK(layer >= 0 && layer < (int)h->layers.size() && h->layers[layer].qtype >= 0, ARTLITE_EINVAL,
+           "moe_weights: layer %d has no weights", layer);
+  AL_CHECK(which >= 0 && which <= 3, ARTLITE_EINVAL, "moe_weights: tensor %d (0 gate, 1 up, 2 down, 3 router)", which);
+  const artlite_moe::Layer& L = h->layers[layer];
+  const int64_t F = h->d.expert_ffn, H = h->d.hidden;
+  switch (which) {
+    case 0: *ptr = L.gate.ptr, *bytes = h->E_local * F * L.rb_gu; break;
+    case 1: *ptr = L.up.ptr, *bytes = h->E_local * F * L.rb_gu; break;
+    case 2: *ptr = L.down.ptr, *bytes = h->E_local * H * L.rb_dn; break;
+    default: *ptr = L.router.ptr, *bytes = h->d.n_experts * H * (L.router_qtype == ARTLITE_F32 ? 4 : 2); break;
+  }
+  return ARTLITE_OK;
+}
+
 int64_t artlite_moe_launch_count(void) { return artlite::launch_count(); }
 
 int artlite_moe_destroy(artlite_moe* h) {
@@ -709,6 +751,7 @@ int artlite_moe_destroy(artlite_moe* h) {
   if (!h->ep_failed) wait(h->st, 0);  // (bounded; after a failed exchange nothing is waited for)
   for (cudaEvent_t e : h->ev)
     if (e) cudaEventDestroy(e);
+  if (h->done) cudaEventDestroy(h->done);
   ep_destroy(h);
   for (artlite_moe::Graph& g : h->graphs) cudaGraphExecDestroy(g.exec);
   cudaStreamDestroy(h->st);

@@ -48,6 +48,9 @@ struct artlite_moe {
   artlite::DevBuf sh_y, sh_s, sh_iota, sh_off;  // the shared expert's outputs (T rows), gates (T), 0..T-1, {0, T} / {T}
   int64_t last_T = 0;
   int last_path = 0;
+  // recorded on the forward's stream at the end of every forward (and graph replay): artlite_moe_sync waits for it,
+  // so that a forward enqueued on a caller's stream is waited for before the status word is read
+  cudaEvent_t done = nullptr;
   bool timing = false;
   std::vector<cudaEvent_t> ev;  // [n_layers][kStages]: the last forward of each layer, read without a sync
   std::vector<int> n_stages;    // per layer

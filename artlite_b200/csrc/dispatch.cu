@@ -1,5 +1,5 @@
 // Dispatch: the (token, slot) pairs grouped by expert, stable in pair order, as moe_plan's histogram / prefix scan /
-// permute (csrc/artlite/moe_host.cpp:243-255), in three kernels over blocks of kDispatchBlockPairs pairs:
+// permute (csrc/artlite/moe_host.cpp:203-215), in three kernels over blocks of kDispatchBlockPairs pairs:
 //   count   per block, a shared-memory histogram of its pairs' experts (ids checked: an id outside [0, E) is reported
 //           through the status word as moe_plan's "expert id {x} of {E}" error, :247);
 //   scan    per expert the exclusive scan over blocks, then over experts (offsets), the units of work per expert and
@@ -7,7 +7,7 @@
 //   rank    per block, in rounds of 256 pairs in order: within a warp the rank among lanes of the same expert
 //           (__match_any_sync), across the round's warps a prefix of per-warp counts, across rounds a running count:
 //           a pair's place = offsets[e] + block base[e] + running[e] + warp prefix + lane rank (stable).
-// Then the reference plan's chunk deal (moe_host.cpp:256-274) for the drop-in artlite_moe_plan.
+// Then the reference plan's chunk deal (moe_host.cpp:216-234) for the drop-in artlite_moe_plan.
 #include "common.cuh"
 #include "kernels.cuh"
 #include "route.cuh"

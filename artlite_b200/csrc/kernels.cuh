@@ -53,7 +53,7 @@ bool small_dispatch_ok(int64_t P, int E);
 int launch_route_dispatch_small(const RouteArgs& r, const DispatchArgs& a, int mult2, int32_t* unit_off2,
                                 cudaStream_t st);
 
-// The reference plan's chunk deal (moe_host.cpp:256-274) from a dispatch: experts / counts / sizes / rows / pos.
+// The reference plan's chunk deal (moe_host.cpp:216-234) from a dispatch: experts / counts / sizes / rows / pos.
 struct ChunkPlanArgs {
   const int32_t* ids;
   const int32_t* slot;

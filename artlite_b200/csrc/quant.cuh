@@ -1,5 +1,5 @@
 // GGUF block decoding on the device, fp32 and exact: the reference's fp32 operations in their order
-// (csrc/artlite/dequant.cpp:43-123, itself built with -ffp-contract=off), written with the _rn intrinsics so that
+// (csrc/artlite/dequant.cpp:21-101, itself built with -ffp-contract=off), written with the _rn intrinsics so that
 // nvcc contracts nothing into an FMA. Every product here has at most 21 significant bits, so the values are exact.
 #pragma once
 
@@ -16,7 +16,7 @@ __device__ __forceinline__ float f16_at(const uint8_t* p) {
   return __half2float(__ushort_as_half(h));
 }
 
-// Q4_0 (dequant.cpp:62-69): 18 B per 32, w = (q - 8) d; values 0..15 the low nibbles of bytes 2..17, 16..31 the high
+// Q4_0 (dequant.cpp:40-47): 18 B per 32, w = (q - 8) d; values 0..15 the low nibbles of bytes 2..17, 16..31 the high
 __device__ __forceinline__ void dq_q4_0(const uint8_t* b, float* o) {
   const float d = f16_at(b);
 #pragma unroll
@@ -27,7 +27,7 @@ __device__ __forceinline__ void dq_q4_0(const uint8_t* b, float* o) {
   }
 }
 
-// Q4_1 (dequant.cpp:71-78): 20 B per 32, w = d q + m
+// Q4_1 (dequant.cpp:49-56): 20 B per 32, w = d q + m
 __device__ __forceinline__ void dq_q4_1(const uint8_t* b, float* o) {
   const float d = f16_at(b), m = f16_at(b + 2);
 #pragma unroll
@@ -38,14 +38,14 @@ __device__ __forceinline__ void dq_q4_1(const uint8_t* b, float* o) {
   }
 }
 
-// Q8_0 (dequant.cpp:80-84): 34 B per 32, w = d q, q int8
+// Q8_0 (dequant.cpp:58-62): 34 B per 32, w = d q, q int8
 __device__ __forceinline__ void dq_q8_0(const uint8_t* b, float* o) {
   const float d = f16_at(b);
 #pragma unroll
   for (int j = 0; j < 32; j++) o[j] = __fmul_rn(d, (float)(int8_t)b[2 + j]);
 }
 
-// Q4_K / Q5_K scale and min of 32-group g (dequant.cpp:92-95): six bits each, packed in 12 bytes at b + 4
+// Q4_K / Q5_K scale and min of 32-group g (dequant.cpp:70-73): six bits each, packed in 12 bytes at b + 4
 __device__ __forceinline__ void k_scale_min(const uint8_t* b, int g, int* sc, int* mn) {
   const uint8_t *lo = b + 4, *hi = b + 8, *top = b + 12;
   if (g < 4) {
@@ -57,7 +57,7 @@ __device__ __forceinline__ void k_scale_min(const uint8_t* b, int g, int* sc, in
   }
 }
 
-// Q4_K / Q5_K 32-group g of a 256 super-block (dequant.cpp:86-103): w = q (d sc_g) - dmin mn_g
+// Q4_K / Q5_K 32-group g of a 256 super-block (dequant.cpp:64-81): w = q (d sc_g) - dmin mn_g
 template <bool Q5>
 __device__ __forceinline__ void dq_k45_group(const uint8_t* b, int g, float* o) {
   const float d = f16_at(b), dmin = f16_at(b + 2);
@@ -74,7 +74,7 @@ __device__ __forceinline__ void dq_k45_group(const uint8_t* b, int g, float* o) 
   }
 }
 
-// Q6_K 32-group g (dequant.cpp:105-123): w = (q - 32) (sc_j d), sc per 16
+// Q6_K 32-group g (dequant.cpp:83-101): w = (q - 32) (sc_j d), sc per 16
 __device__ __forceinline__ void dq_q6_k_group(const uint8_t* b, int g, float* o) {
   const int h = g >> 2, jj = g & 3;
   const uint8_t* c = b + 64 * h + 32 * (jj & 1);

@@ -1,7 +1,7 @@
 // Routing: one warp per token, top-k by rounds of a warp arg-max over 64-bit ordered keys, softmax / sigmoid weights
 // over the k in double, normalised in numpy's pairwise order.
 //
-// Semantics follow artlite::moe_route (csrc/artlite/moe_host.cpp:85-113 route_rows_scalar, :138-214
+// Semantics follow artlite::moe_route (csrc/artlite/moe_host.cpp:45-73 route_rows_scalar, :98-174
 // route_rows_avx512, :216-239 route_rows / moe_route):
 //   key(l, x) = (bits(l + 0) flipped to an unsigned order) << 32 | ~x  (ties to the lower id, -0 == +0, :95-96);
 //   e_j = e^(l_j - l_0) in double; on the reference's vector-path shapes (k <= 16, per_col % 16 == 0, E <= 512) rows
@@ -40,7 +40,7 @@ int launch_route(const RouteArgs& a, cudaStream_t st) {
 }
 
 int check_route_args(int64_t n, int per_col, int E, int k) {
-  // the reference's own check (moe_host.cpp:228), then this build's limits
+  // the reference's own check (moe_host.cpp:188), then this build's limits
   AL_CHECK(per_col > 0 && k >= 1 && k <= E && E % per_col == 0, ARTLITE_EINVAL, "moe_route: k %d of E %d (%d per column)",
            k, E, per_col);
   AL_CHECK(E <= 1024 && k <= 32, ARTLITE_EUNSUPPORTED, "moe_route: E %d k %d (this build: E <= 1024, k <= 32)", E, k);

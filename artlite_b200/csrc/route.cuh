@@ -25,7 +25,7 @@ __device__ __forceinline__ float key_logit(uint64_t key) {
   return __uint_as_float((o & 0x80000000u) ? (o ^ 0x80000000u) : ~o);
 }
 
-// e^x for x <= 0 by the reference's method (moe_host.cpp:115-130): x = n ln 2 + r (ln 2 in two parts), a degree-12
+// e^x for x <= 0 by the reference's method (moe_host.cpp:75-90): x = n ln 2 + r (ln 2 in two parts), a degree-12
 // Taylor polynomial of r by Horner with fused multiply-adds, times 2^n; x clamped at -708.
 __device__ __forceinline__ double exp_nonpos(double x) {
   const double log2e = 1.4426950408889634, ln2hi = 6.93147180369123816490e-01, ln2lo = 1.90821492927058770002e-10;
@@ -92,7 +92,7 @@ __device__ __forceinline__ void route_row(const RouteArgs& a, int64_t t, int lan
     const double l = (double)key_logit(mine);
     e = a.sigmoid ? 1.0 / (1.0 + exp(-l)) : (taylor ? exp_nonpos(l - l0) : exp(l - l0));
   }
-  // numpy's pairwise order for a row of k <= 32 (moe_host.cpp:64-79)
+  // numpy's pairwise order for a row of k <= 32 (moe_host.cpp:24-39)
   double s = 0.0, r0 = 0, r1 = 0, r2 = 0, r3 = 0, r4 = 0, r5 = 0, r6 = 0, r7 = 0;
   const int full = a.k < 8 ? 0 : (a.k / 8) * 8;
 #pragma unroll

@@ -145,6 +145,14 @@ class MoEBlock:
         check(lib().artlite_moe_stage_times(self._h, layer, ms, ctypes.byref(n)))
         return list(ms[:n.value])
 
+    def weights(self, layer: int, which: str) -> tuple[int, int]:
+        """(device address, bytes) of layer ``layer``'s tensor ``which`` ("gate", "up", "down", "router") as it sits
+        in HBM: the GGUF bytes set_weights copied, unconverted (this rank's experts' rows)."""
+        ptr, n = ctypes.c_void_p(), ctypes.c_int64()
+        check(lib().artlite_moe_weights(self._h, layer, ("gate", "up", "down", "router").index(which),
+                                        ctypes.byref(ptr), ctypes.byref(n)))
+        return ptr.value, n.value
+
     def path(self, layer: int = 0) -> str:
         return {0: "none", 1: "gemv", 2: "tc"}[lib().artlite_moe_path(self._h, layer)]
 

@@ -1,5 +1,5 @@
 """The routing and the plan of an MoE layer, with the signatures of the reference's ``artlite.moe.plan``
-(src/artlite/moe/plan.py:124-161): ``route`` and ``Plan.of``, computed by the CUDA kernels of
+(src/artlite/moe/plan.py:25-57): ``route`` and ``Plan.of``, computed by the CUDA kernels of
 ``libartlite_moe_cuda.so`` (``artlite_moe_route`` / ``artlite_moe_plan``) instead of the host C++ (``_native``).
 
 ``route``: per token the k largest logits (ties to the lower id, -0 == +0), weights e^(l - l_max) over the k in

@@ -33,7 +33,7 @@ extern "C" {
 /* status codes */
 #define ARTLITE_OK 0
 #define ARTLITE_EINVAL -1     /* bad argument: the reference's artlite::Error cases (e.g. "moe_route: k 9 of E 8") */
-#define ARTLITE_ECAPACITY -2  /* moe_plan: a column needs more than cap chunks (moe_host.cpp:263) */
+#define ARTLITE_ECAPACITY -2  /* moe_plan: a column needs more than cap chunks (moe_host.cpp:223) */
 #define ARTLITE_ECUDA -3      /* a CUDA runtime / driver call failed */
 #define ARTLITE_ENCCL -4      /* an NCCL call failed (expert-parallel exchange) */
 #define ARTLITE_ETIMEOUT -5   /* a bounded wait ran out (host event wait, device flag wait) */
@@ -71,14 +71,14 @@ int artlite_moe_route(const float* logits, int64_t n, int64_t row, int per_col, 
  * chunks of at most `chunk`, dealt to the cols columns in turn, expert by expert: experts (cols x cap), counts (cols),
  * sizes (cols x cap), rows (cols x cap x chunk; padding repeats the chunk's first token), pos (n x k) =
  * (c cap + kk) chunk + j. ARTLITE_EINVAL on an id outside [0, E); ARTLITE_ECAPACITY when a column needs more than cap
- * chunks (the reference's two artlite::Error cases, moe_host.cpp:247,263).
+ * chunks (the reference's two artlite::Error cases, moe_host.cpp:207,223).
  */
 int artlite_moe_plan(const int32_t* ids, int64_t n, int k, int E, int cols, int cap, int chunk, int32_t* experts,
                      int32_t* counts, int32_t* sizes, int32_t* rows, int64_t* pos);
 
 /*
  * The expert-contiguous dispatch the block runs on the GPU (the histogram / scan / stable permute at the head of
- * moe_plan, moe_host.cpp:243-255): offsets (E + 1, int64) the exclusive scan of the per-expert pair counts, perm
+ * moe_plan, moe_host.cpp:203-215): offsets (E + 1, int64) the exclusive scan of the per-expert pair counts, perm
  * (n k, int32) the pairs t k + i in expert-then-pair order, slot (n k, int32) the position of each pair in perm.
  */
 int artlite_moe_dispatch(const int32_t* ids, int64_t n, int k, int E, int64_t* offsets, int32_t* perm,
@@ -119,7 +119,7 @@ typedef struct {
   int32_t top_k;         /* K (<= 32) */
   int32_t expert_ffn;    /* F */
   int32_t n_layers;      /* weight slots (a stack of blocks, each with its own weights) */
-  int32_t gating;        /* 0 softmax, 1 sigmoid (moe/plan.py:124-135) */
+  int32_t gating;        /* 0 softmax, 1 sigmoid (moe/plan.py:25-36) */
   int32_t act_dtype;     /* x and y: ARTLITE_F32 or ARTLITE_BF16 */
   int32_t max_tokens;    /* the largest T a forward takes (sizes the workspaces) */
   int32_t device;        /* CUDA device ordinal (-1: the current one) */
@@ -164,7 +164,8 @@ int artlite_moe_set_norm(artlite_moe* h, int layer, const void* w, int w_dtype, 
  * blk.L.ffn_down_shexp.weight (H rows of ffn values, down_qtype), and gate_inp = blk.L.ffn_gate_inp_shexp.weight (H
  * values of gate_dtype ARTLITE_F32 / ARTLITE_BF16; NULL: no gate). The layer's output becomes the routed sum +
  * sigmoid(gate_inp . x) swiglu(x), both in one fp32 sum rounded once. Host or device pointers; gate = NULL removes the
- * shared expert. Not with expert parallelism (ep_world > 1): ARTLITE_EUNSUPPORTED.
+ * shared expert. With expert parallelism (ep_world > 1) every rank holds the whole shared expert and runs it on its
+ * own tokens while the routed rows travel.
  */
 int artlite_moe_set_shared(artlite_moe* h, int layer, int ffn, int qtype, const void* gate, const void* up,
                            int down_qtype, const void* down, const void* gate_inp, int gate_dtype);
@@ -184,7 +185,9 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
  */
 int artlite_moe_forward_graph(artlite_moe* h, int layer, const void* x, void* y, int64_t T, void* stream);
 
-/* Wait (bounded by timeout_ms; <= 0: 60 s) for the handle's work and report any device-side status. */
+/* Wait (bounded by timeout_ms; <= 0: 60 s) for the handle's work, its last forward included on whichever stream it
+ * was enqueued, and report any device-side status (a bounded device wait that ran out: ARTLITE_ETIMEOUT; an expert
+ * id out of range: ARTLITE_EDEVICE); the status word is cleared after it is reported. */
 int artlite_moe_sync(artlite_moe* h, int timeout_ms);
 
 /*
@@ -204,6 +207,13 @@ int artlite_moe_stage_times(artlite_moe* h, int layer, float* ms, int* n_out);
  * tensor-core GEMVs or the register-decoding GEMVs), 2 the tcgen05 grouped GEMM (0: none yet). */
 int artlite_moe_path(artlite_moe* h, int layer);
 
+/*
+ * Where layer `layer`'s tensor `which` lives in device memory, as set_weights copied it (the GGUF bytes verbatim, no
+ * conversion; GGUFFile.tensor's raw view, gguf_model.py:494-506): 0 ffn_gate_exps, 1 ffn_up_exps, 2 ffn_down_exps
+ * (this rank's experts' rows), 3 ffn_gate_inp (the router). *bytes excludes the zeroed slack past the tensor.
+ */
+int artlite_moe_weights(artlite_moe* h, int layer, int which, const void** ptr, int64_t* bytes);
+
 /* Kernels this library has launched in this process so far (all handles and entry points). */
 int64_t artlite_moe_launch_count(void);
 
@@ -211,7 +221,7 @@ int artlite_moe_destroy(artlite_moe* h);
 
 /* ---------------------------------------------------------------- expert parallelism (ep_world > 1)
  * The reference runs on one NPU and has no counterpart (its closest analogue is the 8-column deal of moe_plan,
- * moe_host.cpp:256-274, an intra-device split). One process per GPU; rank r of W owns experts [r E / W, (r + 1) E / W)
+ * moe_host.cpp:216-234, an intra-device split). One process per GPU; rank r of W owns experts [r E / W, (r + 1) E / W)
  * and its own tokens; artlite_moe_forward exchanges token rows and expert outputs with NCCL (loaded at run time:
  * libnccl.so.2, or ARTLITE_NCCL_LIB). */
 

@@ -24,12 +24,17 @@ class OracleError(RuntimeError):
     pass
 
 
+def reference_tree() -> str:
+    """The reference checkout: ``ARTLITE_REF``, else ``reference/`` beside this repository's root."""
+    return os.environ.get("ARTLITE_REF") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
 def build() -> None:
     """Compile the C oracle (and the reference's host code when its tree is present) with ``oracle/Makefile``."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if os.path.isdir(os.environ.get("ARTLITE_REF", "/root/reference") + "/csrc/artlite"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref", "REF=" + os.environ.get("ARTLITE_REF", "/root/reference")],
-                       check=True)
+    ref = reference_tree()
+    if os.path.isdir(os.path.join(ref, "csrc", "artlite")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", "REF=" + ref], check=True)
 
 
 def _ptr(a: np.ndarray) -> int:
@@ -61,7 +66,7 @@ class _Lib:
 
     def route(self, logits: np.ndarray, k: int, *, E: int = 0, per_col: int = 0, pitch: int = 0,
               gating: str = "softmax") -> tuple[np.ndarray, np.ndarray]:
-        """``moe_route`` on (T, row) fp32 logits (``artlite.moe.plan.route``'s arguments, ``plan.py:124-135``)."""
+        """``moe_route`` on (T, row) fp32 logits (``artlite.moe.plan.route``'s arguments, ``plan.py:25-36``)."""
         lg = np.ascontiguousarray(logits, np.float32)
         T = lg.shape[0]
         E = E or lg.shape[1]

@@ -8,13 +8,13 @@
  *   - golden vectors written by the reference's NumPy oracle (tests/golden/, made by tests/golden/make_golden.py).
  *
  * Reference files (artlite-project/artlite):
- *   csrc/artlite/moe_host.cpp:64-79    row_sum         numpy's pairwise summation order for short rows
- *   csrc/artlite/moe_host.cpp:85-113   route_rows_scalar  top-k by ordered-int keys, weights in double
- *   csrc/artlite/moe_host.cpp:115-130  exp_nonpos      degree-12 Taylor e^x for x <= 0 (the k == 8 softmax path)
- *   csrc/artlite/moe_host.cpp:138-214  route_rows_avx512  which rows take exp_nonpos (k == 8, softmax, no NaN)
- *   csrc/artlite/moe_host.cpp:216-239  route_rows / moe_route  path choice and argument checks
- *   csrc/artlite/moe_host.cpp:241-275  moe_plan        histogram, scan, stable permute, chunk deal, pos
- *   csrc/artlite/dequant.cpp:43-169    per-format block dequant (fp32, no FMA: build with -ffp-contract=off)
+ *   csrc/artlite/moe_host.cpp:24-39    row_sum         numpy's pairwise summation order for short rows
+ *   csrc/artlite/moe_host.cpp:45-73   route_rows_scalar  top-k by ordered-int keys, weights in double
+ *   csrc/artlite/moe_host.cpp:75-90  exp_nonpos      degree-12 Taylor e^x for x <= 0 (the k == 8 softmax path)
+ *   csrc/artlite/moe_host.cpp:98-174  route_rows_avx512  which rows take exp_nonpos (k == 8, softmax, no NaN)
+ *   csrc/artlite/moe_host.cpp:176-199  route_rows / moe_route  path choice and argument checks
+ *   csrc/artlite/moe_host.cpp:201-235  moe_plan        histogram, scan, stable permute, chunk deal, pos
+ *   csrc/artlite/dequant.cpp:21-147    per-format block dequant (fp32, no FMA: build with -ffp-contract=off)
  *
  * Every function returns 0 on success or a negative status (the reference throws artlite::Error instead).
  */
@@ -27,7 +27,7 @@
 #define ORACLE_EINVAL -1
 #define ORACLE_ECAPACITY -2
 
-/* numpy's pairwise sum of a short row (moe_host.cpp:64-79): plain for n < 8, else 8 accumulators */
+/* numpy's pairwise sum of a short row (moe_host.cpp:24-39): plain for n < 8, else 8 accumulators */
 static double row_sum(const double* a, int n) {
   if (n < 8) {
     double s = 0;
@@ -44,9 +44,9 @@ static double row_sum(const double* a, int n) {
   return s;
 }
 
-static const double kMinWeightSum = 6.103515625e-5; /* 2^-14 (moe_host.cpp:81) */
+static const double kMinWeightSum = 6.103515625e-5; /* 2^-14 (moe_host.cpp:41) */
 
-/* e^x for x <= 0 as the reference's vector path computes it (moe_host.cpp:115-130): x = n ln2 + r with a two-part
+/* e^x for x <= 0 as the reference's vector path computes it (moe_host.cpp:75-90): x = n ln2 + r with a two-part
  * ln 2, a degree-12 Taylor polynomial in r by Horner with fused multiply-adds, times 2^n; x clamped at -708. */
 static double exp_nonpos(double x) {
   const double log2e = 1.4426950408889634, ln2hi = 6.93147180369123816490e-01, ln2lo = 1.90821492927058770002e-10;
@@ -70,18 +70,18 @@ static inline uint32_t f2u(float f) {
   return u;
 }
 
-/* A logit's ordered key (moe_host.cpp:95-96): (bits(l + 0) flipped to an unsigned order) << 32 | ~id. */
+/* A logit's ordered key (moe_host.cpp:55-56): (bits(l + 0) flipped to an unsigned order) << 32 | ~id. */
 static inline uint64_t route_key(float l, int x) {
   const uint32_t u = f2u(l + 0.0f);
   return (uint64_t)(u ^ ((u >> 31) ? 0xFFFFFFFFu : 0x80000000u)) << 32 | (uint32_t)(~(uint32_t)x);
 }
 
-/* The logit of expert x in a token's row (moe_host.cpp:93-95: column x / per_col at its pitch). */
+/* The logit of expert x in a token's row (moe_host.cpp:53-55: column x / per_col at its pitch). */
 static inline float logit_at(const float* p, int x, int per_col, int64_t pitch) {
   return p[(int64_t)(x / per_col) * pitch + x % per_col];
 }
 
-/* moe_route (moe_host.cpp:226-239, rows as route_rows_scalar :85-113 and, for the weights of k == 8 softmax rows
+/* moe_route (moe_host.cpp:186-199, rows as route_rows_scalar :45-73 and, for the weights of k == 8 softmax rows
  * without a NaN on the vector path's shapes, exp_nonpos as route_rows_avx512 :199-212). */
 int oracle_moe_route(const float* logits, int64_t n, int64_t row, int per_col, int64_t pitch, int E, int k,
                      int sigmoid, int32_t* ids, float* weights) {
@@ -107,7 +107,7 @@ int oracle_moe_route(const float* logits, int64_t n, int64_t row, int per_col, i
       top[j] = key;
     }
     const int32_t first = (int32_t)(~(uint32_t)top[0]);
-    /* (the vector path subtracts logits + 0.0f, moe_host.cpp:192: the same differences, -0 and +0 alike) */
+    /* (the vector path subtracts logits + 0.0f, moe_host.cpp:152: the same differences, -0 and +0 alike) */
     const double l0 = (double)logit_at(p, first, per_col, pitch);
     const int taylor = vector_shape && !has_nan && k == 8 && !sigmoid;
     for (int j = 0; j < k; j++) {
@@ -133,7 +133,7 @@ int oracle_moe_route(const float* logits, int64_t n, int64_t row, int per_col, i
   return ORACLE_OK;
 }
 
-/* moe_plan (moe_host.cpp:241-275): an expert's (token, slot) pairs in pair order, in chunks of at most `chunk`, dealt
+/* moe_plan (moe_host.cpp:201-235): an expert's (token, slot) pairs in pair order, in chunks of at most `chunk`, dealt
  * to the cols columns in turn; pos[p] = (c cap + kk) chunk + j. Returns ORACLE_EINVAL on an id outside [0, E),
  * ORACLE_ECAPACITY when a column needs more than cap chunks. */
 int oracle_moe_plan(const int32_t* ids, int64_t n, int k, int E, int cols, int cap, int chunk, int32_t* experts,
@@ -187,7 +187,7 @@ done:
   return rc;
 }
 
-/* The expert-contiguous dispatch the CUDA path builds (the first three steps of moe_plan, moe_host.cpp:243-255):
+/* The expert-contiguous dispatch the CUDA path builds (the first three steps of moe_plan, moe_host.cpp:203-215):
  * offsets[E + 1] (exclusive scan of the per-expert pair counts) and perm[i] = the i-th pair in expert-then-pair order,
  * slot[p] = the position of pair p in perm. */
 int oracle_moe_dispatch(const int32_t* ids, int64_t n, int k, int E, int64_t* offsets, int32_t* perm, int32_t* slot) {
@@ -210,9 +210,9 @@ int oracle_moe_dispatch(const int32_t* ids, int64_t n, int k, int E, int64_t* of
   return ORACLE_OK;
 }
 
-/* ---- dequant (dequant.cpp:43-169), fp32 operations in the reference's order ---- */
+/* ---- dequant (dequant.cpp:21-147), fp32 operations in the reference's order ---- */
 
-static float f16(const uint8_t* p) { /* dequant.cpp:43-51 */
+static float f16(const uint8_t* p) { /* dequant.cpp:21-29 */
   uint16_t h;
   memcpy(&h, p, 2);
   const uint32_t s = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 31, m = h & 1023;
@@ -232,7 +232,7 @@ static float f16(const uint8_t* p) { /* dequant.cpp:43-51 */
   return s ? -v : v;
 }
 
-static void q4_0(const uint8_t* b, float* o) { /* dequant.cpp:62-69: w = (q - 8) d */
+static void q4_0(const uint8_t* b, float* o) { /* dequant.cpp:40-47: w = (q - 8) d */
   const float d = f16(b);
   for (int j = 0; j < 32; j++) {
     const int q = j < 16 ? b[2 + j] & 15 : b[2 + j - 16] >> 4;
@@ -240,7 +240,7 @@ static void q4_0(const uint8_t* b, float* o) { /* dequant.cpp:62-69: w = (q - 8)
   }
 }
 
-static void q4_1(const uint8_t* b, float* o) { /* dequant.cpp:71-78: w = d q + m */
+static void q4_1(const uint8_t* b, float* o) { /* dequant.cpp:49-56: w = d q + m */
   const float d = f16(b), m = f16(b + 2);
   for (int j = 0; j < 32; j++) {
     const int q = j < 16 ? b[4 + j] & 15 : b[4 + j - 16] >> 4;
@@ -248,12 +248,12 @@ static void q4_1(const uint8_t* b, float* o) { /* dequant.cpp:71-78: w = d q + m
   }
 }
 
-static void q8_0(const uint8_t* b, float* o) { /* dequant.cpp:80-84: w = d q */
+static void q8_0(const uint8_t* b, float* o) { /* dequant.cpp:58-62: w = d q */
   const float d = f16(b);
   for (int j = 0; j < 32; j++) o[j] = d * (float)(int8_t)b[2 + j];
 }
 
-/* Q4_K / Q5_K (dequant.cpp:86-103): 6-bit scales and mins of eight 32-groups packed in 12 bytes;
+/* Q4_K / Q5_K (dequant.cpp:64-81): 6-bit scales and mins of eight 32-groups packed in 12 bytes;
  * w = q (d sc_g) - dmin mn_g */
 static void q45_k(const uint8_t* b, float* o, int q5) {
   const float d = f16(b), dmin = f16(b + 2);
@@ -271,7 +271,7 @@ static void q45_k(const uint8_t* b, float* o, int q5) {
   }
 }
 
-static void q6_k(const uint8_t* b, float* o) { /* dequant.cpp:105-123: w = (q - 32) (sc_j d) */
+static void q6_k(const uint8_t* b, float* o) { /* dequant.cpp:83-101: w = (q - 32) (sc_j d) */
   const uint8_t *ql = b, *qh = b + 128;
   const int8_t* sc = (const int8_t*)(b + 192);
   const float d = f16(b + 208);
@@ -306,7 +306,7 @@ typedef struct {
   void (*block)(const uint8_t*, float*);
 } qtype_t;
 
-/* dequant.cpp:176-179's table, the formats this build reads */
+/* dequant.cpp:154-157's table, the formats this build reads */
 static const qtype_t TYPES[] = {{"F32", 1, 4, f32_1},      {"F16", 1, 2, f16_1},       {"BF16", 1, 2, bf16_1},
                                 {"Q4_0", 32, 18, q4_0},    {"Q4_1", 32, 20, q4_1},     {"Q8_0", 32, 34, q8_0},
                                 {"Q4_K", 256, 144, q4_k},  {"Q5_K", 256, 176, q5_k},   {"Q6_K", 256, 210, q6_k}};
@@ -317,7 +317,7 @@ int oracle_dequant_supported(const char* qtype) {
   return 0;
 }
 
-/* dequant_rows (dequant.cpp:196-210): n rows row_bytes apart, their first cols values, into out (n x cols fp32) */
+/* dequant_rows (dequant.cpp:174-188): n rows row_bytes apart, their first cols values, into out (n x cols fp32) */
 int oracle_dequant_rows(const char* qtype, const uint8_t* raw, int64_t n, int64_t row_bytes, int64_t cols,
                         float* out) {
   const qtype_t* t = NULL;

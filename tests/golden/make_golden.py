@@ -45,7 +45,8 @@ def route_cases() -> dict[str, np.ndarray]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=olib.reference_tree(), help="the reference checkout (default: ARTLITE_REF, "
+                    "else reference/ beside this repository)")
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     from tests.moe import ref  # the reference's NumPy oracle  # noqa: E402

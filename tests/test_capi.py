@@ -47,7 +47,7 @@ def test_version_and_last_error_without_gpu():
 
 
 def test_argument_errors_need_no_gpu():
-    """The reference's artlite::Error cases are checked before any CUDA call (moe_host.cpp:228)."""
+    """The reference's artlite::Error cases are checked before any CUDA call (moe_host.cpp:188)."""
     from artlite_b200 import Error
     from artlite_b200.moe import plan
     import numpy as np
@@ -73,7 +73,7 @@ def test_host_package_is_torch_free():
 
 
 def test_mirror_signatures():
-    """route / Plan.of keep the reference's parameters (src/artlite/moe/plan.py:124-156)."""
+    """route / Plan.of keep the reference's parameters (src/artlite/moe/plan.py:25-57)."""
     from artlite_b200.moe import plan
     p = inspect.signature(plan.route).parameters
     assert list(p)[:2] == ["logits", "k"] and all(p[n].kind == p[n].KEYWORD_ONLY for n in ("E", "per_col", "pitch",

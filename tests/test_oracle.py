@@ -71,7 +71,7 @@ def test_plan_bit_exact(golden, orc, case):
 
 
 def test_plan_errors(orc):
-    """moe_plan's two errors (moe_host.cpp:247, :263): an id outside [0, E) and a column over cap."""
+    """moe_plan's two errors (moe_host.cpp:207, :223): an id outside [0, E) and a column over cap."""
     ids = np.zeros((4, 2), np.int32)
     ids[3, 1] = 9
     with pytest.raises(olib.OracleError):
