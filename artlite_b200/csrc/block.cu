@@ -386,6 +386,9 @@ int artlite_moe_create(const artlite_moe_desc* desc, artlite_moe** out) {
   AL_TRY(h->xin.reserve(act * T * H));
   AL_TRY(h->yout.reserve(act * T * H));
   AL_CUDA(cudaMemsetAsync(h->status.ptr, 0, sizeof(DevStatus), h->st));
+  // the fused decode kernel's grid barrier, zeroed now: a forward captured into a graph must not allocate
+  AL_TRY(h->bar.reserve(64));
+  AL_CUDA(cudaMemsetAsync(h->bar.ptr, 0, 64, h->st));
   if (world > 1) AL_TRY(ep_create(h.get()));
   AL_CUDA(cudaStreamSynchronize(h->st));
   *out = h.release();

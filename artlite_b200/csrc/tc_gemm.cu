@@ -13,11 +13,13 @@
 //               per stage: 144 B a row for Q4_0 / Q4_K, 272 B for Q8_0) and the token rows (bf16, 128-byte swizzle);
 //               it also allocates and frees the 512 TMEM columns.
 //   warp 1      MMA issuer: tcgen05.mma kind::f16 (bf16 x bf16 -> fp32), one thread; tcgen05.commit frees stages.
-//   warps 2-9   dequant, two groups of four warps (two warps per SM sub-partition): in group g a thread per weight
-//               row decodes steps 2g and 2g + 1 (64 values each) of every 256-value stage, from only the raw bytes of
-//               those steps loaded into registers; the reference's exact fp32 values (magic-number byte conversion,
-//               f32x2 arithmetic), rounded once to bf16, written into the A stage in the UMMA K-major
-//               128-byte-swizzle layout; fence.proxy.async, then an mbarrier arrive.
+//   warps 2-9   dequant, every warp on every step in step order: thread (h, i) decodes values 32 h .. 32 h + 31 of
+//               A row i of each 64-value step (h = 0 for warps 2-5, 1 for warps 6-9) from only that block's raw bytes;
+//               the reference's exact fp32 values (magic-number byte conversion, f32x2 arithmetic), rounded once to
+//               bf16, written into the A stage in the UMMA K-major 128-byte-swizzle layout; fence.proxy.async, then
+//               every lane arrives on the stage's full barrier. A stage's writers wait on every phase of its empty
+//               barrier in order (a parity wait that skipped phases would have to infer them from other barriers,
+//               whose arrivals from the tensor core are not ordered for an observer).
 //   warps 10-13 epilogue: tcgen05.ld of 32 columns at a time, SwiGLU (gu) or the plain rows (down), bf16 stores.
 // Every mbarrier wait is bounded (kWaitCycles): on expiry the CTA records ARTLITE_ETIMEOUT in the status word, stops
 // issuing, lets copies and MMAs already issued land, frees its TMEM and exits.
@@ -39,7 +41,7 @@ constexpr int kThreads = 448;  // 14 warps: producer, MMA, 8 dequant, 4 epilogue
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at the B200's clocks
 
 __host__ __device__ constexpr int chunk_bytes(int qt) {  // raw bytes of 256 values of a row
-  return qt == ARTLITE_Q8_0 ? 272 : (qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_K) ? 144 : 0;
+  return qt == ARTLITE_Q8_0 ? 272 : (qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_K) ? 144 : qt == ARTLITE_Q5_K ? 176 : 0;
 }
 
 // raw weight stages: three of 18 KB for the 144-byte formats, two of 34 KB for Q8_0 (shared memory)
@@ -291,31 +293,78 @@ __device__ __forceinline__ void dq_q4_k_group(const uint32_t* w, int g, uint32_t
   }
 }
 
-// values 64 sub .. 64 sub + 63 of the stage (w: the row's raw bytes of the 256-value stage, as words) as 32 bf16 pairs
-template <int QT>
-__device__ __forceinline__ void dequant_step(const uint32_t* w, int sub, uint32_t (&o)[32]) {
+// Q5_K group g of the stage's super-block (176 bytes: d, dmin, the twelve scale bytes, qh[32], qs[128]): 32 values
+// q (d sc_g) - dmin mn_g with q = nibble | bit g of qh[l] << 4 (the reference's q45_k<true>)
+__device__ __forceinline__ void dq_q5_k_group(const uint32_t* w, int g, uint32_t* o16) {
+  const float d = half_at(w, 0), dmin = half_at(w, 2);
+  int sc, mn;
+  if (g < 4) {
+    sc = byte_at(w, 4 + g) & 63;
+    mn = byte_at(w, 8 + g) & 63;
+  } else {
+    sc = (byte_at(w, 12 + g - 4) & 15) | (byte_at(w, 4 + g - 4) >> 6) << 4;
+    mn = (byte_at(w, 12 + g - 4) >> 4) | (byte_at(w, 8 + g - 4) >> 6) << 4;
+  }
+  const uint64_t dsc = dup2(__fmul_rn(d, (float)sc)), ndmn = dup2(-__fmul_rn(dmin, (float)mn));
+  const uint64_t off = dup2(-8388608.0f);  // -2^23
+  const int wq = 12 + 8 * (g >> 1);        // the group's 32 qs bytes: words wq .. wq + 7 (qh: words 4 .. 11)
 #pragma unroll
-  for (int hb = 0; hb < 2; hb++) {
-    if constexpr (QT == ARTLITE_Q4_0) dq_q4_0_block(w, 18 * (2 * sub + hb), o + 16 * hb);
-    else if constexpr (QT == ARTLITE_Q8_0) dq_q8_0_block(w, 34 * (2 * sub + hb), o + 16 * hb);
-    else dq_q4_k_group(w, 2 * sub + hb, o + 16 * hb);
+  for (int k = 0; k < 8; k++) {
+    const uint32_t nib = (g & 1) ? (w[wq + k] >> 4) & 0x0F0F0F0Fu : w[wq + k] & 0x0F0F0F0Fu;
+    const uint32_t v = nib | (((w[4 + k] >> g) & 0x01010101u) << 4);
+    uint64_t a, b;
+    magic4(v, a, b);
+    o16[2 * k] = bf16x2(add2(mul2(add2(a, off), dsc), ndmn));
+    o16[2 * k + 1] = bf16x2(add2(mul2(add2(b, off), dsc), ndmn));
   }
 }
 
-// the 16-byte words of a row's stage bytes that dequant group grp (its steps 2 grp, 2 grp + 1) reads
-template <int QT>
-struct RawSpan {
-  // Q4_0: blocks 4 grp .. 4 grp + 3 = bytes 72 grp .. 72 grp + 71; Q8_0: bytes 136 grp ..; Q4_K: the header and
-  // qs bytes 16 + 64 grp ..
-  static constexpr int first(int grp) { return QT == ARTLITE_Q4_0 ? 4 * grp : QT == ARTLITE_Q8_0 ? 8 * grp : 0; }
-  static constexpr int count = QT == ARTLITE_Q8_0 ? 9 : 5;
+// the 16-byte chunks [lo, hi] of a row's stage bytes that block / group 2 sub + h of a 256-value chunk reads
+template <int QT, int H>
+struct BlockSpan {
+  static constexpr int b(int sub) { return 2 * sub + H; }
+  static constexpr int lo(int sub) {
+    return QT == ARTLITE_Q4_0 ? (18 * b(sub)) / 16 : QT == ARTLITE_Q8_0 ? (34 * b(sub)) / 16 : 0;
+  }
+  static constexpr int hi(int sub) {
+    return QT == ARTLITE_Q4_0 ? (18 * b(sub) + 17) / 16
+         : QT == ARTLITE_Q8_0 ? (34 * b(sub) + 33) / 16
+         : QT == ARTLITE_Q4_K ? 0 : 2;  // (Q4_K: the header; Q5_K: the header and qh)
+  }
+  // Q4_K / Q5_K: the group's qs bytes (Q4_K 16 + 32 sub, Q5_K 48 + 32 sub): chunks qlo, qlo + 1
+  static constexpr int qlo(int sub) { return QT == ARTLITE_Q4_K ? 1 + 2 * sub : 3 + 2 * sub; }
 };
+
+// block / group 2 sub + H of the stage row at src (its raw bytes, 16-byte chunks) as 16 bf16 pairs
+template <int QT, int H>
+__device__ __forceinline__ void dequant_block(const uint4* src, uint32_t* w, int sub, uint32_t (&o)[16]) {
+  using S = BlockSpan<QT, H>;
+#pragma unroll
+  for (int v = S::lo(sub); v <= S::hi(sub); v++) {
+    const uint4 u = src[v];
+    w[4 * v] = u.x, w[4 * v + 1] = u.y, w[4 * v + 2] = u.z, w[4 * v + 3] = u.w;
+  }
+  if constexpr (QT == ARTLITE_Q4_K || QT == ARTLITE_Q5_K) {
+#pragma unroll
+    for (int v = S::qlo(sub); v <= S::qlo(sub) + 1; v++) {
+      const uint4 u = src[v];
+      w[4 * v] = u.x, w[4 * v + 1] = u.y, w[4 * v + 2] = u.z, w[4 * v + 3] = u.w;
+    }
+  }
+  const int b = 2 * sub + H;
+  if constexpr (QT == ARTLITE_Q4_0) dq_q4_0_block(w, 18 * b, o);
+  else if constexpr (QT == ARTLITE_Q8_0) dq_q8_0_block(w, 34 * b, o);
+  else if constexpr (QT == ARTLITE_Q5_K) dq_q5_k_group(w, b, o);
+  else dq_q4_k_group(w, b, o);
+}
 
 // ---------------------------------------------------------------- the kernel
 
 // the kernel's shared-memory pipeline depth: A + B stages and raw weight stages, per format and mode
 __host__ __device__ constexpr int b_stage_bytes(bool pair) { return pair ? B_BYTES / 2 : B_BYTES; }
-__host__ __device__ constexpr int ab_stages(int qt, bool pair) { return pair ? (qt == ARTLITE_Q8_0 ? 4 : 5) : 3; }
+__host__ __device__ constexpr int ab_stages(int qt, bool pair) {
+  return pair ? (qt == ARTLITE_Q8_0 || qt == ARTLITE_Q5_K ? 4 : 5) : 3;
+}
 // the epilogue's transpose buffers: per epilogue warp 32 token rows of up to 32 bf16 values, rows 80 bytes apart
 // (16-byte row reads of 8 consecutive lanes fall in distinct banks)
 constexpr int kEpiRow = 80, kEpiWarp = 32 * kEpiRow;
@@ -339,7 +388,7 @@ __device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
   return r;
 }
 __device__ __forceinline__ void arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // the pair's TMA load: the bytes land in this CTA, the transaction count goes to the barrier at `bar` (a
 // shared::cluster address, here the leader CTA's)
@@ -367,7 +416,7 @@ __device__ __forceinline__ void commit_pair(uint64_t* bar) {
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
@@ -415,17 +464,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < SS; i++) {
-      mbar_init(&sm->full_a[i], 4 * NPEER);
+      mbar_init(&sm->full_a[i], 256 * NPEER);
       mbar_init(&sm->full_b[i], 1);
       mbar_init(&sm->empty[i], 1);
     }
     for (int i = 0; i < R; i++) {
       mbar_init(&sm->raw_full[i], 1);
-      mbar_init(&sm->raw_empty[i], 8);
+      mbar_init(&sm->raw_empty[i], 256);
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&sm->tfull[i], 1);
-      mbar_init(&sm->tempty[i], 4 * NPEER);
+      mbar_init(&sm->tempty[i], 128 * NPEER);
     }
     sm->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -521,9 +570,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
       if (++acc == 2) acc = 0, aph ^= 1;
     }
   } else if (warp >= 2 && warp < 10) {
-    // ---------------- dequant: two groups of 4 warps; thread i of group grp owns A row i and writes steps 2 grp and
-    // 2 grp + 1 of every 256-value stage (64 values each), reading only the raw bytes of those steps
-    const int grp = (warp - 2) >> 2, i = threadIdx.x - 64 - 128 * grp;
+    // ---------------- dequant: all eight warps on every step, in step order (as every other role waits on every phase
+    // of the barriers it uses: a stage's writers never skip one of its phases). Thread (h, i), h = its warp's half
+    // (warps 2-5: 0, 6-9: 1), i its A row, decodes values 32 h .. 32 h + 31 of each 64-value step of its row: one
+    // 32-value block (Q4_0 / Q8_0) or group (Q4_K / Q5_K), from only that block's raw bytes.
+    const int h = (warp - 2) >> 2, i = threadIdx.x - 64 - 128 * h;
     int raw_row = i;
     if (GU) {
       const int q = i >> 5, l = i & 31;
@@ -534,49 +585,29 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
     for (int t = t0; t < total; t += tstep) {
       for (int kc = 0; kc < p.K / KC; kc++) {
         if (!wait(&sm->abort, &sm->raw_full[r], rph, p.status, 6)) goto out;
-        uint32_t w[NW + 4];
         const uint4* src = reinterpret_cast<const uint4*>(sR + r * BM * CB + raw_row * CB);
-        if (grp == 0) {
 #pragma unroll
-          for (int v = 0; v < (QT == ARTLITE_Q8_0 ? 9 : 5); v++) {
-            const uint4 u = src[v];
-            w[4 * v] = u.x, w[4 * v + 1] = u.y, w[4 * v + 2] = u.z, w[4 * v + 3] = u.w;
-          }
-        } else {
-          if (QT == ARTLITE_Q4_K) {  // (the header)
-            const uint4 u = src[0];
-            w[0] = u.x, w[1] = u.y, w[2] = u.z, w[3] = u.w;
-          }
-#pragma unroll
-          for (int v = (QT == ARTLITE_Q4_K ? 5 : RawSpan<QT>::first(1));
-               v < (QT == ARTLITE_Q4_K ? 9 : RawSpan<QT>::first(1) + RawSpan<QT>::count); v++) {
-            const uint4 u = src[v];
-            w[4 * v] = u.x, w[4 * v + 1] = u.y, w[4 * v + 2] = u.z, w[4 * v + 3] = u.w;
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm->raw_empty[r]);
-        if (++r == R) r = 0, rph ^= 1;
-#pragma unroll
-        for (int j = 0; j < 2; j++) {
-          const int sub = 2 * grp + j;
+        for (int sub = 0; sub < KC / BK; sub++) {
           const int step = n + sub, s = step % SS;
           const uint32_t ph = (step / SS) & 1;
-          uint32_t o[32];
-          if (grp == 0) dequant_step<QT>(w, j, o);
-          else dequant_step<QT>(w, 2 + j, o);
+          uint32_t w[NW + 4];
+          uint32_t o[16];
+          const int blk = 2 * sub + h;  // (the 32-value block / group)
+          if (h == 0) dequant_block<QT, 0>(src, w, sub, o);
+          else dequant_block<QT, 1>(src, w, sub, o);
           if (!wait(&sm->abort, &sm->empty[s], ph ^ 1, p.status, 7)) goto out;
           uint8_t* row = sA + s * A_BYTES + i * 128;
 #pragma unroll
-          for (int c = 0; c < 8; c++)
-            *reinterpret_cast<uint4*>(row + ((c ^ (i & 7)) << 4)) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+          for (int c = 0; c < 4; c++)
+            *reinterpret_cast<uint4*>(row + (((4 * h + c) ^ (i & 7)) << 4)) =
+                make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+          (void)blk;
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          if (lane == 0) {
-            if (PAIR && crank != 0) arrive_cluster(full_a0 + s * (uint32_t)sizeof(uint64_t));
-            else mbar_arrive(&sm->full_a[s]);
-          }
+          if (PAIR && crank != 0) arrive_cluster(full_a0 + s * (uint32_t)sizeof(uint64_t));
+          else mbar_arrive(&sm->full_a[s]);
         }
+        mbar_arrive(&sm->raw_empty[r]);  // (every lane, after its last use of the stage's bytes)
+        if (++r == R) r = 0, rph ^= 1;
         n += KC / BK;
       }
     }
@@ -646,11 +677,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
         }
       }
       fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (PAIR && crank != 0) arrive_cluster(tempty0 + acc * (uint32_t)sizeof(uint64_t));
-        else mbar_arrive(&sm->tempty[acc]);
-      }
+      if (PAIR && crank != 0) arrive_cluster(tempty0 + acc * (uint32_t)sizeof(uint64_t));
+      else mbar_arrive(&sm->tempty[acc]);
       if (++acc == 2) acc = 0, aph ^= 1;
     }
   }
@@ -892,12 +920,12 @@ bool tc_supported(int qtype, int K, int N) {
 
 size_t tc_sched_bytes(int E) { return sizeof(int32_t) * (E + 1); }
 
-// the pair (cta_group::2) kernel with ARTLITE_TC_PAIR=1 (measured slower than the one-CTA kernel at the benchmark's
-// shapes: the token operand's L2 traffic is not what bounds it), when the shape splits into pairs
+// the pair (cta_group::2) kernel where the shape splits into pairs (ARTLITE_TC_PAIR=0: the one-CTA kernel): it halves
+// each SM's token-operand traffic (measured at T = 16384, Q4_0: gate/up 1.08 -> 1.01 ms, down 0.60 -> 0.55 ms)
 bool tc_use_pair(int N, bool gu) {
-  const char* v = getenv("ARTLITE_TC_PAIR");
-  const bool on = v && v[0] == '1';
-  return on && (gu ? N % 128 == 0 : N % 256 == 0);
+  const char* v = getenv("ARTLITE_TC_PAIR");  // (read per launch: a caller may switch it between forwards)
+  const bool off = v && v[0] == '0';
+  return !off && (gu ? N % 128 == 0 : N % 256 == 0);
 }
 
 int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
@@ -962,6 +990,7 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
     AL_TC_CASE(ARTLITE_Q4_0)
     AL_TC_CASE(ARTLITE_Q8_0)
     AL_TC_CASE(ARTLITE_Q4_K)
+    AL_TC_CASE(ARTLITE_Q5_K)
     default: break;
   }
 #undef AL_TC_CASE

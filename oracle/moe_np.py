@@ -225,27 +225,33 @@ class Layer:
     gate: np.ndarray
     up: np.ndarray
     down: np.ndarray
+    down_qtype: str = ""  # (the down tensor's own type, as mixed files have it; "": qtype)
+
+    @property
+    def dqtype(self) -> str:
+        return self.down_qtype or self.qtype
 
     def expert(self, e: int) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
         """(gate (F, H), up (F, H), down (H, F)) fp32 of expert e (``tests/moe/ref.py:27-40``'s row ranges)."""
         F, H = self.F, self.H
         return (dequant(self.qtype, self.gate[e * F:(e + 1) * F], H),
                 dequant(self.qtype, self.up[e * F:(e + 1) * F], H),
-                dequant(self.qtype, self.down[e * H:(e + 1) * H], F))
+                dequant(self.dqtype, self.down[e * H:(e + 1) * H], F))
 
 
 def make_block(seed: int, T: int, *, H: int = 2048, E: int = 128, F: int = 768, qtype: str = "Q4_0",
-               x_bf16: bool = True, zipf: float = 0.0) -> tuple[Layer, np.ndarray, np.ndarray]:
+               x_bf16: bool = True, zipf: float = 0.0, down_qtype: str = "") -> tuple[Layer, np.ndarray, np.ndarray]:
     """(layer, x (T, H): bf16 bits if ``x_bf16`` else fp32, router bias (E,) fp32) from one seeded stream: router,
-    x, gate, up, down; ``zipf`` s > 0 adds bias_e = -s ln(r_e), r a seeded permutation of 1..E (drawn last)."""
+    x, gate, up, down; ``zipf`` s > 0 adds bias_e = -s ln(r_e), r a seeded permutation of 1..E (drawn last);
+    ``down_qtype`` the down tensor's own type (default: qtype)."""
     rng = np.random.default_rng(seed)
     router = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
     x = rng.standard_normal((T, H)).astype(np.float32)
     gate = random_blocks(rng, qtype, E * F, H)
     up = random_blocks(rng, qtype, E * F, H)
-    down = random_blocks(rng, qtype, E * H, F)
+    down = random_blocks(rng, down_qtype or qtype, E * H, F)
     bias = np.zeros(E, np.float32)
     if zipf:
         r = rng.permutation(E) + 1
         bias = (-zipf * np.log(r)).astype(np.float32)
-    return Layer(qtype, H, E, F, router, gate, up, down), (to_bf16_bits(x) if x_bf16 else x), bias
+    return Layer(qtype, H, E, F, router, gate, up, down, down_qtype), (to_bf16_bits(x) if x_bf16 else x), bias

@@ -23,7 +23,7 @@ def expert_fn(layer: moe_np.Layer):
     def get(e: int):
         return (o.dequant_rows(layer.qtype, layer.gate[e * F:(e + 1) * F], H),
                 o.dequant_rows(layer.qtype, layer.up[e * F:(e + 1) * F], H),
-                o.dequant_rows(layer.qtype, layer.down[e * H:(e + 1) * H], F))
+                o.dequant_rows(layer.dqtype, layer.down[e * H:(e + 1) * H], F))
     return get
 
 
@@ -45,7 +45,8 @@ def make_block(layer: moe_np.Layer, T: int, *, act: str, path: str, gating: str 
     b = MoEBlock(hidden=layer.H, n_experts=layer.E, top_k=top_k, expert_ffn=layer.F, max_tokens=T, act_dtype=act,
                  path=path, gating=gating, n_layers=n_layers)
     for L in range(n_layers):
-        b.set_weights(L, gate=layer.gate, up=layer.up, down=layer.down, router=layer.router, qtype=layer.qtype)
+        b.set_weights(L, gate=layer.gate, up=layer.up, down=layer.down, router=layer.router, qtype=layer.qtype,
+                      down_qtype=layer.dqtype)
     return b
 
 

@@ -140,3 +140,32 @@ def test_config5_full_expert_count():
     b.close()
     ids, w = check_routing(dbg, x[:64], layer, 8)
     assert moe_np.rel_max(y64, torch_moe_ffn(layer, x[:64], ids, w)) <= BF16_TOL
+
+
+@pytest.mark.parametrize("qtype,T,zipf", [("Q4_0", 16384, 0.0), ("Q8_0", 4096, 1.1), ("Q4_K", 16384, 0.0)])
+def test_tcgen05_many_repeats_bit_identical(qtype, T, zipf):
+    """Forty forwards of a benchmarked shape in one block, device buffers in and out: every output bit-identical to
+    the first, and the first within tolerance of the reference on every token. The tcgen05 pipeline's waits are the
+    kind of code whose races show up as a rare wrong tile: this is the repetition harness for them."""
+    import torch
+    layer, x, bias = moe_np.make_block(45, T, qtype=qtype, zipf=zipf)
+    b = make_block(layer, T, act="bf16", path="tc")
+    if zipf:
+        b.set_router_bias(0, bias)
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    yd = torch.empty_like(xd)
+    outs = []
+    st = torch.cuda.current_stream().cuda_stream  # (the forwards and the copies in one stream order)
+    for _ in range(40):
+        b.forward_ptr(xd.data_ptr(), yd.data_ptr(), T, stream=st)
+        outs.append(yd.clone())
+    torch.cuda.synchronize()
+    b.sync()
+    first = outs[0]
+    bad = [i for i, o in enumerate(outs) if not torch.equal(o, first)]
+    dbg = b.debug(T)
+    b.close()
+    assert not bad, f"forwards {bad} differ from the first"
+    ids, w = check_routing(dbg, x, layer, 8, bias=bias if zipf else None)
+    y = moe_np.bf16_to_f32(first.cpu().numpy().view(np.uint16))
+    assert moe_np.rel_max(y, torch_moe_ffn(layer, x, ids, w)) <= BF16_TOL
