@@ -155,10 +155,12 @@ def test_tcgen05_many_repeats_bit_identical(qtype, T, zipf):
     xd = torch.from_numpy(x.view(np.int16)).cuda()
     yd = torch.empty_like(xd)
     outs = []
-    st = torch.cuda.current_stream().cuda_stream  # (the forwards and the copies in one stream order)
-    for _ in range(40):
-        b.forward_ptr(xd.data_ptr(), yd.data_ptr(), T, stream=st)
-        outs.append(yd.clone())
+    stream = torch.cuda.Stream()  # (the forwards and the copies in one stream order; not the legacy default stream,
+    torch.cuda.synchronize()      # whose handle 0 would mean "the block's own stream" to forward_ptr)
+    with torch.cuda.stream(stream):
+        for _ in range(40):
+            b.forward_ptr(xd.data_ptr(), yd.data_ptr(), T, stream=stream.cuda_stream)
+            outs.append(yd.clone())
     torch.cuda.synchronize()
     b.sync()
     first = outs[0]
