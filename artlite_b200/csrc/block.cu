@@ -387,8 +387,8 @@ int artlite_moe_create(const artlite_moe_desc* desc, artlite_moe** out) {
   AL_TRY(h->yout.reserve(act * T * H));
   AL_CUDA(cudaMemsetAsync(h->status.ptr, 0, sizeof(DevStatus), h->st));
   // the fused decode kernel's grid barrier, zeroed now: a forward captured into a graph must not allocate
-  AL_TRY(h->bar.reserve(64));
-  AL_CUDA(cudaMemsetAsync(h->bar.ptr, 0, 64, h->st));
+  AL_TRY(h->bar.reserve(1024));
+  AL_CUDA(cudaMemsetAsync(h->bar.ptr, 0, 1024, h->st));
   if (world > 1) AL_TRY(ep_create(h.get()));
   AL_CUDA(cudaStreamSynchronize(h->st));
   *out = h.release();
@@ -628,6 +628,15 @@ int artlite_moe_set_shared(artlite_moe* h, int layer, int ffn, int qtype, const 
     for (int64_t i = 0; i < T; i++) io[i] = (int32_t)i;
     AL_CUDA(cudaMemcpyAsync(h->sh_iota.ptr, io.data(), sizeof(int32_t) * T, cudaMemcpyHostToDevice, h->st));
     AL_TRY(wait(h->st, 0));
+  }
+  L.sh_has_dm = false;
+  if (qtype == ARTLITE_Q4_K && down_qtype == ARTLITE_Q4_K && F % 64 == 0 && H % 128 == 0 &&
+      (!gate_inp || gate_dtype == ARTLITE_F32)) {  // (the fused decode kernel can run this shared expert)
+    AL_TRY(make_raw_map(&L.sh_dm_gate, L.sh_gate.ptr, L.sh_rb_gu, F, 144, 64));
+    AL_TRY(make_raw_map(&L.sh_dm_up, L.sh_up.ptr, L.sh_rb_gu, F, 144, 64));
+    AL_TRY(make_raw_map(&L.sh_dm_down, L.sh_down.ptr, L.sh_rb_dn, H, 144, 128));
+    AL_TRY(h->sh_hq.reserve(std::max(h->sh_hq.bytes, (size_t)(sizeof(uint16_t) * T * F + sizeof(float) * T * (F / 32)))));
+    L.sh_has_dm = true;
   }
   L.has_shared = true;
   return wait(h->st, 0);

@@ -38,6 +38,9 @@ struct artlite_moe {
     int sh_F = 0, sh_qtype = -1, sh_down_qtype = -1, sh_gate_dtype = -1;
     int64_t sh_rb_gu = 0, sh_rb_dn = 0;
     artlite::DevBuf sh_gate, sh_up, sh_down, sh_ginp;
+    // Q4_K shared experts: tensor maps of its raw rows for the fused decode kernel (as dm_* for the routed experts)
+    bool sh_has_dm = false;
+    CUtensorMap sh_dm_gate, sh_dm_up, sh_dm_down;
   };
   std::vector<Layer> layers;
   // workspaces
@@ -46,6 +49,7 @@ struct artlite_moe {
   artlite::DevBuf xn;  // the normed input rows (layers with artlite_moe_set_norm)
   artlite::DevBuf bar;  // the fused decode kernel's grid barrier (zeroed once; left zeroed by every complete run)
   artlite::DevBuf sh_y, sh_s, sh_iota, sh_off;  // the shared expert's outputs (T rows), gates (T), 0..T-1, {0, T} / {T}
+  artlite::DevBuf sh_hq;  // the fused decode kernel's shared-expert h rows (fragment order, then their group sums)
   int64_t last_T = 0;
   int last_path = 0;
   // recorded on the forward's stream at the end of every forward (and graph replay): artlite_moe_sync waits for it,

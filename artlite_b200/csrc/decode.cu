@@ -35,6 +35,8 @@ constexpr long long kBarrierCycles = 4000000000LL;  // about 2 s
 
 struct GridBar {
   unsigned count, gen;
+  unsigned pad[14];
+  int tb_done[kMaxPairs / 4];  // per block of 4 tokens: router units finished (the last one routes the tokens)
 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -72,6 +74,8 @@ __device__ __forceinline__ bool grid_sync(GridBar* b, DevStatus* st, int where) 
   return ok != 0;
 }
 
+static_assert(sizeof(GridBar) <= 1024, "the handle reserves 1 KiB for the grid barrier and the token-block counts");
+
 struct DecodeArgs {
   const void* x;
   int x_dtype;
@@ -94,6 +98,17 @@ struct DecodeArgs {
   int32_t *counts, *perm, *slot;
   float *h, *y;
   const void* res;  // rows added last to the output (the residual of a layer with a norm), or null
+  // the shared expert (Q4_K, ref.shared_expert): its raw rows' maps, width, gate vector (fp32, or null: ungated), its
+  // h rows (fragment order) and sums, its output rows (fp32, T x H), the per-token gates, 0 .. T - 1
+  bool shared;
+  CUtensorMap smg, smu, smd;
+  const uint8_t *sh_gate, *sh_up, *sh_down;  // (their raw rows)
+  int64_t sh_rb_dn;
+  int Fs;
+  const float* sgate;
+  uint4* shq;
+  float *shs, *shy, *sh_s;
+  const int32_t* iota;
   void* out;
   GridBar* bar;
   DevStatus* status;
@@ -140,7 +155,9 @@ __device__ __forceinline__ void router_unit(const DecodeArgs& a, int t, int e, i
 // warp one block over a quarter of H (each lane 4 consecutive values of every 128), so that a router row and an x row
 // are read 4 times less often than a warp per logit reads them; the quarters' sums meet in shared memory (part: 128
 // floats) and add in a fixed order, + bias
+template <int J>
 __device__ __forceinline__ void router_tiles(const DecodeArgs& a, float* part, int warp, int lane) {
+  __shared__ int route_tb[2];
   const int TB = (a.T + 3) >> 2, EB = a.E >> 2, units = TB * EB;
   const int kq = a.H >> 2;
   for (int u0 = blockIdx.x * 2; u0 < units; u0 += gridDim.x * 2) {  // (the same trip count for the whole CTA)
@@ -196,6 +213,31 @@ __device__ __forceinline__ void router_tiles(const DecodeArgs& a, float* part, i
           a.logits[(int64_t)t * a.E + e] = a.bias ? v + a.bias[e] : v;
         }
       }
+      __threadfence();
+    }
+    // a token block is routed by the CTA that writes its last logits: the logits published (fence), one count a unit;
+    // the CTA whose count completes the block's E / 4 units routes its tokens (a warp each) and resets the count
+    if (a.T > rq::kWarps) {
+      __syncthreads();
+      if (threadIdx.x < 2) {
+        const int u2 = u0 + threadIdx.x;
+        int tb = -1;
+        if (u2 < units) {
+          __threadfence();
+          if (atomicAdd(&a.bar->tb_done[u2 / EB], 1) == EB - 1) {
+            __threadfence();
+            tb = u2 / EB;
+            a.bar->tb_done[tb] = 0;
+          }
+        }
+        route_tb[threadIdx.x] = tb;
+      }
+      __syncthreads();
+      const int tb = route_tb[warp >> 2], t = tb * 4 + (warp & 3);
+      if (tb >= 0 && t < a.T) {
+        RouteArgs r{a.logits, a.T, a.E, a.E, 0, a.E, a.K, a.gating, a.vector_shape, a.ids, a.w};
+        route_row<J>(r, t, lane);
+      }
     }
     __syncthreads();
   }
@@ -206,6 +248,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
   extern __shared__ __align__(128) float sm[];
   __shared__ int64_t s64[32];
   __shared__ int32_t s32[32];
+  __shared__ int32_t sh_uo[2];  // (the shared expert's item offsets and pair offsets: one expert of T pairs)
+  __shared__ int64_t sh_off[2];
   const int P = a.T * a.K, E = a.E;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // shared memory: x staging | ids | w | perm | slot | cnt | run | wc | offs | uo_gu | uo_dn
@@ -221,6 +265,22 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
   int32_t* uo_gu = reinterpret_cast<int32_t*>(offs + kMaxExperts + 1);
   int32_t* uo_dn = uo_gu + kMaxExperts + 1;
 
+  // the router rows and the tokens' x, prefetched into L2 at once by every CTA (its share, one bulk prefetch each):
+  // the router phase's loads are then L2 hits instead of a few rounds of DRAM latency
+  if (threadIdx.x == 0) {
+    const int64_t rbytes = (int64_t)a.E * a.H * (a.router_dtype == ARTLITE_F32 ? 4 : 2);
+    const int64_t xbytes = (int64_t)a.T * a.H * (a.x_dtype == ARTLITE_BF16 ? 2 : 4);
+    const int64_t rc = ((rbytes + gridDim.x - 1) / gridDim.x + 15) & ~(int64_t)15;
+    const int64_t r0 = rc * blockIdx.x;
+    if (r0 < rbytes)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const uint8_t*>(a.router) + r0),
+                   "r"((uint32_t)min64(rc, rbytes - r0)) : "memory");
+    const int64_t xc = ((xbytes + gridDim.x - 1) / gridDim.x + 15) & ~(int64_t)15;
+    const int64_t x0 = xc * blockIdx.x;
+    if (x0 < xbytes)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const uint8_t*>(a.x) + x0),
+                   "r"((uint32_t)min64(xc, xbytes - x0)) : "memory");
+  }
   griddep_wait();
   constexpr bool kMs = QG == ARTLITE_Q4_K;  // (then QD == QG)
   ms::Pipe pp{};
@@ -240,8 +300,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     }
   }
   // ---- 1. router logits (and the tokens' x in fragment order)
-  if (a.H % 512 == 0 && E % 4 == 0) {
-    router_tiles(a, sm, warp, lane);  // (the staging area is free until phase 3; its end holds the mbarriers)
+  const bool tiles = a.H % 512 == 0 && E % 4 == 0;
+  if (tiles) {
+    router_tiles<J>(a, sm, warp, lane);  // (the staging area is free until phase 3; its end holds the mbarriers)
   } else {
     for (int u = blockIdx.x * rq::kWarps + warp; u < a.T * E; u += gridDim.x * rq::kWarps)
       router_unit(a, u / E, u % E, lane);
@@ -262,6 +323,26 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
       if (t == 0) a.xs[u >> 2] = part;
     }
   }
+  if (a.shared) {  // the shared expert's gates: a warp per token, as launch_shared_gate (combine.cu)
+    for (int t = blockIdx.x * rq::kWarps + warp; t < a.T; t += gridDim.x * rq::kWarps) {
+      float acc = 0.0f;
+      if (a.sgate) {
+        for (int c = lane * 8; c < a.H; c += 256) {
+          float xv[4], xw[4];
+#pragma unroll
+          for (int hh = 0; hh < 2; hh++) {
+            load4(a.x, a.x_dtype, (int64_t)t * a.H + c + 4 * hh, xv);
+            load4(a.sgate, ARTLITE_F32, c + 4 * hh, xw);
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc = fmaf(xv[j], xw[j], acc);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+      }
+      if (lane == 0) a.sh_s[t] = a.sgate ? __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-acc))) : 1.0f;
+    }
+  }
   if (!grid_sync(a.bar, a.status, 1)) return;
   // ---- 2. routing and the dispatch
   const bool local = a.T <= rq::kWarps;  // every CTA routes all tokens itself
@@ -270,9 +351,11 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     if (local) {
       if (warp < a.T) route_row<J>(r, warp, lane);
     } else {
-      const int t = blockIdx.x * rq::kWarps + warp;
-      if (t < a.T) route_row<J>(r, t, lane);
-      if (!grid_sync(a.bar, a.status, 2)) return;
+      if (!tiles) {  // (the router tiles route each token block as it completes: done before barrier 1)
+        const int t = blockIdx.x * rq::kWarps + warp;
+        if (t < a.T) route_row<J>(r, t, lane);
+        if (!grid_sync(a.bar, a.status, 2)) return;
+      }
       for (int p = threadIdx.x; p < P; p += kThreads) ids_s[p] = __ldcg(a.ids + p), w_s[p] = __ldcg(a.w + p);
     }
   }
@@ -350,11 +433,20 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     g.x_dtype = a.x_dtype;
     g.k = a.K;
     g.out = a.h;
-    const int total = uo_gu[E];
+    const int routed = uo_gu[E];
+    const int sh_items = a.shared ? (a.T + kGemvTokens - 1) / kGemvTokens * (a.Fs / 64) : 0;
+    const int total = routed + sh_items;
     const int i0 = (int)((int64_t)blockIdx.x * total / gridDim.x), i1 = (int)((int64_t)(blockIdx.x + 1) * total / gridDim.x);
     if constexpr (kMs) {
-      ms::Gemv m{&a.mg, &a.mu, a.H, a.F, E, a.K, a.xq, a.xs, a.hq, a.hs, nullptr};
-      ms::run<true>(m, uo_gu, offs, perm_s, reinterpret_cast<uint8_t*>(xs), pp, i0, i1, a.status);
+      ms::Gemv m{&a.mg, &a.mu, a.H, a.F, E, a.K, a.xq, a.xs, a.hq, a.hs, nullptr, a.gate, a.up, a.rb_gu};
+      ms::run<true>(m, uo_gu, offs, perm_s, reinterpret_cast<uint8_t*>(xs), pp, i0, min(i1, routed), a.status);
+      if (i1 > routed) {  // (the shared expert: one expert, every token a pair of its own, in token order)
+        sh_uo[0] = 0, sh_uo[1] = sh_items, sh_off[0] = 0, sh_off[1] = a.T;
+        __syncthreads();
+        ms::Gemv ms_{&a.smg, &a.smu, a.H, a.Fs, 1, 1, a.xq, a.xs, a.shq, a.shs, nullptr, a.sh_gate, a.sh_up, a.rb_gu};
+        ms::run<true>(ms_, sh_uo, sh_off, a.iota, reinterpret_cast<uint8_t*>(xs), pp, max(i0, routed) - routed,
+                      i1 - routed, a.status);
+      }
     } else {
       rq::run_items<QG, true>(g, a.R_gu, uo_gu, offs, perm_s, xs, i0, i1);
     }
@@ -373,11 +465,20 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     d.x_dtype = ARTLITE_F32;
     d.k = a.K;
     d.out = a.y;
-    const int total = uo_dn[E];
+    const int routed = uo_dn[E];
+    const int sh_items = a.shared ? (a.T + kGemvTokens - 1) / kGemvTokens * (a.H / 128) : 0;
+    const int total = routed + sh_items;
     const int i0 = (int)((int64_t)blockIdx.x * total / gridDim.x), i1 = (int)((int64_t)(blockIdx.x + 1) * total / gridDim.x);
     if constexpr (kMs) {
-      ms::Gemv m{&a.md, nullptr, a.F, a.H, E, a.K, a.hq, a.hs, nullptr, nullptr, a.y};
-      ms::run<false>(m, uo_dn, offs, perm_s, reinterpret_cast<uint8_t*>(xs), pp, i0, i1, a.status);
+      ms::Gemv m{&a.md, nullptr, a.F, a.H, E, a.K, a.hq, a.hs, nullptr, nullptr, a.y, a.down, nullptr, a.rb_dn};
+      ms::run<false>(m, uo_dn, offs, perm_s, reinterpret_cast<uint8_t*>(xs), pp, i0, min(i1, routed), a.status);
+      if (i1 > routed) {
+        sh_uo[0] = 0, sh_uo[1] = sh_items, sh_off[0] = 0, sh_off[1] = a.T;
+        __syncthreads();
+        ms::Gemv ms_{&a.smd, nullptr, a.Fs, a.H, 1, 1, a.shq, a.shs, nullptr, nullptr, a.shy, a.sh_down, nullptr, a.sh_rb_dn};
+        ms::run<false>(ms_, sh_uo, sh_off, a.iota, reinterpret_cast<uint8_t*>(xs), pp, max(i0, routed) - routed,
+                       i1 - routed, a.status);
+      }
     } else {
       rq::run_items<QD, false>(d, a.R_dn, uo_dn, offs, perm_s, xs, i0, i1);
     }
@@ -400,6 +501,15 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
         acc[6] = fmaf(wi, y1.z, acc[6]), acc[7] = fmaf(wi, y1.w, acc[7]);
       }
       const int64_t o = (int64_t)t * a.H + c;
+      if (a.shared) {  // (the shared expert's gated rows, after the routed sum)
+        const float si = a.sh_s[t];
+        const float4* sr = reinterpret_cast<const float4*>(a.shy + o);
+        const float4 s0 = __ldcg(sr), s1 = __ldcg(sr + 1);
+        acc[0] = fmaf(si, s0.x, acc[0]), acc[1] = fmaf(si, s0.y, acc[1]);
+        acc[2] = fmaf(si, s0.z, acc[2]), acc[3] = fmaf(si, s0.w, acc[3]);
+        acc[4] = fmaf(si, s1.x, acc[4]), acc[5] = fmaf(si, s1.y, acc[5]);
+        acc[6] = fmaf(si, s1.z, acc[6]), acc[7] = fmaf(si, s1.w, acc[7]);
+      }
       if (a.res) {  // (the residual, last in the fp32 sum)
         float r[8];
         if (a.x_dtype == ARTLITE_BF16) {
@@ -463,7 +573,8 @@ bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t 
   // tokens with the register-decoding GEMVs, below 16 with the small-batch tensor-core ones (measured at B = 8: 110 us
   // against the fused kernel's 117; at B = 16: 170 against 161)
   const int64_t t_min = t_set ? t_set : mss_use(h, routed_weights(L), 1, d.act_dtype, d.expert_ffn) ? 16 : 8;
-  return !off && !L.has_shared && T >= t_min && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts && h.E_local == d.n_experts &&
+  const bool shared_ok = !L.has_shared || (L.sh_has_dm && L.qtype == ARTLITE_Q4_K && L.has_dm && L.sh_F % 256 == 0);
+  return !off && shared_ok && T >= t_min && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts && h.E_local == d.n_experts &&
          rq_type(L.qtype) && L.down_qtype == L.qtype && d.hidden % 256 == 0 && d.expert_ffn % 256 == 0 &&
          gemv_rq_rows_per_warp(L.qtype, d.hidden, true) > 0 && gemv_rq_rows_per_warp(L.down_qtype, d.expert_ffn, false) > 0 &&
          (L.qtype != ARTLITE_Q4_K || (d.act_dtype == ARTLITE_BF16 && L.has_dm)) &&
@@ -524,6 +635,23 @@ int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, vo
   a.res = res;
   a.bar = h->bar.as<GridBar>();
   a.status = h->status.as<DevStatus>();
+  a.shared = L.has_shared;
+  if (L.has_shared) {
+    a.smg = L.sh_dm_gate;
+    a.smu = L.sh_dm_up;
+    a.smd = L.sh_dm_down;
+    a.sh_gate = L.sh_gate.as<uint8_t>();
+    a.sh_up = L.sh_up.as<uint8_t>();
+    a.sh_down = L.sh_down.as<uint8_t>();
+    a.sh_rb_dn = L.sh_rb_dn;
+    a.Fs = L.sh_F;
+    a.sgate = L.sh_has_gate ? L.sh_ginp.as<float>() : nullptr;
+    a.shq = h->sh_hq.as<uint4>();
+    a.shs = reinterpret_cast<float*>(h->sh_hq.as<uint8_t>() + sizeof(uint16_t) * T * L.sh_F);
+    a.shy = h->sh_y.as<float>();
+    a.sh_s = h->sh_s.as<float>();
+    a.iota = h->sh_iota.as<int32_t>();
+  }
   const size_t smem = decode_smem(L.qtype, d.hidden, d.expert_ffn);
   auto go = [&](auto kern) -> int {
     AL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -52,6 +52,7 @@ __device__ __forceinline__ double exp_nonpos(double x) {
 template <int J>
 __device__ __forceinline__ void route_row(const RouteArgs& a, int64_t t, int lane) {
   const float* p = a.logits + t * a.row;
+  const bool flat = a.per_col >= a.E;  // (one column: the logit of x at p[x], no division)
   uint64_t key[J];
   bool nan = false;
 #pragma unroll
@@ -59,26 +60,25 @@ __device__ __forceinline__ void route_row(const RouteArgs& a, int64_t t, int lan
     const int x = lane + 32 * j;
     key[j] = 0;  // below every real key (~x != 0)
     if (x < a.E) {
-      const float l = __ldcg(p + (int64_t)(x / a.per_col) * a.pitch + x % a.per_col);
+      const float l = __ldcg(flat ? p + x : p + (int64_t)(x / a.per_col) * a.pitch + x % a.per_col);
       nan |= l != l;
       key[j] = route_key(l, x);
     }
   }
   nan = __any_sync(0xFFFFFFFFu, nan);
-  uint64_t mine = 0;  // lane r < k: the r-th largest key
+  // lane r < k: the r-th largest key. A round's warp maximum of the 64-bit keys by two 32-bit reductions: the largest
+  // high word, then the largest low word among the lanes whose best key has it (keys are unique: one owner)
+  uint64_t mine = 0;
   for (int r = 0; r < a.k; r++) {
     uint64_t m = 0;
     int mj = 0;
 #pragma unroll
     for (int j = 0; j < J; j++)
       if (key[j] > m) m = key[j], mj = j;
-    uint64_t wm = m;
-#pragma unroll
-    for (int off = 16; off; off >>= 1) {
-      const uint64_t o = __shfl_xor_sync(0xFFFFFFFFu, wm, off);
-      wm = o > wm ? o : wm;
-    }
-    if (m == wm) {  // the owner (keys are unique)
+    const uint32_t hi = (uint32_t)(m >> 32), whi = __reduce_max_sync(0xFFFFFFFFu, hi);
+    const uint32_t wlo = __reduce_max_sync(0xFFFFFFFFu, hi == whi ? (uint32_t)m : 0u);
+    const uint64_t wm = (uint64_t)whi << 32 | wlo;
+    if (m == wm) {  // the owner
 #pragma unroll
       for (int j = 0; j < J; j++)
         if (j == mj) key[j] = 0;

@@ -37,18 +37,27 @@ namespace tc {
 
 constexpr int BM = 128, BNMAX = 256, BK = 64, KC = 256, SMAX = 5, RMAX = 3;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BNMAX * BK * 2;
-constexpr int kThreads = 448;  // 14 warps: producer, MMA, 8 dequant, 4 epilogue
+constexpr int kThreads = 480;  // 15 warps: producer, MMA, 8 dequant, 4 epilogue, the Q6_K copy warp
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at the B200's clocks
 
 __host__ __device__ constexpr int chunk_bytes(int qt) {  // raw bytes of 256 values of a row
-  return qt == ARTLITE_Q8_0 ? 272 : (qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_K) ? 144 : qt == ARTLITE_Q5_K ? 176 : 0;
+  return qt == ARTLITE_Q8_0 ? 272 : (qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_K) ? 144 : qt == ARTLITE_Q5_K ? 176
+       : qt == ARTLITE_Q6_K ? 210 : 0;
+}
+// a raw stage row in shared memory: the chunk's bytes (TMA formats), or for Q6_K (whose rows need not be 16-byte
+// pitched, so no tensor map can describe them) the 16-byte-aligned 224-byte window around the 210-byte super-block,
+// copied by the copy warp, in rows 240 bytes apart (16-byte loads of 8 consecutive rows fall in distinct banks)
+__host__ __device__ constexpr int raw_pitch(int qt) { return qt == ARTLITE_Q6_K ? 240 : chunk_bytes(qt);
 }
 
 // raw weight stages: three of 18 KB for the 144-byte formats, two of 34 KB for Q8_0 (shared memory)
-__host__ __device__ constexpr int raw_stages(int qt) { return qt == ARTLITE_Q8_0 ? 2 : 3; }
+__host__ __device__ constexpr int raw_stages(int qt) { return qt == ARTLITE_Q8_0 || qt == ARTLITE_Q6_K ? 2 : 3; }
 
 struct Params {
   CUtensorMap map_w0, map_w1, map_x;
+  const uint8_t* gw0;  // the raw rows in global memory (gate / down; up), for the Q6_K copy warp
+  const uint8_t* gw1;
+  int64_t rb;          // their row bytes
   const int64_t* offsets;
   const int32_t* wexp;  // (may be null) the weight expert of each row group
   const int32_t* toff;  // [E + 1] tiles per expert (ceil(n_e / 256) * MT), scanned
@@ -181,6 +190,22 @@ __device__ __forceinline__ Tile tile_of(const Params& p, int t) {
   T.valid = min(n_e - start, tile_n);
   T.n_mma = (T.valid + 15) & ~15;
   return T;
+}
+
+// the global address of raw row `row` (of the tile's 128) for 256-value chunk kc
+template <bool GU>
+__device__ __forceinline__ uintptr_t raw_src(const Params& p, const Tile& T, int npeer, uint32_t crank, int row, int kc) {
+  const int m = npeer * T.m + (int)crank;
+  const uint8_t* base;
+  int64_t r;
+  if (GU) {  // (gate / up: rows 0-63 gate, 64-127 up, of this CTA's 64 features)
+    base = row < 64 ? p.gw0 : p.gw1;
+    r = (int64_t)T.we * p.N + 64 * m + (row & 63);
+  } else {
+    base = p.gw0;
+    r = (int64_t)T.we * p.N + BM * m + row;
+  }
+  return reinterpret_cast<uintptr_t>(base + r * p.rb + (int64_t)kc * 210);
 }
 
 // ---------------------------------------------------------------- dequant of one 64-value step into bf16 pairs
@@ -319,6 +344,39 @@ __device__ __forceinline__ void dq_q5_k_group(const uint32_t* w, int g, uint32_t
   }
 }
 
+// a 32-bit word at byte b (b + off even) of a Q6_K window (16-byte aligned shared memory)
+__device__ __forceinline__ uint32_t q6_word(const uint8_t* win, int b) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(win + (b & ~3));
+  return (b & 2) ? __funnelshift_r(w[0], w[1], 16) : w[0];
+}
+
+// Q6_K values 64 sub + 32 H .. + 31 of the super-block that starts at byte off of the window win (the reference's
+// q6_k, dequant.cpp:83-101: value 128 h + 32 jj + l = (low nibble for jj < 2, else high, of ql[64 h + 32 (jj & 1) + l]
+// | crumb jj of qh[32 h + l] << 4) - 32, times sc[8 h + 2 jj + (l >= 16)] d (fp32, rounded once each): here
+// h = sub / 2, jj = 2 (sub & 1) + H
+template <int H>
+__device__ __forceinline__ void dq_q6_k_block(const uint8_t* win, int off, int sub, uint32_t (&o)[16]) {
+  const int h2 = sub >> 1, jj = 2 * (sub & 1) + H;
+  const uint32_t dw = q6_word(win, off + 208);
+  const float d = __half2float(__ushort_as_half((unsigned short)(dw & 0xFFFFu)));
+  const uint32_t scw = q6_word(win, off + 192 + 8 * h2 + 2 * jj);  // (sc[8 h + 2 jj], sc[8 h + 2 jj + 1])
+  const int sc0 = (int)(int8_t)(scw & 0xFFu), sc1 = (int)(int8_t)((scw >> 8) & 0xFFu);
+  const uint64_t s0 = dup2(__fmul_rn((float)sc0, d)), s1 = dup2(__fmul_rn((float)sc1, d));
+  const uint64_t bias = dup2(-8388640.0f);  // -(2^23 + 32)
+  const int qlb = off + 64 * h2 + 32 * H, qhb = off + 128 + 32 * h2;
+  const int sh = (sub & 1) ? 4 : 0, ch = 2 * jj;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const uint32_t ql = q6_word(win, qlb + 4 * k), qh = q6_word(win, qhb + 4 * k);
+    const uint32_t v = ((ql >> sh) & 0x0F0F0F0Fu) | (((qh >> ch) & 0x03030303u) << 4);
+    uint64_t a, b;
+    magic4(v, a, b);
+    const uint64_t sc = k < 4 ? s0 : s1;
+    o[2 * k] = bf16x2(mul2(add2(a, bias), sc));
+    o[2 * k + 1] = bf16x2(mul2(add2(b, bias), sc));
+  }
+}
+
 // the 16-byte chunks [lo, hi] of a row's stage bytes that block / group 2 sub + h of a 256-value chunk reads
 template <int QT, int H>
 struct BlockSpan {
@@ -363,14 +421,14 @@ __device__ __forceinline__ void dequant_block(const uint4* src, uint32_t* w, int
 // the kernel's shared-memory pipeline depth: A + B stages and raw weight stages, per format and mode
 __host__ __device__ constexpr int b_stage_bytes(bool pair) { return pair ? B_BYTES / 2 : B_BYTES; }
 __host__ __device__ constexpr int ab_stages(int qt, bool pair) {
-  return pair ? (qt == ARTLITE_Q8_0 || qt == ARTLITE_Q5_K ? 4 : 5) : 3;
+  return pair ? (qt == ARTLITE_Q8_0 || qt == ARTLITE_Q5_K || qt == ARTLITE_Q6_K ? 4 : 5) : 3;
 }
 // the epilogue's transpose buffers: per epilogue warp 32 token rows of up to 32 bf16 values, rows 80 bytes apart
 // (16-byte row reads of 8 consecutive lanes fall in distinct banks)
 constexpr int kEpiRow = 80, kEpiWarp = 32 * kEpiRow;
 __host__ __device__ constexpr size_t smem_bytes(int qt, bool pair) {
   return 1024 + (size_t)ab_stages(qt, pair) * (A_BYTES + b_stage_bytes(pair)) +
-         (size_t)raw_stages(qt) * BM * chunk_bytes(qt) + 4 * kEpiWarp + 512;
+         (size_t)raw_stages(qt) * BM * raw_pitch(qt) + 4 * kEpiWarp + 512;
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -453,7 +511,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
   uint8_t* sA = base;
   uint8_t* sB = sA + SS * A_BYTES;
   uint8_t* sR = sB + SS * BB;
-  uint8_t* sE = sR + R * BM * CB;  // the epilogue warps' transpose buffers
+  constexpr int RPITCH = raw_pitch(QT);
+  uint8_t* sE = sR + R * BM * RPITCH;  // the epilogue warps' transpose buffers
   Smem* sm = reinterpret_cast<Smem*>(sE + 4 * kEpiWarp);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = p.toff[p.E];
@@ -469,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
       mbar_init(&sm->empty[i], 1);
     }
     for (int i = 0; i < R; i++) {
-      mbar_init(&sm->raw_full[i], 1);
+      mbar_init(&sm->raw_full[i], QT == ARTLITE_Q6_K ? 32 : 1);  // (Q6_K: the copy warp's lanes; else the TMA)
       mbar_init(&sm->raw_empty[i], 256);
     }
     for (int i = 0; i < 2; i++) {
@@ -516,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
         if (++s == SS) s = 0, sph ^= 1;
       }
     }
-  } else if (warp == 0 && lane == 1) {
+  } else if (warp == 0 && lane == 1 && QT != ARTLITE_Q6_K) {
     // ---------------- producer of the raw weight rows (R stages of 256 values, ahead of the B stages)
     int r = 0, rph = 0;
     for (int t = t0; t < total; t += tstep) {
@@ -585,7 +644,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
     for (int t = t0; t < total; t += tstep) {
       for (int kc = 0; kc < p.K / KC; kc++) {
         if (!wait(&sm->abort, &sm->raw_full[r], rph, p.status, 6)) goto out;
-        const uint4* src = reinterpret_cast<const uint4*>(sR + r * BM * CB + raw_row * CB);
+        const uint4* src = reinterpret_cast<const uint4*>(sR + r * BM * RPITCH + raw_row * RPITCH);
+        int q6off = 0;  // (Q6_K: where the row's super-block starts in its window)
+        if constexpr (QT == ARTLITE_Q6_K) q6off = (int)(raw_src<GU>(p, tile_of(p, t), NPEER, crank, raw_row, kc) & 15);
 #pragma unroll
         for (int sub = 0; sub < KC / BK; sub++) {
           const int step = n + sub, s = step % SS;
@@ -593,8 +654,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
           uint32_t w[NW + 4];
           uint32_t o[16];
           const int blk = 2 * sub + h;  // (the 32-value block / group)
-          if (h == 0) dequant_block<QT, 0>(src, w, sub, o);
-          else dequant_block<QT, 1>(src, w, sub, o);
+          if constexpr (QT == ARTLITE_Q6_K) {
+            if (h == 0) dq_q6_k_block<0>(reinterpret_cast<const uint8_t*>(src), q6off, sub, o);
+            else dq_q6_k_block<1>(reinterpret_cast<const uint8_t*>(src), q6off, sub, o);
+          } else {
+            if (h == 0) dequant_block<QT, 0>(src, w, sub, o);
+            else dequant_block<QT, 1>(src, w, sub, o);
+          }
           if (!wait(&sm->abort, &sm->empty[s], ph ^ 1, p.status, 7)) goto out;
           uint8_t* row = sA + s * A_BYTES + i * 128;
 #pragma unroll
@@ -610,6 +676,32 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
         if (++r == R) r = 0, rph ^= 1;
         n += KC / BK;
       }
+    }
+  } else if (warp == 14) {
+    // ---------------- Q6_K: the copy warp. Each lane copies four rows' windows (the 224 bytes from the 16-byte boundary
+    // at or below the row's 210-byte super-block) with 16-byte cp.async, then arrives on the stage's full barrier when
+    // its copies have landed
+    if constexpr (QT == ARTLITE_Q6_K) {
+      int r = 0, rph = 0;
+      for (int t = t0; t < total; t += tstep) {
+        const Tile T = tile_of(p, t);
+        for (int kc = 0; kc < p.K / KC; kc++) {
+          if (!wait(&sm->abort, &sm->raw_empty[r], rph ^ 1, p.status, 1)) goto out;
+          uint8_t* dst = sR + r * BM * RPITCH;
+#pragma unroll
+          for (int j = 0; j < BM / 32; j++) {
+            const int row = lane + 32 * j;
+            const uintptr_t g = raw_src<GU>(p, T, NPEER, crank, row, kc) & ~(uintptr_t)15;
+            const uint32_t d0 = smem_u32(dst + row * RPITCH);
+#pragma unroll
+            for (int c = 0; c < 14; c++)
+              asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d0 + 16 * c), "l"(g + 16 * c) : "memory");
+          }
+          asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sm->raw_full[r])) : "memory");
+          if (++r == R) r = 0, rph ^= 1;
+        }
+      }
+      asm volatile("cp.async.wait_all;" ::: "memory");
     }
   } else if (warp >= 10) {
     // ---------------- epilogue: TMEM lanes 32 q .. 32 q + 31
@@ -930,7 +1022,9 @@ bool tc_use_pair(int N, bool gu) {
 
 int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
   AL_CHECK(tc_supported(a.qtype, a.K, a.N), ARTLITE_EUNSUPPORTED, "tc gemm: type %d K %d N %d", a.qtype, a.K, a.N);
-  AL_CHECK(a.row_bytes % 16 == 0 && a.row_bytes == (int64_t)a.K / tc::KC * tc::chunk_bytes(a.qtype), ARTLITE_EINVAL,
+  // (Q6_K rows need not be 16-byte pitched: the copy warp reads 16-byte-aligned windows; the TMA formats' rows must be)
+  AL_CHECK((a.qtype == ARTLITE_Q6_K || a.row_bytes % 16 == 0) &&
+               a.row_bytes == (int64_t)a.K / tc::KC * tc::chunk_bytes(a.qtype), ARTLITE_EINVAL,
            "tc gemm: row bytes %lld", (long long)a.row_bytes);
   AL_CHECK(((uintptr_t)a.w0 % 16) == 0 && (!gu || ((uintptr_t)a.w1 % 16) == 0) && ((uintptr_t)a.x % 16) == 0,
            ARTLITE_EINVAL, "tc gemm: unaligned operand");
@@ -942,9 +1036,14 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
   tc::Params p{};
   const int cb = tc::chunk_bytes(a.qtype);
   const int64_t wrows = (int64_t)(a.wE > 0 ? a.wE : a.E) * a.N;
-  AL_TRY(make_map(&p.map_w0, a.w0, a.row_bytes / 2, wrows, cb / 2, gu ? 64 : tc::BM, false));
-  if (gu) AL_TRY(make_map(&p.map_w1, a.w1, a.row_bytes / 2, wrows, cb / 2, 64, false));
-  else p.map_w1 = p.map_w0;
+  if (a.qtype != ARTLITE_Q6_K) {
+    AL_TRY(make_map(&p.map_w0, a.w0, a.row_bytes / 2, wrows, cb / 2, gu ? 64 : tc::BM, false));
+    if (gu) AL_TRY(make_map(&p.map_w1, a.w1, a.row_bytes / 2, wrows, cb / 2, 64, false));
+    else p.map_w1 = p.map_w0;
+  }
+  p.gw0 = static_cast<const uint8_t*>(a.w0);
+  p.gw1 = static_cast<const uint8_t*>(gu ? a.w1 : a.w0);
+  p.rb = a.row_bytes;
   AL_TRY(make_map(&p.map_x, a.x, a.K, a.x_rows, tc::BK, pair ? tc::BNMAX / 2 : tc::BNMAX, true));
   AL_TRY(launch_unit_scan(a.counts, a.E, tc::BNMAX, MT, static_cast<int32_t*>(a.sched), st));
   p.offsets = a.offsets;
@@ -991,6 +1090,7 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
     AL_TC_CASE(ARTLITE_Q8_0)
     AL_TC_CASE(ARTLITE_Q4_K)
     AL_TC_CASE(ARTLITE_Q5_K)
+    AL_TC_CASE(ARTLITE_Q6_K)
     default: break;
   }
 #undef AL_TC_CASE

@@ -341,32 +341,57 @@ def run_config(args) -> None:
         print(json.dumps(line), flush=True)
 
 
-def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "auto") -> list[dict]:
+# the reference's own MoE model's decode shape (Qwen3.6-35B-A3B, qwen35moe: 256 experts, top-8, FFN 512, a gated
+# shared expert of FFN 512; tests/moe/ref.py:43-60)
+QWEN35 = {"name": "qwen35moe", "H": 2048, "E": 256, "K": 8, "F": 512, "Fs": 512}
+
+
+def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "auto", shape: dict | None = None) -> list[dict]:
     """benchmark config 2 on one GPU: decode batches B = 1, 4, 16, 64 of the Q4_K block (bf16 x), each forward a CUDA
     graph, over `layers` layers in turn (their touched experts far exceed L2). One dict per B: tokens/s, and the
     HBM roofline of the bytes a forward must read (U touched experts x 2,654,208 B + the fp32 router 1,048,576 B).
-    The block's device status word is read after the timed steps (raises on a kernel-reported error)."""
+    `shape` (H, E, K, F and a shared expert's Fs) measures another block shape the same way (the shared expert's rows
+    and its gate vector are part of every forward's bytes). The block's device status word is read after the timed
+    steps (raises on a kernel-reported error)."""
     import torch
     from artlite_b200.moe.block import MoEBlock
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     L = layers
-    block = MoEBlock(hidden=H, n_experts=E, top_k=K, expert_ffn=F, max_tokens=max(batches), n_layers=L,
+    sh = shape or {"name": "decode-q4_k", "H": H, "E": E, "K": K, "F": F, "Fs": 0}
+    h_, e_, k_, f_, fs = sh["H"], sh["E"], sh["K"], sh["F"], sh["Fs"]
+    block = MoEBlock(hidden=h_, n_experts=e_, top_k=k_, expert_ffn=f_, max_tokens=max(batches), n_layers=L,
                      act_dtype="bf16", device=0, path=path)
     g = torch.Generator(device=dev)
     g.manual_seed(3000)
+
+    def q4k(rows, cols):
+        n = cols // 256
+        raw = torch.randint(0, 256, (rows, n, 144), dtype=torch.uint8, generator=g, device=dev)
+        for o in (0, 2):
+            d = (torch.randn((rows, n), generator=g, device=dev) * 0.02).abs().half()
+            raw[..., o:o + 2] = d.view(torch.uint8).view(rows, n, 2)
+        return raw.view(rows, n * 144)
+
     for layer in range(L):
-        gate, up, down, router = gen_layer_q4k(torch, g, dev)
+        gate, up, down = q4k(e_ * f_, h_), q4k(e_ * f_, h_), q4k(e_ * h_, f_)
+        router = torch.randn((e_, h_), generator=g, device=dev) * 0.02
         block.set_weights(layer, gate=gate.data_ptr(), up=up.data_ptr(), down=down.data_ptr(),
                           router=router.data_ptr(), qtype="Q4_K")
+        if fs:
+            sg, su, sd = q4k(fs, h_), q4k(fs, h_), q4k(h_, fs)
+            ginp = torch.randn((h_,), generator=g, device=dev) * 0.02
+            block.set_shared(layer, gate=sg.data_ptr(), up=su.data_ptr(), down=sd.data_ptr(), ffn=fs, qtype="Q4_K",
+                             gate_inp=ginp.data_ptr(), gate_dtype="F32")
+            del sg, su, sd, ginp
         del gate, up, down, router
     torch.cuda.empty_cache()
     peaks, src = measured_peaks()
     stream = torch.cuda.Stream(device=dev)
     out = []
     for B in batches:
-        x = torch.randn((B, H), generator=g, device=dev).to(torch.bfloat16)
-        y = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+        x = torch.randn((B, h_), generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty((B, h_), dtype=torch.bfloat16, device=dev)
         touched = []
         for layer in range(L):  # (the routing of each layer: its touched experts)
             block.forward_ptr(x.data_ptr(), y.data_ptr(), B, layer=layer, stream=stream.cuda_stream)
@@ -391,9 +416,10 @@ def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "a
         block.sync()  # (the device status word: raises if a kernel reported an error)
         ms_layer = e0.elapsed_time(e1) / (steps * L)
         U = float(np.mean(touched))
-        nbytes = U * 2654208 + E * H * 4
+        per_expert = 3 * f_ * h_ * 144 // 256  # (Q4_K: 144 bytes per 256 values)
+        nbytes = U * per_expert + e_ * h_ * 4 + (3 * fs * h_ * 144 // 256 + h_ * 4 if fs else 0)
         gbs = nbytes / (ms_layer / 1000.0) / 1e9
-        out.append({"workload": f"decode-q4_k-b{B}", "batch": B, "us_per_layer": ms_layer * 1000.0,
+        out.append({"workload": f"{sh['name']}-b{B}", "batch": B, "us_per_layer": ms_layer * 1000.0,
                     "tokens_per_s": B / (ms_layer / 1000.0), "experts_touched": U,
                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                  "frac": gbs / peaks["hbm_gbs"], "peak_source": f"{src} hbm_gbs",
@@ -406,7 +432,8 @@ def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "a
 
 
 def run_decode(args) -> None:
-    for line in measure_decode(args.batches, args.layers, args.steps, args.warmup, args.path):
+    for line in measure_decode(args.batches, args.layers, args.steps, args.warmup, args.path,
+                               QWEN35 if args.qwen35 else None):
         print(json.dumps(line), flush=True)
 
 
@@ -423,6 +450,7 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the decode sweep and config 3 of the default line")
     ap.add_argument("--decode", action="store_true", help="benchmark config 2 (decode batches, Q4_K) instead")
+    ap.add_argument("--qwen35", action="store_true", help="with --decode: the qwen35moe shape (E 256, F 512, shared)")
     ap.add_argument("--config", type=int, choices=[3, 5], help="benchmark config 3 or 5 (one GPU) instead")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"], help="expert path of --decode")
     ap.add_argument("--batches", type=int, nargs="+", default=[1, 4, 16, 64], help="decode batches of --decode")
@@ -573,6 +601,10 @@ def main() -> None:
                                                                         "experts_touched", "roofline", "path",
                                                                         "layers", "steps", "clocks")}
                                   for d in measure_decode([1, 4, 16, 64], 8, 20, 3)}
+        extras["qwen35moe_decode"] = {
+            f"B{d['batch']}": {k: d[k] for k in ("us_per_layer", "tokens_per_s", "experts_touched", "roofline", "path",
+                                                 "layers", "steps", "clocks")}
+            for d in measure_decode([1, 16, 64], 8, 20, 3, shape=QWEN35)}
         c3 = measure_config(3, 4, 10, 3)[0]
         extras["config3"] = {k: c3.get(k) for k in ("workload", "ms_per_layer", "tokens_per_s", "path", "roofline",
                                                     "layer_roofline", "stage_ms_mean", "layers", "steps", "clocks")}

@@ -258,3 +258,28 @@ def test_norm_and_residual(path, T, act):
     want = xf + moe_np.moe_ffn(xn, ids, w, expert_fn(layer))
     got = moe_np.bf16_to_f32(y) if act == "bf16" else y
     assert moe_np.rel_max(got, want) <= (BF16_TOL if act == "bf16" or path == "tc" else FP32_TOL)
+
+
+@pytest.mark.parametrize("T,gated", [(16, True), (64, True), (24, False)])
+def test_qwen35moe_decode_shared_fused(T, gated):
+    """The reference's own MoE decode shape (qwen35moe: H=2048, E=256, K=8, F=512, a shared expert of FFN 512, Q4_K)
+    at decode batches that take the fused decode kernel, the shared expert inside it: the routed sum plus
+    sigmoid(x . g) swiglu_s(x) (ref.moe_ffn + ref.shared_expert, tests/moe/ref.py:43-60), gated and ungated."""
+    H, E, F, Fs = 2048, 256, 512, 512
+    layer, x, _ = moe_np.make_block(100 + T, T, qtype="Q4_K", E=E, H=H, F=F)
+    rng = np.random.default_rng(101)
+    sg, su = moe_np.random_blocks(rng, "Q4_K", Fs, H), moe_np.random_blocks(rng, "Q4_K", Fs, H)
+    sd = moe_np.random_blocks(rng, "Q4_K", H, Fs)
+    g = (rng.standard_normal(H) * 0.02).astype(np.float32) if gated else None
+    b = make_block(layer, T, act="bf16", path="auto")
+    b.set_shared(0, gate=sg, up=su, down=sd, ffn=Fs, qtype="Q4_K", gate_inp=g)
+    y = moe_np.bf16_to_f32(b.forward(x))
+    took = b.path(0)
+    dbg = b.debug(T)
+    b.close()
+    assert took == "gemv"
+    ids, w = check_routing(dbg, x, layer, 8)
+    want = oracle_y(layer, x, ids, w) + moe_np.shared_expert(x_f32(x), moe_np.dequant("Q4_K", sg, H),
+                                                             moe_np.dequant("Q4_K", su, H),
+                                                             moe_np.dequant("Q4_K", sd, Fs), g)
+    assert moe_np.rel_max(y, want) <= BF16_TOL

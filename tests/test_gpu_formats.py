@@ -30,20 +30,23 @@ def run_checked(layer, x, T, path, k=8):
 
 
 @pytest.mark.parametrize("qtype,down", [("Q5_K", "Q5_K"), ("Q4_K", "Q5_K"), ("Q5_K", "Q4_K"), ("Q4_0", "Q5_K"),
-                                        ("Q8_0", "Q5_K")])
-def test_tcgen05_q5_k_and_mixed(qtype, down):
-    """Q5_K on the tensor cores, alone and mixed with the other formats (E=16, H=512, F=256, T=200: ragged groups)."""
+                                        ("Q8_0", "Q5_K"), ("Q6_K", "Q6_K"), ("Q4_K", "Q6_K"), ("Q8_0", "Q6_K")])
+def test_tcgen05_q5_k_q6_k_and_mixed(qtype, down):
+    """Q5_K and Q6_K on the tensor cores, alone and mixed with the other formats (E=16, H=512, F=256, T=200: ragged
+    groups; Q6_K rows of 420 and 210 bytes, not 16-byte pitched, through the copy warp)."""
     layer, x, _ = moe_np.make_block(90, 200, qtype=qtype, down_qtype=down, E=16, H=512, F=256)
     y, ids, w, took = run_checked(layer, x, 200, "tc")
     assert took == "tc"
     assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= BF16_TOL
 
 
-def test_q4_k_m_prefill_shape():
-    """A Q4_K_M-style layer at config 3's size (T=4096, H=2048, E=128, K=8, F=768, Q4_K gate / up, Q5_K down) on the
-    tcgen05 path, every token against the torch fp32 reference, which is pinned to the NumPy oracle on a stride."""
+@pytest.mark.parametrize("down", ["Q6_K", "Q5_K"])
+def test_q4_k_m_prefill_shape(down):
+    """A Q4_K_M-style layer at config 3's size (T=4096, H=2048, E=128, K=8, F=768, Q4_K gate / up, Q6_K or Q5_K down)
+    on the tcgen05 path, every token against the torch fp32 reference, which is pinned to the NumPy oracle on a
+    stride."""
     T = 4096
-    layer, x, _ = moe_np.make_block(91, T, qtype="Q4_K", down_qtype="Q5_K")
+    layer, x, _ = moe_np.make_block(91, T, qtype="Q4_K", down_qtype=down)
     y, ids, w, took = run_checked(layer, x, T, "auto")
     assert took == "tc"
     ref = torch_moe_ffn(layer, x, ids, w)
