@@ -12,7 +12,8 @@ DEFAULT_LIB = os.path.join(HERE, "lib", "libartlite_moe_cuda.so")
 
 OK, EINVAL, ECAPACITY, ECUDA, ENCCL, ETIMEOUT, EDEVICE, EUNSUPPORTED = 0, -1, -2, -3, -4, -5, -6, -7
 # ggml tensor type ids (include/artlite_moe.h; gguf_model.py:385-390)
-QTYPES = {"F32": 0, "F16": 1, "Q4_0": 2, "Q4_1": 3, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "BF16": 30}
+QTYPES = {"F32": 0, "F16": 1, "Q4_0": 2, "Q4_1": 3, "Q8_0": 8, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ4_NL": 20,
+          "IQ4_XS": 23, "BF16": 30}
 
 # every entry point include/artlite_moe.h declares (tests check the library exports each of them)
 EXPORTS = ("artlite_moe_last_error", "artlite_moe_version", "artlite_moe_route", "artlite_moe_plan",

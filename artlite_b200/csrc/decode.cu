@@ -102,8 +102,6 @@ struct DecodeArgs {
   // h rows (fragment order) and sums, its output rows (fp32, T x H), the per-token gates, 0 .. T - 1
   bool shared;
   CUtensorMap smg, smu, smd;
-  const uint8_t *sh_gate, *sh_up, *sh_down;  // (their raw rows)
-  int64_t sh_rb_dn;
   int Fs;
   const float* sgate;
   uint4* shq;
@@ -438,12 +436,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     const int total = routed + sh_items;
     const int i0 = (int)((int64_t)blockIdx.x * total / gridDim.x), i1 = (int)((int64_t)(blockIdx.x + 1) * total / gridDim.x);
     if constexpr (kMs) {
-      ms::Gemv m{&a.mg, &a.mu, a.H, a.F, E, a.K, a.xq, a.xs, a.hq, a.hs, nullptr, a.gate, a.up, a.rb_gu};
+      ms::Gemv m{&a.mg, &a.mu, a.H, a.F, E, a.K, a.xq, a.xs, a.hq, a.hs, nullptr};
       ms::run<true>(m, uo_gu, offs, perm_s, reinterpret_cast<uint8_t*>(xs), pp, i0, min(i1, routed), a.status);
       if (i1 > routed) {  // (the shared expert: one expert, every token a pair of its own, in token order)
         sh_uo[0] = 0, sh_uo[1] = sh_items, sh_off[0] = 0, sh_off[1] = a.T;
         __syncthreads();
-        ms::Gemv ms_{&a.smg, &a.smu, a.H, a.Fs, 1, 1, a.xq, a.xs, a.shq, a.shs, nullptr, a.sh_gate, a.sh_up, a.rb_gu};
+        ms::Gemv ms_{&a.smg, &a.smu, a.H, a.Fs, 1, 1, a.xq, a.xs, a.shq, a.shs, nullptr};
         ms::run<true>(ms_, sh_uo, sh_off, a.iota, reinterpret_cast<uint8_t*>(xs), pp, max(i0, routed) - routed,
                       i1 - routed, a.status);
       }
@@ -470,12 +468,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     const int total = routed + sh_items;
     const int i0 = (int)((int64_t)blockIdx.x * total / gridDim.x), i1 = (int)((int64_t)(blockIdx.x + 1) * total / gridDim.x);
     if constexpr (kMs) {
-      ms::Gemv m{&a.md, nullptr, a.F, a.H, E, a.K, a.hq, a.hs, nullptr, nullptr, a.y, a.down, nullptr, a.rb_dn};
+      ms::Gemv m{&a.md, nullptr, a.F, a.H, E, a.K, a.hq, a.hs, nullptr, nullptr, a.y};
       ms::run<false>(m, uo_dn, offs, perm_s, reinterpret_cast<uint8_t*>(xs), pp, i0, min(i1, routed), a.status);
       if (i1 > routed) {
         sh_uo[0] = 0, sh_uo[1] = sh_items, sh_off[0] = 0, sh_off[1] = a.T;
         __syncthreads();
-        ms::Gemv ms_{&a.smd, nullptr, a.Fs, a.H, 1, 1, a.shq, a.shs, nullptr, nullptr, a.shy, a.sh_down, nullptr, a.sh_rb_dn};
+        ms::Gemv ms_{&a.smd, nullptr, a.Fs, a.H, 1, 1, a.shq, a.shs, nullptr, nullptr, a.shy};
         ms::run<false>(ms_, sh_uo, sh_off, a.iota, reinterpret_cast<uint8_t*>(xs), pp, max(i0, routed) - routed,
                        i1 - routed, a.status);
       }
@@ -640,10 +638,6 @@ int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, vo
     a.smg = L.sh_dm_gate;
     a.smu = L.sh_dm_up;
     a.smd = L.sh_dm_down;
-    a.sh_gate = L.sh_gate.as<uint8_t>();
-    a.sh_up = L.sh_up.as<uint8_t>();
-    a.sh_down = L.sh_down.as<uint8_t>();
-    a.sh_rb_dn = L.sh_rb_dn;
     a.Fs = L.sh_F;
     a.sgate = L.sh_has_gate ? L.sh_ginp.as<float>() : nullptr;
     a.shq = h->sh_hq.as<uint4>();

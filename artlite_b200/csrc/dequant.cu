@@ -15,7 +15,8 @@ struct Named {
 };
 constexpr Named kNames[] = {{"F32", ARTLITE_F32},   {"F16", ARTLITE_F16},   {"BF16", ARTLITE_BF16},
                             {"Q4_0", ARTLITE_Q4_0}, {"Q4_1", ARTLITE_Q4_1}, {"Q8_0", ARTLITE_Q8_0},
-                            {"Q4_K", ARTLITE_Q4_K}, {"Q5_K", ARTLITE_Q5_K}, {"Q6_K", ARTLITE_Q6_K}};
+                            {"Q4_K", ARTLITE_Q4_K}, {"Q5_K", ARTLITE_Q5_K}, {"Q6_K", ARTLITE_Q6_K},
+                            {"Q3_K", ARTLITE_Q3_K}, {"IQ4_NL", ARTLITE_IQ4_NL}, {"IQ4_XS", ARTLITE_IQ4_XS}};
 }  // namespace
 
 int qtype_from_name(const char* name) {
@@ -92,6 +93,9 @@ int launch_dequant_rows(int qtype, const uint8_t* raw, int64_t n, int64_t row_by
     case ARTLITE_Q4_K: dequant_rows_kernel<ARTLITE_Q4_K><<<grid, 128, 0, st>>>(raw, n, row_bytes, cols, out); break;
     case ARTLITE_Q5_K: dequant_rows_kernel<ARTLITE_Q5_K><<<grid, 128, 0, st>>>(raw, n, row_bytes, cols, out); break;
     case ARTLITE_Q6_K: dequant_rows_kernel<ARTLITE_Q6_K><<<grid, 128, 0, st>>>(raw, n, row_bytes, cols, out); break;
+    case ARTLITE_Q3_K: dequant_rows_kernel<ARTLITE_Q3_K><<<grid, 128, 0, st>>>(raw, n, row_bytes, cols, out); break;
+    case ARTLITE_IQ4_NL: dequant_rows_kernel<ARTLITE_IQ4_NL><<<grid, 128, 0, st>>>(raw, n, row_bytes, cols, out); break;
+    case ARTLITE_IQ4_XS: dequant_rows_kernel<ARTLITE_IQ4_XS><<<grid, 128, 0, st>>>(raw, n, row_bytes, cols, out); break;
     default: dequant_rows_kernel<ARTLITE_F32><<<grid, 128, 0, st>>>(raw, n, row_bytes, cols, out); break;
   }
   AL_LAUNCHED();

@@ -244,6 +244,9 @@ int launch_gemv(const ExpertGemvArgs& a, const int32_t* unit_off, int rt, cudaSt
     case ARTLITE_Q4_K: return go(expert_gemv<ARTLITE_Q4_K, GU, NT>);
     case ARTLITE_Q5_K: return go(expert_gemv<ARTLITE_Q5_K, GU, NT>);
     case ARTLITE_Q6_K: return go(expert_gemv<ARTLITE_Q6_K, GU, NT>);
+    case ARTLITE_Q3_K: return go(expert_gemv<ARTLITE_Q3_K, GU, NT>);
+    case ARTLITE_IQ4_NL: return go(expert_gemv<ARTLITE_IQ4_NL, GU, NT>);
+    case ARTLITE_IQ4_XS: return go(expert_gemv<ARTLITE_IQ4_XS, GU, NT>);
     case ARTLITE_F32: return go(expert_gemv<ARTLITE_F32, GU, NT>);
     case ARTLITE_F16: return go(expert_gemv<ARTLITE_F16, GU, NT>);
     case ARTLITE_BF16: return go(expert_gemv<ARTLITE_BF16, GU, NT>);

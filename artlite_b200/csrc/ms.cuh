@@ -123,8 +123,6 @@ struct Gemv {
   uint4* hq;
   float* hs;
   float* y;
-  const uint8_t *p0, *p1;  // the raw rows of m0 / m1 (an item's rows are contiguous: prefetched into L2 as one range)
-  int64_t rb;              // bytes a row
 };
 
 struct Pipe {  // the CTA's stages: full mbarriers (the copies landed: one arrival + bytes) and the parity each thread
@@ -191,17 +189,6 @@ __device__ __forceinline__ void refill(const Gemv& a, const Item& it, int sb, co
   const int64_t srow = __shfl_sync(0xFFFFFFFFu, my_row, (lane >> 1) & 7);
   if (lane < 16) cp16(buf + kSOff + (lane >> 1) * 32 + (lane & 1) * 16, a.xs + srow * G + sb * 8 + (lane & 1) * 4);
   cp_arrive(bar);
-}
-
-// the raw rows of item it (gate and up, or down) into L2, one bulk prefetch a matrix (lane 0 of the calling warp): the
-// stages' tile loads of the item then read L2, and the DRAM stream runs an item ahead of them in long contiguous reads
-template <bool GU>
-__device__ __forceinline__ void prefetch_item(const Gemv& a, const Item& it) {
-  const int rows = GU ? 64 : 128;
-  const int64_t off = ((int64_t)it.e * a.N + (int64_t)it.rt * rows) * a.rb;
-  const uint32_t bytes = (uint32_t)(rows * a.rb);
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.p0 + off), "r"(bytes) : "memory");
-  if (GU) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.p1 + off), "r"(bytes) : "memory");
 }
 
 // x of a step for this lane, from the stage: the B fragments of token slot g for the column's 8 groups, and the group
@@ -313,20 +300,14 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
   const bool producer = threadIdx.x == 0;
   int e_run = expert_of(i0, a.E, uo);  // (the compute side's expert hint)
   int e_fill = e_run;                  // (this warp's hint for the refills it issues)
-  int e_pf = e_run;                    // (and for the items it prefetches)
-  const int n_items = i1 - i0;
-  // prologue (warp 0): the first two items into L2, steps 0 .. kStages - 1 (the stages are free: the previous user
-  // waited for every copy it started)
+  // prologue (warp 0): steps 0 .. kStages - 1 (the stages are free: the previous user waited for every copy it started)
   if (warp == 0) {
     const bool go = !*(volatile int*)pp.failed;
     int n = 0;
-    if (go) {
-      if (lane == 0)
-        for (int q = 0; q < 2 && q < n_items; q++) prefetch_item<GU>(a, item_at<GU>(a, i0 + q, e_pf, uo, offs));
+    if (go)
       for (int s = 0; s < kStages && s < S; s++, n++)
         refill<GU>(a, item_at<GU>(a, i0 + s / SB, e_fill, uo, offs), s % SB, perm, smem + s * kStageBytes, &pp.full[s],
                    lane);
-    }
     if (lane == 0) *(volatile int*)pp.issued = n;
   }
   float y[4] = {0, 0, 0, 0};
@@ -364,9 +345,6 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
     if (__shfl_sync(0xFFFFFFFFu, last, 0) && s2 < S && !*(volatile int*)pp.failed) {
       const int q = s2 / SB;
       refill<GU>(a, item_at<GU>(a, i0 + q, e_fill, uo, offs), s2 - q * SB, perm, buf, &pp.full[b], lane);
-      // an item's first step: the item after it into L2 (the first two were prefetched by the prologue)
-      if (s2 == q * SB && q + 1 < n_items && q >= 1 && lane == 0)
-        prefetch_item<GU>(a, item_at<GU>(a, i0 + q + 1, e_pf, uo, offs));
       if (lane == 0) atomicMax(pp.issued, s2 + 1);
     }
     if (++sb == SB) {  // the item's last column: its outputs

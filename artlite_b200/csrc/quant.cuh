@@ -1,5 +1,5 @@
 // GGUF block decoding on the device, fp32 and exact: the reference's fp32 operations in their order
-// (csrc/artlite/dequant.cpp:21-101, itself built with -ffp-contract=off), written with the _rn intrinsics so that
+// (csrc/artlite/dequant.cpp:21-140, itself built with -ffp-contract=off), written with the _rn intrinsics so that
 // nvcc contracts nothing into an FMA. Every product here has at most 21 significant bits, so the values are exact.
 #pragma once
 
@@ -90,16 +90,65 @@ __device__ __forceinline__ void dq_q6_k_group(const uint8_t* b, int g, float* o)
   }
 }
 
+// Q3_K 16-value sub-block s (dequant.cpp:103-117): 110 B per 256 = hmask[32], qs[64], 12 scale bytes, d (fp16 at
+// 108). Its 6-bit scale (stored + 32): low nibble of byte s (s < 8) or high nibble of byte s - 8, top crumb from byte
+// 8 + s % 4 at bit 2 (s / 4). Value 16 s + l = 128 n + 32 j + i: q = crumb j of qs[32 n + i] | bit (4 n + j) of
+// hmask[i] << 2, w = (d (scale - 32)) (q - 4)
+__device__ __forceinline__ void dq_q3_k_sub(const uint8_t* b, int s, float* o) {
+  const uint8_t* sc = b + 96;
+  const int low = s < 8 ? sc[s] & 15 : sc[s - 8] >> 4, top = (sc[8 + (s & 3)] >> (2 * (s >> 2))) & 3;
+  const float a = __fmul_rn(f16_at(b + 108), (float)((low | top << 4) - 32));
+  const int n = s >> 3, j = (s >> 1) & 3, i0 = 16 * (s & 1);
+#pragma unroll
+  for (int l = 0; l < 16; l++) {
+    const int q = ((b[32 + 32 * n + i0 + l] >> (2 * j)) & 3) | ((b[i0 + l] >> (4 * n + j)) & 1) << 2;
+    o[l] = __fmul_rn(a, __fsub_rn((float)q, 4.0f));
+  }
+}
+
+// the IQ4_NL / IQ4_XS code values (dequant.cpp:119, ggml's non-linear 4-bit grid), as a byte lookup
+__device__ __forceinline__ float iq4_value(int q) {
+  constexpr int8_t v[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+  return (float)v[q];
+}
+
+// IQ4_NL (dequant.cpp:121-126): 18 B per 32, Q4_0's layout, w = d grid[q]
+__device__ __forceinline__ void dq_iq4_nl(const uint8_t* b, float* o) {
+  const float d = f16_at(b);
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    const int c = b[2 + j];
+    o[j] = __fmul_rn(d, iq4_value(c & 15));
+    o[j + 16] = __fmul_rn(d, iq4_value(c >> 4));
+  }
+}
+
+// IQ4_XS 32-group g (dequant.cpp:128-140): 136 B per 256 = d, a u16 of high scale crumbs, 4 bytes of low scale
+// nibbles, 8 x 16 code bytes; ls = nibble (g % 2) of byte 4 + g / 2 | crumb g of the u16 << 4, w = (d (ls - 32)) grid[q]
+__device__ __forceinline__ void dq_iq4_xs_group(const uint8_t* b, int g, float* o) {
+  const int hi = b[2] | b[3] << 8;
+  const int ls = ((b[4 + (g >> 1)] >> (4 * (g & 1))) & 15) | ((hi >> (2 * g)) & 3) << 4;
+  const float dl = __fmul_rn(f16_at(b), (float)(ls - 32));
+  const uint8_t* q = b + 8 + 16 * g;
+#pragma unroll
+  for (int j = 0; j < 16; j++) {
+    o[j] = __fmul_rn(dl, iq4_value(q[j] & 15));
+    o[j + 16] = __fmul_rn(dl, iq4_value(q[j] >> 4));
+  }
+}
+
 // values and bytes per block of a GGUF type (0: not read by this build)
 __host__ __device__ constexpr int q_per(int qt) {
-  return qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_1 || qt == ARTLITE_Q8_0 ? 32
-         : (qt == ARTLITE_Q4_K || qt == ARTLITE_Q5_K || qt == ARTLITE_Q6_K) ? 256
+  return qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_1 || qt == ARTLITE_Q8_0 || qt == ARTLITE_IQ4_NL ? 32
+         : (qt == ARTLITE_Q3_K || qt == ARTLITE_Q4_K || qt == ARTLITE_Q5_K || qt == ARTLITE_Q6_K || qt == ARTLITE_IQ4_XS)
+             ? 256
          : (qt == ARTLITE_F32 || qt == ARTLITE_F16 || qt == ARTLITE_BF16) ? 1
                                                                           : 0;
 }
 __host__ __device__ constexpr int q_bytes(int qt) {
   return qt == ARTLITE_Q4_0 ? 18 : qt == ARTLITE_Q4_1 ? 20 : qt == ARTLITE_Q8_0 ? 34 : qt == ARTLITE_Q4_K ? 144
-         : qt == ARTLITE_Q5_K ? 176 : qt == ARTLITE_Q6_K ? 210 : qt == ARTLITE_F32 ? 4
+         : qt == ARTLITE_Q5_K ? 176 : qt == ARTLITE_Q6_K ? 210 : qt == ARTLITE_Q3_K ? 110 : qt == ARTLITE_IQ4_NL ? 18
+         : qt == ARTLITE_IQ4_XS ? 136 : qt == ARTLITE_F32 ? 4
          : (qt == ARTLITE_F16 || qt == ARTLITE_BF16) ? 2 : 0;
 }
 
@@ -118,6 +167,13 @@ __device__ __forceinline__ void dq_group(const uint8_t* row, int g, float* o) {
     dq_k45_group<true>(row + 176 * (g >> 3), g & 7, o);
   } else if constexpr (QT == ARTLITE_Q6_K) {
     dq_q6_k_group(row + 210 * (g >> 3), g & 7, o);
+  } else if constexpr (QT == ARTLITE_Q3_K) {
+    dq_q3_k_sub(row + 110 * (g >> 3), 2 * (g & 7), o);
+    dq_q3_k_sub(row + 110 * (g >> 3), 2 * (g & 7) + 1, o + 16);
+  } else if constexpr (QT == ARTLITE_IQ4_NL) {
+    dq_iq4_nl(row + 18 * g, o);
+  } else if constexpr (QT == ARTLITE_IQ4_XS) {
+    dq_iq4_xs_group(row + 136 * (g >> 3), g & 7, o);
   } else if constexpr (QT == ARTLITE_F32) {
 #pragma unroll
     for (int j = 0; j < 32; j++) o[j] = reinterpret_cast<const float*>(row)[32 * g + j];

@@ -122,4 +122,90 @@ __device__ __forceinline__ void route_row(const RouteArgs& a, int64_t t, int lan
   }
 }
 
+// The routing and dispatch of a decode-sized batch by one CTA of NT threads (r.ids is a.ids; n k <= kSmallPairs pairs,
+// E <= kSmallExperts, NT >= E): every token routed into shared memory (a warp a row), the ids and weights copied out
+// for the caller, then the histogram, the scan and the stable rank of the pairs exactly as the dispatch kernels do for
+// a single block, and both expert GEMVs' unit scans. sm: dynamic shared memory of
+// 4 ((NT / 32 + 2) E + 1) + 8 E + 8 P bytes. Called by dispatch.cu's route_dispatch_small and by the last CTA of
+// router.cu's router_route_kernel.
+template <int J, int NT>
+__device__ __forceinline__ void route_dispatch_cta(RouteArgs r, const DispatchArgs& a, int mult2, int32_t* unit_off2,
+                                                   int32_t* sm) {
+  __shared__ int64_t s64[32];
+  __shared__ int32_t s32[32];
+  constexpr int NW = NT / 32;
+  int32_t* wc = sm;                 // [NW][E] per-warp counts of the current round
+  int32_t* run = sm + NW * a.E;     // [E] placed so far
+  int32_t* cnt = run + a.E;         // [E] histogram
+  int64_t* off = reinterpret_cast<int64_t*>(cnt + a.E + (a.E & 1));  // [E] offsets
+  int32_t* ids_s = reinterpret_cast<int32_t*>(off + a.E);             // [P] the routed ids
+  float* w_s = reinterpret_cast<float*>(ids_s + a.P);                 // [P] and weights
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  {
+    RouteArgs rl = r;
+    rl.ids = ids_s;
+    rl.w = w_s;
+    for (int64_t t = warp; t < r.n; t += NW) route_row<J>(rl, t, lane);
+  }
+  for (int i = threadIdx.x; i < (NW + 2) * a.E; i += NT) sm[i] = 0;
+  __syncthreads();  // (the rows' ids are visible to the block)
+  for (int64_t p = threadIdx.x; p < a.P; p += NT) {
+    const int32_t x = ids_s[p];
+    r.ids[p] = x;
+    r.w[p] = w_s[p];
+    if (x < 0 || x >= a.E)
+      report(a.status, ARTLITE_EDEVICE, x, a.E, 1);
+    else
+      atomicAdd(&cnt[x], 1);
+  }
+  __syncthreads();
+  const int e = threadIdx.x;
+  const int32_t c = e < a.E ? cnt[e] : 0;
+  int64_t tot64;
+  const int64_t o = block_exclusive_scan<int64_t>(c, s64, &tot64);
+  if (e < a.E) {
+    off[e] = o;
+    a.offsets[e] = o;
+    a.counts[e] = c;
+  }
+  if (e == 0) a.offsets[a.E] = tot64;
+  for (int which = 0; which < 2; which++) {
+    const int mult = which ? mult2 : a.unit_mult;
+    int32_t* uo = which ? unit_off2 : a.unit_off;
+    if (!uo) continue;
+    const int32_t u = e < a.E ? (c + a.unit_rows - 1) / a.unit_rows * mult : 0;
+    int32_t tot;
+    const int32_t v = block_exclusive_scan<int32_t>(u, s32, &tot);
+    if (e < a.E) uo[e] = v;
+    if (e == 0) uo[a.E] = tot;
+  }
+  __syncthreads();
+  const unsigned lt = (1u << lane) - 1u;
+  for (int64_t r0 = 0; r0 < a.P; r0 += NT) {
+    const int64_t p = r0 + threadIdx.x;
+    int32_t x = p < a.P ? ids_s[p] : -1;
+    const bool valid = x >= 0 && x < a.E;
+    if (!valid) x = -1 - lane;
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, x);
+    const int rank = __popc(peers & lt);
+    const bool leader = rank == 0;
+    if (valid && leader) wc[warp * a.E + x] = __popc(peers);
+    __syncthreads();
+    if (valid) {
+      int32_t pre = run[x];
+      for (int w = 0; w < warp; w++) pre += wc[w * a.E + x];
+      const int64_t dest = off[x] + pre + rank;
+      a.perm[dest] = (int32_t)p;
+      a.slot[p] = (int32_t)dest;
+    }
+    __syncthreads();
+    if (valid && leader) {
+      atomicAdd(&run[x], __popc(peers));
+      wc[warp * a.E + x] = 0;
+    }
+    __syncthreads();
+  }
+}
+
+
 }  // namespace artlite

@@ -19,7 +19,7 @@ _KV_STRING, _KV_ARRAY = 8, 9
 # ggml type id: (name, values per block, bytes per block)
 GGML_TYPES = {0: ("F32", 1, 4), 1: ("F16", 1, 2), 2: ("Q4_0", 32, 18), 3: ("Q4_1", 32, 20), 8: ("Q8_0", 32, 34),
               10: ("Q2_K", 256, 84), 11: ("Q3_K", 256, 110), 12: ("Q4_K", 256, 144), 13: ("Q5_K", 256, 176),
-              14: ("Q6_K", 256, 210), 30: ("BF16", 1, 2)}
+              14: ("Q6_K", 256, 210), 20: ("IQ4_NL", 32, 18), 23: ("IQ4_XS", 256, 136), 30: ("BF16", 1, 2)}
 TYPE_IDS = {v[0]: k for k, v in GGML_TYPES.items()}
 
 

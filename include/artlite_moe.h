@@ -46,9 +46,12 @@ extern "C" {
 #define ARTLITE_Q4_0 2
 #define ARTLITE_Q4_1 3
 #define ARTLITE_Q8_0 8
+#define ARTLITE_Q3_K 11
 #define ARTLITE_Q4_K 12
 #define ARTLITE_Q5_K 13
 #define ARTLITE_Q6_K 14
+#define ARTLITE_IQ4_NL 20
+#define ARTLITE_IQ4_XS 23
 #define ARTLITE_BF16 30
 
 /* The message of the last failed call on this thread ("" if none). */

@@ -4,13 +4,15 @@
 - ``moe_route``: ``tests/moe/ref.py:11-18`` (softmax over all E, a stable argsort of -p, w / max(sum, 2^-14)).
 - ``swiglu`` / ``moe_ffn`` / ``shared_expert``: ``tests/moe/ref.py:21-24,43-52,55-60`` (float32 matmuls).
 - ``dequant``: ``src/artlite/gguf_model.py:50-129`` (``QTensor.fields``) and ``:278-330`` (``QTensor.dequantize``)
-  for Q4_0, Q4_1, Q8_0, Q4_K, Q5_K, Q6_K, F32, F16, BF16.
+  for Q4_0, Q4_1, Q8_0, Q3_K, Q4_K, Q5_K, Q6_K, IQ4_NL, IQ4_XS, F32, F16, BF16 (Q3_K :141-162,297-299; IQ4_NL
+  :195-200,320-321; IQ4_XS :201-212,322-324).
 - ``rel`` / ``rel_max``: ``tests/numerics.py:24-27,50-53``.
 - Block generators: the synthetic GGUF blocks of the benchmark configurations (fp16 d from |N(0, 0.02)|; Q4_0 nibbles
   uniform 0..15; Q4_K 6-bit scales / mins uniform 0..63 packed as ``gguf_model.py:116-121`` reads them; Q8_0 int8
   uniform -127..127), drawn from one ``default_rng(seed)`` stream in the order router, x, gate, up, down. The other
   block formats (test cases only): Q4_1 m = -8 d; Q5_K as Q4_K with uniform high bits; Q6_K int8 scales uniform
-  -32..31 with d from |N(0, 0.002)|; all quant bits uniform.
+  -32..31 with d from |N(0, 0.002)|; Q3_K d from |N(0, 0.004)|; IQ4_NL d from |N(0, 0.0005)|, IQ4_XS d from
+  |N(0, 0.00005)|; all quant and scale bits uniform.
 """
 
 from dataclasses import dataclass
@@ -19,7 +21,11 @@ import numpy as np
 
 # (values per block, bytes per block) of the GGUF types (gguf_model.py:385-390)
 BLOCKS = {"F32": (1, 4), "F16": (1, 2), "BF16": (1, 2), "Q4_0": (32, 18), "Q4_1": (32, 20), "Q8_0": (32, 34),
-          "Q4_K": (256, 144), "Q5_K": (256, 176), "Q6_K": (256, 210)}
+          "Q3_K": (256, 110), "Q4_K": (256, 144), "Q5_K": (256, 176), "Q6_K": (256, 210), "IQ4_NL": (32, 18),
+          "IQ4_XS": (256, 136)}
+
+# IQ4_NL / IQ4_XS code values (gguf_model.py's IQ4_VALUES, ggml's non-linear 4-bit grid)
+IQ4_GRID = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], np.float32)
 
 
 def row_bytes(qtype: str, cols: int) -> int:
@@ -153,6 +159,32 @@ def dequant(qtype: str, raw: np.ndarray, cols: int) -> np.ndarray:
         sc = np.ascontiguousarray(b[..., 192:208]).view(np.int8)
         a = _f16(b[..., 208:210])[..., None] * sc.astype(np.float32)
         w = a[..., None] * (q.reshape(rows, -1, 16, 16).astype(np.float32) - 32.0)
+    elif qtype == "Q3_K":
+        nbk = b.shape[1]
+        # value 128 n + 32 j + i: crumb j of qs[32 n + i], bit (4 n + j) of hmask[i] as bit 2
+        qs = b[..., 32:96].reshape(rows, nbk, 2, 1, 32)
+        j = np.arange(4, dtype=np.uint8).reshape(1, 1, 1, 4, 1)
+        n = np.arange(2, dtype=np.uint8).reshape(1, 1, 2, 1, 1)
+        hm = b[..., 0:32].reshape(rows, nbk, 1, 1, 32)
+        q = ((qs >> (2 * j)) & 3) | (((hm >> (4 * n + j)) & 1) << 2)  # (rows, nbk, n, j, i)
+        sb = b[..., 96:108]
+        low = np.concatenate([sb[..., :8] & 0xF, sb[..., :8] >> 4], axis=-1)  # sub-blocks 0 .. 15
+        top = (sb[..., 8:12, None] >> (2 * np.arange(4, dtype=np.uint8))) & 3  # [i, k]: sub-block 4 k + i
+        sc = (low | (top.transpose(0, 1, 3, 2).reshape(rows, nbk, 16) << 4)).astype(np.float32) - 32.0
+        a = _f16(b[..., 108:110])[..., None] * sc
+        w = a[..., None] * (q.reshape(rows, nbk, 16, 16).astype(np.float32) - 4.0)
+    elif qtype == "IQ4_NL":
+        q = np.concatenate([b[..., 2:] & 0xF, b[..., 2:] >> 4], axis=-1)
+        w = _f16(b[..., 0:2])[..., None] * IQ4_GRID[q]
+    elif qtype == "IQ4_XS":
+        nbk = b.shape[1]
+        hi = (np.ascontiguousarray(b[..., 2:4]).view("<u2") >> (2 * np.arange(8, dtype=np.uint16))) & 3
+        lo = np.stack([b[..., 4:8] & 0xF, b[..., 4:8] >> 4], axis=-1).reshape(rows, nbk, 8)
+        ls = (lo | (hi.astype(np.uint8) << 4)).astype(np.float32)
+        qs = b[..., 8:].reshape(rows, nbk, 8, 16)
+        q = np.concatenate([qs & 0xF, qs >> 4], axis=-1)
+        dl = _f16(b[..., 0:2])[..., None] * (ls - 32.0)
+        w = dl[..., None] * IQ4_GRID[q]
     else:
         raise ValueError(qtype)
     return np.ascontiguousarray(w, dtype=np.float32).reshape(rows, cols)
@@ -197,6 +229,13 @@ def random_blocks(rng: np.random.Generator, qtype: str, rows: int, cols: int) ->
         raw[..., :192] = rng.integers(0, 256, (rows, n, 192), dtype=np.uint8)
         raw[..., 192:208] = rng.integers(-32, 32, (rows, n, 16), dtype=np.int8).view(np.uint8)
         raw[..., 208:] = _fp16_abs_normal(rng, (rows, n), 0.002).view(np.uint8).reshape(rows, n, 2)
+    elif qtype == "Q3_K":
+        raw[..., :108] = rng.integers(0, 256, (rows, n, 108), dtype=np.uint8)
+        raw[..., 108:] = _fp16_abs_normal(rng, (rows, n), 0.004).view(np.uint8).reshape(rows, n, 2)
+    elif qtype in ("IQ4_NL", "IQ4_XS"):
+        scale = 0.0005 if qtype == "IQ4_NL" else 0.00005
+        raw[..., 0:2] = _fp16_abs_normal(rng, (rows, n), scale).view(np.uint8).reshape(rows, n, 2)
+        raw[..., 2:] = rng.integers(0, 256, (rows, n, nb - 2), dtype=np.uint8)
     else:
         raise ValueError(qtype)
     return raw.reshape(rows, n * nb)

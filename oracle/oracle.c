@@ -289,6 +289,54 @@ static void q6_k(const uint8_t* b, float* o) { /* dequant.cpp:83-101: w = (q - 3
     }
 }
 
+/* Q3_K (dequant.cpp:103-117): 110 B per 256 = hmask[32], qs[64], 12 scale bytes, d. Sixteen 16-value sub-blocks s,
+ * each with a 6-bit scale (stored + 32): low nibble from byte s (s < 8) or the high nibble of byte s - 8, top two bits
+ * from byte 8 + s % 4 at bit 2 (s / 4). Value v = 128 n + 32 j + i (i < 32): a 3-bit q = crumb j of qs[32 n + i] | bit
+ * (4 n + j) of hmask[i] << 2; w = (d (scale - 32)) (q - 4). */
+static void q3_k(const uint8_t* b, float* o) {
+  const uint8_t *hm = b, *qs = b + 32, *sc = b + 96;
+  const float d = f16(b + 108);
+  for (int s = 0; s < 16; s++) {
+    const int low = s < 8 ? sc[s] & 15 : sc[s - 8] >> 4, top = (sc[8 + (s & 3)] >> (2 * (s >> 2))) & 3;
+    const float a = d * (float)((low | top << 4) - 32);
+    const int n = s >> 3, j = (s >> 1) & 3;
+    for (int l = 0; l < 16; l++) {
+      const int i = 16 * (s & 1) + l;
+      const int q = ((qs[32 * n + i] >> (2 * j)) & 3) | ((hm[i] >> (4 * n + j)) & 1) << 2;
+      o[16 * s + l] = a * ((float)q - 4.0f);
+    }
+  }
+}
+
+/* the sixteen IQ4_NL / IQ4_XS code values (dequant.cpp:119, ggml's non-linear 4-bit grid) */
+static const int8_t IQ4_GRID[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+/* IQ4_NL (dequant.cpp:121-126): 18 B per 32, d then Q4_0's nibble layout; w = d grid[q] */
+static void iq4_nl(const uint8_t* b, float* o) {
+  const float d = f16(b);
+  for (int l = 0; l < 16; l++) {
+    o[l] = d * (float)IQ4_GRID[b[2 + l] & 15];
+    o[16 + l] = d * (float)IQ4_GRID[b[2 + l] >> 4];
+  }
+}
+
+/* IQ4_XS (dequant.cpp:128-140): 136 B per 256 = d, a u16 of high scale crumbs, 4 bytes of low scale nibbles, 8 x 16
+ * code bytes. 32-group g: scale ls = nibble (g % 2) of byte 4 + g / 2 | crumb g of the u16 << 4; its codes in Q4_0's
+ * layout at 8 + 16 g; w = (d (ls - 32)) grid[q] */
+static void iq4_xs(const uint8_t* b, float* o) {
+  const float d = f16(b);
+  const int hi = b[2] | b[3] << 8;
+  for (int g = 0; g < 8; g++) {
+    const int ls = ((b[4 + (g >> 1)] >> (4 * (g & 1))) & 15) | ((hi >> (2 * g)) & 3) << 4;
+    const float dl = d * (float)(ls - 32);
+    const uint8_t* q = b + 8 + 16 * g;
+    for (int l = 0; l < 16; l++) {
+      o[32 * g + l] = dl * (float)IQ4_GRID[q[l] & 15];
+      o[32 * g + 16 + l] = dl * (float)IQ4_GRID[q[l] >> 4];
+    }
+  }
+}
+
 static void f32_1(const uint8_t* b, float* o) { memcpy(o, b, 4); }
 static void f16_1(const uint8_t* b, float* o) { *o = f16(b); }
 static void bf16_1(const uint8_t* b, float* o) {
@@ -306,10 +354,11 @@ typedef struct {
   void (*block)(const uint8_t*, float*);
 } qtype_t;
 
-/* dequant.cpp:154-157's table, the formats this build reads */
+/* dequant.cpp:154-157's table */
 static const qtype_t TYPES[] = {{"F32", 1, 4, f32_1},      {"F16", 1, 2, f16_1},       {"BF16", 1, 2, bf16_1},
                                 {"Q4_0", 32, 18, q4_0},    {"Q4_1", 32, 20, q4_1},     {"Q8_0", 32, 34, q8_0},
-                                {"Q4_K", 256, 144, q4_k},  {"Q5_K", 256, 176, q5_k},   {"Q6_K", 256, 210, q6_k}};
+                                {"Q3_K", 256, 110, q3_k},  {"Q4_K", 256, 144, q4_k},   {"Q5_K", 256, 176, q5_k},
+                                {"Q6_K", 256, 210, q6_k},  {"IQ4_NL", 32, 18, iq4_nl}, {"IQ4_XS", 256, 136, iq4_xs}};
 
 int oracle_dequant_supported(const char* qtype) {
   for (size_t i = 0; i < sizeof(TYPES) / sizeof(TYPES[0]); i++)

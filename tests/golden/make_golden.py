@@ -90,8 +90,11 @@ def main() -> None:
     # --- dequant: random blocks (bytes uniform, fp16 scales N(0, 0.01) as tests/tensors.py:30-35), 8 rows of 512
     qt = {"Q4_0": gguf.GGMLQuantizationType.Q4_0, "Q4_1": gguf.GGMLQuantizationType.Q4_1,
           "Q8_0": gguf.GGMLQuantizationType.Q8_0, "Q4_K": gguf.GGMLQuantizationType.Q4_K,
-          "Q5_K": gguf.GGMLQuantizationType.Q5_K, "Q6_K": gguf.GGMLQuantizationType.Q6_K}
-    f16_at = {"Q4_0": (0,), "Q4_1": (0, 2), "Q8_0": (0,), "Q4_K": (0, 2), "Q5_K": (0, 2), "Q6_K": (208,)}
+          "Q5_K": gguf.GGMLQuantizationType.Q5_K, "Q6_K": gguf.GGMLQuantizationType.Q6_K,
+          "Q3_K": gguf.GGMLQuantizationType.Q3_K, "IQ4_NL": gguf.GGMLQuantizationType.IQ4_NL,
+          "IQ4_XS": gguf.GGMLQuantizationType.IQ4_XS}
+    f16_at = {"Q4_0": (0,), "Q4_1": (0, 2), "Q8_0": (0,), "Q4_K": (0, 2), "Q5_K": (0, 2), "Q6_K": (208,),
+              "Q3_K": (108,), "IQ4_NL": (0,), "IQ4_XS": (0,)}
     for i, (name, t) in enumerate(qt.items()):
         per, nb = moe_np.BLOCKS[name]
         rows, cols = 8, 512

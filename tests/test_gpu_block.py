@@ -73,13 +73,24 @@ def test_decode_fp32_tight(qtype):
     assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= FP32_TOL
 
 
-@pytest.mark.parametrize("qtype", ["Q4_1", "Q5_K", "Q6_K"])
+@pytest.mark.parametrize("qtype", ["Q4_1", "Q5_K", "Q6_K", "Q3_K", "IQ4_NL", "IQ4_XS"])
 def test_decode_generic_formats(qtype):
     """The formats without a register-decoding GEMV (the generic staged kernel) through the block, fp32 tight."""
     layer, x, _ = moe_np.make_block(6, 12, qtype=qtype, x_bf16=False, E=16, H=512, F=256)
     y, dbg = run(layer, x, act="f32", path="gemv", T=12)
     ids, w = check_routing(dbg, x, layer, 8)
     assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= FP32_TOL
+
+
+@pytest.mark.parametrize("qtype,down", [("Q3_K", "Q3_K"), ("IQ4_XS", "IQ4_XS"), ("IQ4_NL", "Q6_K"), ("Q4_K", "Q3_K")])
+def test_low_bit_formats_prefill_and_mixed(qtype, down):
+    """Q3_K, IQ4_NL and IQ4_XS experts (the reference's low-bit files: dequant.cpp:103-140), alone and under another
+    down type, through the block's automatic path at a prefill size and a decode size, bf16 activations."""
+    for T in (300, 6):
+        layer, x, _ = moe_np.make_block(40 + T, T, qtype=qtype, down_qtype=down, E=16, H=512, F=256)
+        y, dbg = run(layer, x, act="bf16", path="auto", T=T)
+        ids, w = check_routing(dbg, x, layer, 8)
+        assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= BF16_TOL, T
 
 
 @pytest.mark.parametrize("qtype", ["Q4_0", "Q8_0", "Q4_K"])

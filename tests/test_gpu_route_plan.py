@@ -136,7 +136,7 @@ def test_dispatch_vs_oracle(orc, T, E, zipf):
     assert np.array_equal(off, roff) and np.array_equal(perm, rperm) and np.array_equal(slot, rslot)
 
 
-@pytest.mark.parametrize("qtype", ("Q4_0", "Q4_1", "Q8_0", "Q4_K", "Q5_K", "Q6_K"))
+@pytest.mark.parametrize("qtype", ("Q4_0", "Q4_1", "Q8_0", "Q4_K", "Q5_K", "Q6_K", "Q3_K", "IQ4_NL", "IQ4_XS"))
 def test_dequant_golden(golden, qtype):
     raw, want = golden[f"dq_{qtype}_raw"], golden[f"dq_{qtype}_cpp"]
     got = P.dequant_rows(qtype, raw, want.shape[1])

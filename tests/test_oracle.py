@@ -92,7 +92,7 @@ def test_dispatch_is_stable_permutation(golden, orc):
         assert (flat[seg] == e).all() and (np.diff(seg) > 0).all()
 
 
-@pytest.mark.parametrize("qtype", ("Q4_0", "Q4_1", "Q8_0", "Q4_K", "Q5_K", "Q6_K"))
+@pytest.mark.parametrize("qtype", ("Q4_0", "Q4_1", "Q8_0", "Q4_K", "Q5_K", "Q6_K", "Q3_K", "IQ4_NL", "IQ4_XS"))
 def test_dequant_bit_exact(golden, orc, qtype):
     """C and NumPy dequant equal the reference's compiled dequant_rows bit for bit, and gguf-py's values."""
     raw, want = golden[f"dq_{qtype}_raw"], golden[f"dq_{qtype}_cpp"]
