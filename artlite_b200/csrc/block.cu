@@ -111,13 +111,7 @@ int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* 
                        Marker& mk, int mult_gu, int mult_dn) {
   const artlite_moe_desc& d = h->d;
   const int H = d.hidden, E = d.n_experts, K = d.top_k;
-  static const bool fold_off = [] {
-    const char* v = getenv("ARTLITE_ROUTER_FOLD");
-    return v && v[0] == '0';
-  }();
-  // decode-sized: the router with the routing and dispatch in its last CTA (one launch)
-  const bool fold = !fold_off && mult_gu > 0 && router_small_ok(T, H) && router_route_ok(T, H, E, K);
-  if (T > 0 && !fold) {
+  if (T > 0) {
     if (router_small_ok(T, H))
       AL_TRY(launch_router_small(xd, d.act_dtype, L.router.ptr, L.router_qtype, L.has_bias ? L.bias.as<float>() : nullptr,
                                  T, H, E, h->logits.as<float>(), st));
@@ -146,12 +140,7 @@ int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* 
     da.unit_rows = kGemvTokens;
     da.unit_mult = mult_gu;
     da.unit_off = h->unit_gu.as<int32_t>();
-    if (fold)
-      AL_TRY(launch_router_route_small(xd, d.act_dtype, L.router.ptr, L.router_qtype,
-                                       L.has_bias ? L.bias.as<float>() : nullptr, T, H, h->logits.as<float>(), ra, da,
-                                       mult_dn, h->unit_dn.as<int32_t>(), h->rdone.as<int>(), st));
-    else
-      AL_TRY(launch_route_dispatch_small(ra, da, mult_dn, h->unit_dn.as<int32_t>(), st));
+    AL_TRY(launch_route_dispatch_small(ra, da, mult_dn, h->unit_dn.as<int32_t>(), st));
   } else {
     AL_TRY(launch_route(ra, st));
     AL_TRY(launch_dispatch(da, st));
@@ -400,8 +389,6 @@ int artlite_moe_create(const artlite_moe_desc* desc, artlite_moe** out) {
   // the fused decode kernel's grid barrier, zeroed now: a forward captured into a graph must not allocate
   AL_TRY(h->bar.reserve(1024));
   AL_CUDA(cudaMemsetAsync(h->bar.ptr, 0, 1024, h->st));
-  AL_TRY(h->rdone.reserve(256));
-  AL_CUDA(cudaMemsetAsync(h->rdone.ptr, 0, 256, h->st));
   if (world > 1) AL_TRY(ep_create(h.get()));
   AL_CUDA(cudaStreamSynchronize(h->st));
   *out = h.release();

@@ -48,7 +48,6 @@ struct artlite_moe {
   artlite::DevBuf h, y, xp, tiles;
   artlite::DevBuf xn;  // the normed input rows (layers with artlite_moe_set_norm)
   artlite::DevBuf bar;  // the fused decode kernel's grid barrier (zeroed once; left zeroed by every complete run)
-  artlite::DevBuf rdone;  // the small-batch router's count of finished CTAs (zeroed once; left zeroed by every run)
   artlite::DevBuf sh_y, sh_s, sh_iota, sh_off;  // the shared expert's outputs (T rows), gates (T), 0..T-1, {0, T} / {T}
   artlite::DevBuf sh_hq;  // the fused decode kernel's shared-expert h rows (fragment order, then their group sums)
   int64_t last_T = 0;

@@ -30,6 +30,7 @@
 #include <nccl.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include <algorithm>
 #include <mutex>
@@ -48,6 +49,10 @@ struct Nccl {
   void* so = nullptr;
   ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
   ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  // (non-blocking communicators: present from NCCL 2.14; without them the initialisation blocks)
+  ncclResult_t (*commInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*commGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*commFinalize)(ncclComm_t) = nullptr;
   ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*commAbort)(ncclComm_t) = nullptr;
   ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
@@ -83,20 +88,64 @@ int nccl(Nccl** out) {
     sym(n.groupEnd, "ncclGroupEnd");
     sym(n.errorString, "ncclGetErrorString");
     AL_CHECK(ok, ARTLITE_ENCCL, "nccl: a symbol is missing from the loaded library");
+    sym(n.commInitRankConfig, "ncclCommInitRankConfig");
+    sym(n.commGetAsyncError, "ncclCommGetAsyncError");
+    sym(n.commFinalize, "ncclCommFinalize");
+    if (!n.commInitRankConfig || !n.commGetAsyncError || !n.commFinalize)
+      n.commInitRankConfig = nullptr, n.commGetAsyncError = nullptr, n.commFinalize = nullptr;
     g_nccl = n;
   }
   *out = &g_nccl;
   return ARTLITE_OK;
 }
 
+// (a call on a non-blocking communicator may answer ncclInProgress: accepted here, settled by nccl_settle)
 #define AL_NCCL(call)                                                                               \
   do {                                                                                              \
     const ncclResult_t r_ = (call);                                                                 \
-    if (r_ != ncclSuccess) {                                                                        \
+    if (r_ != ncclSuccess && r_ != ncclInProgress) {                                                \
       ::artlite::set_error("%s:%d %s: %s", __FILE__, __LINE__, #call, N->errorString(r_));          \
       return ARTLITE_ENCCL;                                                                         \
     }                                                                                               \
   } while (0)
+
+int now_ms() {
+  timespec t;
+  clock_gettime(CLOCK_MONOTONIC, &t);
+  return (int)(t.tv_sec * 1000 + t.tv_nsec / 1000000);
+}
+
+// Waits, up to timeout_ms, until the communicator's pending work (its initialisation, a group's enqueue) is done:
+// ARTLITE_OK, ARTLITE_ENCCL (NCCL reported an error) or ARTLITE_ETIMEOUT. A blocking communicator is always settled.
+int nccl_settle(Nccl* N, ncclComm_t comm, int timeout_ms, const char* what) {
+  if (!N->commGetAsyncError) return ARTLITE_OK;
+  const int t0 = now_ms();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    const ncclResult_t r = N->commGetAsyncError(comm, &st);
+    if (r != ncclSuccess) st = r;
+    if (st == ncclSuccess) return ARTLITE_OK;
+    if (st != ncclInProgress) {
+      set_error("%s: %s", what, N->errorString(st));
+      return ARTLITE_ENCCL;
+    }
+    if (now_ms() - t0 > timeout_ms) {
+      set_error("%s: not done within %d ms", what, timeout_ms);
+      return ARTLITE_ETIMEOUT;
+    }
+    struct timespec ts{0, 20000};
+    nanosleep(&ts, nullptr);
+  }
+}
+
+// the bound on a host wait for the peers (ARTLITE_EP_TIMEOUT_MS, default 30 s) and on the communicator's forming
+// (ARTLITE_EP_INIT_TIMEOUT_MS, default 120 s)
+int env_ms(const char* name, int dflt) {
+  const char* v = getenv(name);
+  const int t = v ? atoi(v) : 0;
+  return t > 0 ? t : dflt;
+}
+int ep_timeout_ms() { return env_ms("ARTLITE_EP_TIMEOUT_MS", 30000); }
 
 __global__ void iota_kernel(int32_t* p, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -169,8 +218,16 @@ void ep_destroy(artlite_moe* h) {
     Nccl* N;
     if (nccl(&N) == ARTLITE_OK) {
       // (after a failed exchange the peers may never complete theirs: abort, which does not wait for them)
-      if (h->ep_failed) N->commAbort(static_cast<ncclComm_t>(h->comm));
-      else N->commDestroy(static_cast<ncclComm_t>(h->comm));
+      // (a non-blocking communicator is finalized first, with a bound: one that does not settle is aborted)
+      ncclComm_t c = static_cast<ncclComm_t>(h->comm);
+      bool abort = h->ep_failed;
+      if (!abort && N->commFinalize) {
+        const ncclResult_t r = N->commFinalize(c);
+        abort = (r != ncclSuccess && r != ncclInProgress) ||
+                nccl_settle(N, c, ep_timeout_ms(), "expert parallelism: finalize") != ARTLITE_OK;
+      }
+      if (abort) N->commAbort(c);
+      else N->commDestroy(c);
     }
     h->comm = nullptr;
   }
@@ -191,11 +248,6 @@ namespace {
 int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t T, cudaStream_t st, Marker& mk,
                     const void* res);
 
-int ep_timeout_ms() {
-  const char* v = getenv("ARTLITE_EP_TIMEOUT_MS");
-  const int t = v ? atoi(v) : 0;
-  return t > 0 ? t : 30000;
-}
 }  // namespace
 
 // The EP forward; any failure once the exchanges have begun aborts the communicator (the peers' next bounded wait
@@ -233,6 +285,7 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
     AL_NCCL(N->recv(h->ep_rcounts.as<int32_t>() + q * El, El, ncclInt32, q, comm, st));
   }
   AL_NCCL(N->groupEnd());
+  AL_TRY(nccl_settle(N, comm, ep_timeout_ms(), "expert parallelism: count exchange"));
   AL_CUDA(cudaMemcpyAsync(h->hb_counts, h->counts.ptr, sizeof(int32_t) * E, cudaMemcpyDeviceToHost, st));
   AL_CUDA(cudaMemcpyAsync(h->hb_counts + E, h->ep_rcounts.ptr, sizeof(int32_t) * E, cudaMemcpyDeviceToHost, st));
   const int tmo = ep_timeout_ms();
@@ -368,6 +421,7 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
         AL_NCCL(N->recv(xr + h->ep_cr_pos[k] * H, (size_t)h->ep_cr_rows[k] * H, ncclBfloat16, q, comm, h->ep_st));
     }
     AL_NCCL(N->groupEnd());
+    AL_TRY(nccl_settle(N, comm, ep_timeout_ms(), "expert parallelism: exchange"));
     AL_CUDA(cudaEventRecord(ev_r[c], h->ep_st));
   }
   // 5: the local experts in place: the own groups while the rows travel, then each chunk of the peers' groups once its
@@ -438,6 +492,7 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
         AL_NCCL(N->recv(ys + h->ep_cs_pos[k] * H * el, (size_t)h->ep_cs_rows[k] * H, dt, q, comm, h->ep_st));
     }
     AL_NCCL(N->groupEnd());
+    AL_TRY(nccl_settle(N, comm, ep_timeout_ms(), "expert parallelism: exchange"));
   }
   AL_CUDA(cudaEventRecord(ev_b, h->ep_st));
   AL_CUDA(cudaStreamWaitEvent(st, ev_b, 0));
@@ -510,8 +565,25 @@ int artlite_moe_ep_init(artlite_moe* h, const void* unique_id, int bytes) {
   AL_CUDA(cudaSetDevice(h->dev));
   ncclUniqueId id;
   memcpy(&id, unique_id, sizeof id);
-  ncclComm_t comm;
-  AL_NCCL(N->commInitRank(&comm, h->d.ep_world, id, h->d.ep_rank));
+  ncclComm_t comm = nullptr;
+  if (!N->commInitRankConfig) {
+    AL_NCCL(N->commInitRank(&comm, h->d.ep_world, id, h->d.ep_rank));
+    h->comm = comm;
+    return ARTLITE_OK;
+  }
+  // non-blocking: the host's wait for every rank to join is bounded; past it the half-formed communicator is aborted
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  AL_NCCL(N->commInitRankConfig(&comm, h->d.ep_world, id, h->d.ep_rank, &cfg));
+  const int tmo = env_ms("ARTLITE_EP_INIT_TIMEOUT_MS", 120000);
+  const int rc = nccl_settle(N, comm, tmo, "ep_init");
+  if (rc != ARTLITE_OK) {
+    N->commAbort(comm);
+    if (rc == ARTLITE_ETIMEOUT)
+      set_error("ep_init: rank %d of %d: the communicator did not form within %d ms (aborted)", h->d.ep_rank,
+                h->d.ep_world, tmo);
+    return rc;
+  }
   h->comm = comm;
   return ARTLITE_OK;
 }

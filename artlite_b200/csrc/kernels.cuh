@@ -82,12 +82,6 @@ int launch_router(const void* x, int x_dtype, const void* w, int w_dtype, const 
 // the same for decode-sized batches (T <= kRouterSmallTokens, H % 4 == 0): a warp per (token, expert) over the grid
 constexpr int kRouterSmallTokens = 256;
 bool router_small_ok(int64_t T, int H);
-// the router of 1 - 16 tokens (H % 256 == 0, E <= 256, T k <= 512) with the routing and dispatch of
-// launch_route_dispatch_small folded into its last CTA; done: a device int, zero, left zero
-bool router_route_ok(int64_t T, int H, int E, int k);
-int launch_router_route_small(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T,
-                              int H, float* logits, const RouteArgs& r, const DispatchArgs& a, int mult2,
-                              int32_t* unit_off2, int* done, cudaStream_t st);
 int launch_router_small(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H,
                         int E, float* logits, cudaStream_t st);
 

@@ -126,8 +126,7 @@ __device__ __forceinline__ void route_row(const RouteArgs& a, int64_t t, int lan
 // E <= kSmallExperts, NT >= E): every token routed into shared memory (a warp a row), the ids and weights copied out
 // for the caller, then the histogram, the scan and the stable rank of the pairs exactly as the dispatch kernels do for
 // a single block, and both expert GEMVs' unit scans. sm: dynamic shared memory of
-// 4 ((NT / 32 + 2) E + 1) + 8 E + 8 P bytes. Called by dispatch.cu's route_dispatch_small and by the last CTA of
-// router.cu's router_route_kernel.
+// 4 ((NT / 32 + 2) E + 1) + 8 E + 8 P bytes. Called by dispatch.cu's route_dispatch_small.
 template <int J, int NT>
 __device__ __forceinline__ void route_dispatch_cta(RouteArgs r, const DispatchArgs& a, int mult2, int32_t* unit_off2,
                                                    int32_t* sm) {

@@ -9,7 +9,6 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
-#include "route.cuh"
 
 namespace artlite {
 
@@ -181,31 +180,6 @@ __global__ void __launch_bounds__(256) router_cta_kernel(const void* x, int x_dt
   for (int e = blockIdx.x; e < E; e += gridDim.x) router_cta_expert(x, x_dtype, w, w_dtype, bias, T, H, E, logits, e, part);
 }
 
-// The router of a decode-sized batch with its routing and dispatch folded in (one launch instead of two): a CTA per
-// expert writes its logits as router_cta_kernel does, publishes them (a fence) and counts itself done; the CTA whose
-// count is the E-th routes and dispatches every token (route_dispatch_cta, 256 threads) from the logits in L2, then
-// resets the count for the next launch.
-template <int J>
-__global__ void __launch_bounds__(256) router_route_kernel(const void* x, int x_dtype, const void* w, int w_dtype,
-                                                           const float* bias, int64_t T, int H, float* logits,
-                                                           RouteArgs r, DispatchArgs a, int mult2, int32_t* unit_off2,
-                                                           int* done) {
-  __shared__ float part[8][8];
-  __shared__ int last;
-  extern __shared__ int32_t sm[];
-  griddep_wait();
-  griddep_launch();
-  router_cta_expert(x, x_dtype, w, w_dtype, bias, T, H, a.E, logits, blockIdx.x, part);
-  if (threadIdx.x < 8) __threadfence();  // (the logit writers: their stores before the count)
-  __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(done, 1) == (int)gridDim.x - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  route_dispatch_cta<J, 256>(r, a, mult2, unit_off2, sm);
-  if (threadIdx.x == 0) *done = 0;
-}
-
 bool router_small_ok(int64_t T, int H) { return T <= kRouterSmallTokens && H % 4 == 0; }
 
 int launch_router_small(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H,
@@ -218,31 +192,6 @@ int launch_router_small(const void* x, int x_dtype, const void* w, int w_dtype, 
   const int64_t warps = T * E;
   const unsigned grid = (unsigned)std::min<int64_t>(cdiv(warps, 8), (int64_t)kNumSMs * 8);
   return launch_pdl(router_small_kernel, dim3(grid), dim3(256), 0, st, x, x_dtype, w, w_dtype, bias, T, H, E, logits);
-}
-
-bool router_route_ok(int64_t T, int H, int E, int k) {
-  return T >= 1 && T <= 16 && H % 256 == 0 && E <= 256 && T * k <= 512 && k <= 32;
-}
-
-int launch_router_route_small(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T,
-                              int H, float* logits, const RouteArgs& r, const DispatchArgs& a, int mult2,
-                              int32_t* unit_off2, int* done, cudaStream_t st) {
-  AL_CHECK(router_route_ok(T, H, a.E, r.k) && a.P == T * r.k && r.n == T && r.E == a.E && a.ids == r.ids &&
-               r.logits == logits && r.row == a.E && r.per_col >= a.E,
-           ARTLITE_EINVAL,
-           "router_route: T %lld H %d E %d k %d", (long long)T, H, a.E, r.k);
-  const size_t smem = sizeof(int32_t) * ((256 / 32 + 2) * (size_t)a.E + 1) + sizeof(int64_t) * a.E +
-                      (sizeof(int32_t) + sizeof(float)) * (size_t)a.P;
-  auto go = [&](auto kern) -> int {
-    AL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    return launch_pdl(kern, dim3((unsigned)a.E), dim3(256), smem, st, x, x_dtype, w, w_dtype, bias, T, H, logits, r, a, mult2,
-                      unit_off2, done);
-  };
-  const int J = (a.E + 31) / 32;
-  if (J <= 1) return go(router_route_kernel<1>);
-  if (J <= 2) return go(router_route_kernel<2>);
-  if (J <= 4) return go(router_route_kernel<4>);
-  return go(router_route_kernel<8>);
 }
 
 int launch_router(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H, int E,
