@@ -74,7 +74,7 @@ struct artlite_moe {
   static constexpr int kEpChunks = 4;  // the peers' row groups in up to this many expert chunks (pipelined)
   int ep_chunks = 1;
   cudaEvent_t ep_ev[2 + 2 * kEpChunks] = {};  // rows gathered, returns in, per chunk: rows in, outputs ready
-  artlite::DevBuf ep_rcounts, ep_loff, ep_lcounts, ep_wexp, ep_ident, xr, ys;
+  artlite::DevBuf ep_loff, ep_lcounts, ep_wexp, ep_ident, xr, ys;
   artlite::DevBuf ep_idx, xe;          // the regroup's row maps (2 x ep_max_rows) and expert-major rows
   int32_t* hb_idx = nullptr;           // pinned: the same maps, built on the host
   int ep_regroup = -1;                 // rows regrouped expert-major before the experts: -1 from 8 ranks, 0 no, 1 yes
@@ -86,6 +86,17 @@ struct artlite_moe {
   std::vector<int64_t> ep_cs_pos, ep_cs_rows, ep_cr_pos, ep_cr_rows;  // per (peer, chunk): sent / received blocks
   int64_t ep_max_rows = 0;             // rows a rank can receive: max_tokens K world
   bool ep_failed = false;              // an exchange failed: the communicator is aborted, never waited for
+  // the peer-store exchange (ep.cu): the rows and outputs written straight into the peers' receive buffers by this
+  // library's kernels over NVLink (CUDA IPC mappings), each block followed by a flag in the peer's flag array
+  artlite::DevBuf ep_flags;            // [2 world] u32: rows in from source q at q, outputs in from owner q at world + q
+  artlite::DevBuf ep_done;             // the push kernels' count of finished CTAs (zero, left zero)
+  artlite::DevBuf ep_fullc;            // [world][E] every rank's pairs per expert (the count exchange)
+  int32_t* hb_full = nullptr;          // pinned: the same
+  std::vector<uint8_t*> ep_peer_xr, ep_peer_ys;  // per rank: its receive / return buffer (null for this rank)
+  std::vector<uint32_t*> ep_peer_flags;
+  std::vector<int64_t> ep_peer_xr_bytes, ep_peer_ys_bytes;  // their sizes
+  bool ep_p2p = false;                 // rows and outputs by the peer-store kernels (else NCCL send / recv)
+  uint32_t ep_epoch = 0;               // forwards so far (the flags' value for the current one)
 };
 
 

@@ -147,6 +147,72 @@ int env_ms(const char* name, int dflt) {
 }
 int ep_timeout_ms() { return env_ms("ARTLITE_EP_TIMEOUT_MS", 30000); }
 
+// ---------------------------------------------------------------- the peer-store exchange
+//
+// A push copies up to kMaxPeers blocks of rows from this GPU's memory into other GPUs' buffers (CUDA IPC mappings,
+// reached over NVLink by plain 16-byte loads and stores: no TMA, no multicast), then raises each destination's flag to
+// the forward's epoch: every CTA fences its stores at system scope and counts itself done; the last one releases the
+// flags (st.release.sys). A wait (one warp, a lane per source) acquires the flags of every peer at system scope, up to
+// a deadline (about 2 s of the GPU's global timer), after which it reports ARTLITE_ETIMEOUT in the status word and
+// returns: no wait here is unbounded. The blocks of a push never overlap; a buffer is written only between two
+// count exchanges that both of its owner's consecutive forwards take part in, so no push can reach a buffer that its
+// owner is still reading.
+constexpr int kMaxPeers = 8;
+struct PushArgs {
+  const uint8_t* src[kMaxPeers];
+  uint8_t* dst[kMaxPeers];
+  int64_t n16[kMaxPeers + 1];  // exclusive prefix of the blocks' 16-byte units
+  uint32_t* flag[kMaxPeers];   // the destination's flag (null: no block to that rank)
+  int nb;
+  uint32_t epoch;
+  int* done;
+};
+
+__global__ void __launch_bounds__(512) ep_push_kernel(const PushArgs a) {
+  const int64_t total = a.n16[a.nb];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int b = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    while (i >= a.n16[b + 1]) b++;
+    const int64_t j = i - a.n16[b];
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.src[b]) + j);
+    reinterpret_cast<uint4*>(a.dst[b])[j] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(a.done, 1) == (int)gridDim.x - 1) {
+      __threadfence_system();
+      for (int k = 0; k < a.nb; k++)
+        if (a.flag[k]) asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flag[k]), "r"(a.epoch) : "memory");
+      *a.done = 0;
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// every peer's flag at flags[q] (q != r, q < W) reaching epoch; where: the report's detail
+__global__ void ep_wait_kernel(const uint32_t* flags, int W, int r, uint32_t epoch, DevStatus* status, int where) {
+  const int q = threadIdx.x;
+  if (q >= W || q == r) return;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + q) : "memory");
+    if ((int32_t)(v - epoch) >= 0) return;
+    if (global_ns() - t0 > 2000000000ull) {
+      report(status, ARTLITE_ETIMEOUT, where, q);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
 __global__ void iota_kernel(int32_t* p, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = (int32_t)i;
@@ -160,7 +226,6 @@ int ep_create(artlite_moe* h) {
   const int64_t T = d.max_tokens > 0 ? d.max_tokens : 1;
   const int64_t R = T * K * W;  // the most rows a rank can receive (every rank's pairs all on its experts)
   h->ep_max_rows = R;
-  AL_TRY(h->ep_rcounts.reserve(sizeof(int32_t) * E));
   AL_TRY(h->ep_loff.reserve(sizeof(int64_t) * (E + 1)));  // the W El row groups' offsets in the receive buffer
   AL_TRY(h->ep_lcounts.reserve(sizeof(int32_t) * E));     // their rows
   AL_TRY(h->ep_wexp.reserve(sizeof(int32_t) * E));        // their weight experts: group q El + e -> e
@@ -176,6 +241,12 @@ int ep_create(artlite_moe* h) {
   AL_TRY(h->unit_gu.reserve(sizeof(int32_t) * (E + 1)));
   AL_TRY(h->unit_dn.reserve(sizeof(int32_t) * (E + 1)));
   AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_counts), sizeof(int32_t) * 2 * E, cudaHostAllocDefault));
+  AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_full), sizeof(int32_t) * W * E, cudaHostAllocDefault));
+  AL_TRY(h->ep_fullc.reserve(sizeof(int32_t) * W * E));
+  AL_TRY(h->ep_flags.reserve(sizeof(uint32_t) * 2 * W));
+  AL_TRY(h->ep_done.reserve(256));
+  AL_CUDA(cudaMemsetAsync(h->ep_flags.ptr, 0, sizeof(uint32_t) * 2 * W, h->st));
+  AL_CUDA(cudaMemsetAsync(h->ep_done.ptr, 0, 256, h->st));
   AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_loff), sizeof(int64_t) * (E + 1), cudaHostAllocDefault));
   AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_lcounts), sizeof(int32_t) * E, cudaHostAllocDefault));
   AL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h->hb_idx), sizeof(int32_t) * 2 * R, cudaHostAllocDefault));
@@ -231,6 +302,15 @@ void ep_destroy(artlite_moe* h) {
     }
     h->comm = nullptr;
   }
+  for (uint8_t* p : h->ep_peer_xr)
+    if (p) cudaIpcCloseMemHandle(p);
+  for (uint8_t* p : h->ep_peer_ys)
+    if (p) cudaIpcCloseMemHandle(p);
+  for (uint32_t* p : h->ep_peer_flags)
+    if (p) cudaIpcCloseMemHandle(p);
+  h->ep_peer_xr.clear(), h->ep_peer_ys.clear(), h->ep_peer_flags.clear();
+  h->ep_p2p = false;
+  if (h->hb_full) cudaFreeHost(h->hb_full), h->hb_full = nullptr;
   for (cudaEvent_t& e : h->ep_ev)
     if (e) cudaEventDestroy(e), e = nullptr;
   if (h->ep_st) cudaStreamDestroy(h->ep_st), h->ep_st = nullptr;
@@ -245,6 +325,89 @@ void ep_destroy(artlite_moe* h) {
 }
 
 namespace {
+// One small exchange of `bytes` per rank over the communicator: every rank's `mine` into all[rank] (its own too);
+// bounded waits.
+int ep_allgather_host(artlite_moe* h, Nccl* N, ncclComm_t comm, const void* mine, void* all, size_t bytes) {
+  const int W = h->d.ep_world, r = h->d.ep_rank;
+  DevBuf buf;
+  AL_TRY(buf.reserve(bytes * (W + 1)));
+  uint8_t* b = buf.as<uint8_t>();
+  AL_CUDA(cudaMemcpyAsync(b + bytes * W, mine, bytes, cudaMemcpyHostToDevice, h->st));
+  AL_NCCL(N->groupStart());
+  for (int q = 0; q < W; q++) {
+    AL_NCCL(N->send(b + bytes * W, bytes, ncclUint8, q, comm, h->st));
+    AL_NCCL(N->recv(b + bytes * q, bytes, ncclUint8, q, comm, h->st));
+  }
+  AL_NCCL(N->groupEnd());
+  AL_TRY(nccl_settle(N, comm, ep_timeout_ms(), "ep_init: handle exchange"));
+  AL_CUDA(cudaMemcpyAsync(all, b, bytes * W, cudaMemcpyDeviceToHost, h->st));
+  const int rc = wait_deadline(h->st, ep_timeout_ms());
+  if (rc == ARTLITE_ETIMEOUT) set_error("ep_init: rank %d: the handle exchange did not complete", r);
+  return rc;
+}
+
+// The peer-store exchange's set-up (every rank takes part): the CUDA IPC handles of each rank's receive buffer, return
+// buffer and flags go to every rank, which maps its peers' (NVLink peer access); it is used only if every rank wants
+// it (ARTLITE_EP_EXCHANGE=nccl keeps NCCL send / recv; so do expert chunks) and every rank mapped every peer.
+int ep_p2p_setup(artlite_moe* h, Nccl* N, ncclComm_t comm) {
+  const int W = h->d.ep_world, r = h->d.ep_rank;
+  const char* v = getenv("ARTLITE_EP_EXCHANGE");
+  struct Slot {
+    int32_t ok, pad[11];
+    int64_t xr_bytes, ys_bytes;  // (a push checks its block's end against the owner's buffer)
+    cudaIpcMemHandle_t hx, hy, hf;
+  };
+  Slot m;
+  memset(&m, 0, sizeof m);
+  m.xr_bytes = (int64_t)h->xr.bytes;
+  m.ys_bytes = (int64_t)h->ys.bytes;
+  m.ok = !(v && !strcmp(v, "nccl")) && h->ep_chunks == 1 && W <= kMaxPeers &&
+         cudaIpcGetMemHandle(&m.hx, h->xr.ptr) == cudaSuccess && cudaIpcGetMemHandle(&m.hy, h->ys.ptr) == cudaSuccess &&
+         cudaIpcGetMemHandle(&m.hf, h->ep_flags.ptr) == cudaSuccess;
+  cudaGetLastError();  // (a refusal above is an answer, not an error)
+  std::vector<Slot> all(W);
+  AL_TRY(ep_allgather_host(h, N, comm, &m, all.data(), sizeof(Slot)));
+  bool ok = true;
+  for (const Slot& q : all) ok = ok && q.ok;
+  h->ep_peer_xr.assign(W, nullptr);
+  h->ep_peer_ys.assign(W, nullptr);
+  h->ep_peer_flags.assign(W, nullptr);
+  h->ep_peer_xr_bytes.assign(W, 0);
+  h->ep_peer_ys_bytes.assign(W, 0);
+  for (int q = 0; q < W; q++) h->ep_peer_xr_bytes[q] = all[q].xr_bytes, h->ep_peer_ys_bytes[q] = all[q].ys_bytes;
+  if (ok)
+    for (int q = 0; q < W && ok; q++) {
+      if (q == r) continue;
+      void *px = nullptr, *py = nullptr, *pf = nullptr;
+      ok = cudaIpcOpenMemHandle(&px, all[q].hx, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess &&
+           cudaIpcOpenMemHandle(&py, all[q].hy, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess &&
+           cudaIpcOpenMemHandle(&pf, all[q].hf, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+      h->ep_peer_xr[q] = static_cast<uint8_t*>(px);
+      h->ep_peer_ys[q] = static_cast<uint8_t*>(py);
+      h->ep_peer_flags[q] = static_cast<uint32_t*>(pf);
+    }
+  cudaGetLastError();
+  // every rank's verdict: the exchange is used only where every rank mapped every peer
+  int32_t mine = ok ? 1 : 0;
+  std::vector<int32_t> verdicts(W);
+  AL_TRY(ep_allgather_host(h, N, comm, &mine, verdicts.data(), sizeof(int32_t)));
+  bool all_ok = true;
+  for (int32_t x : verdicts) all_ok = all_ok && x == 1;
+  if (!all_ok) {
+    for (int q = 0; q < W; q++) {
+      if (h->ep_peer_xr[q]) cudaIpcCloseMemHandle(h->ep_peer_xr[q]);
+      if (h->ep_peer_ys[q]) cudaIpcCloseMemHandle(h->ep_peer_ys[q]);
+      if (h->ep_peer_flags[q]) cudaIpcCloseMemHandle(h->ep_peer_flags[q]);
+    }
+    h->ep_peer_xr.assign(W, nullptr);
+    h->ep_peer_ys.assign(W, nullptr);
+    h->ep_peer_flags.assign(W, nullptr);
+    cudaGetLastError();
+  }
+  h->ep_p2p = all_ok;
+  return ARTLITE_OK;
+}
+
 int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t T, cudaStream_t st, Marker& mk,
                     const void* res);
 
@@ -278,16 +441,16 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   const int64_t P = T * K;
   // 1: routing and the dispatch over all experts
   AL_TRY(route_and_dispatch(h, L, xd, T, st, mk));
-  // 2: counts, then the plan on the host
+  // 2: counts (every rank's whole count vector to every rank: the peer-store exchange places its blocks by the other
+  // ranks' plans), then the plan on the host
   AL_NCCL(N->groupStart());
   for (int q = 0; q < W; q++) {
-    AL_NCCL(N->send(h->counts.as<int32_t>() + q * El, El, ncclInt32, q, comm, st));
-    AL_NCCL(N->recv(h->ep_rcounts.as<int32_t>() + q * El, El, ncclInt32, q, comm, st));
+    AL_NCCL(N->send(h->counts.as<int32_t>(), E, ncclInt32, q, comm, st));
+    AL_NCCL(N->recv(h->ep_fullc.as<int32_t>() + (size_t)q * E, E, ncclInt32, q, comm, st));
   }
   AL_NCCL(N->groupEnd());
   AL_TRY(nccl_settle(N, comm, ep_timeout_ms(), "expert parallelism: count exchange"));
-  AL_CUDA(cudaMemcpyAsync(h->hb_counts, h->counts.ptr, sizeof(int32_t) * E, cudaMemcpyDeviceToHost, st));
-  AL_CUDA(cudaMemcpyAsync(h->hb_counts + E, h->ep_rcounts.ptr, sizeof(int32_t) * E, cudaMemcpyDeviceToHost, st));
+  AL_CUDA(cudaMemcpyAsync(h->hb_full, h->ep_fullc.ptr, sizeof(int32_t) * W * E, cudaMemcpyDeviceToHost, st));
   const int tmo = ep_timeout_ms();
   const int rc = wait_deadline(st, tmo);
   if (rc == ARTLITE_ETIMEOUT) {  // a peer that never sent its counts (the caller aborts the communicator)
@@ -296,6 +459,10 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
     return ARTLITE_ETIMEOUT;
   }
   AL_TRY(rc);
+  const int32_t* full = h->hb_full;      // [q][e]: rank q's pairs for expert e (all E)
+  for (int e = 0; e < E; e++) h->hb_counts[e] = full[(size_t)r * E + e];
+  for (int q = 0; q < W; q++)
+    for (int e = 0; e < El; e++) h->hb_counts[E + q * El + e] = full[(size_t)q * E + r * El + e];
   const int32_t* sc = h->hb_counts;      // this rank's pairs per expert (all E)
   const int32_t* rcv = h->hb_counts + E; // [q][e]: peer q's pairs for local expert e
   std::vector<int64_t>& send_base = h->ep_send_base;
@@ -408,9 +575,55 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   cudaEvent_t* ev_y = h->ep_ev + 2 + C;  // [C] a chunk's outputs ready
   AL_CUDA(cudaEventRecord(ev_g, st));
   AL_TRY(mk.mark());
+  // rows a source s sends to rank q (its pairs for q's experts), from the count matrix
+  auto rows_to = [&](int s, int q) {
+    int64_t n = 0;
+    for (int e = 0; e < El; e++) n += full[(size_t)s * E + q * El + e];
+    return n;
+  };
+  const bool p2p = h->ep_p2p;
+  const uint32_t epoch = ++h->ep_epoch;
+  DevStatus* status = h->status.as<DevStatus>();
   // 4: the peers' rows, chunk by chunk, on the exchange stream
   AL_CUDA(cudaStreamWaitEvent(h->ep_st, ev_g, 0));
-  for (int c = 0; c < C; c++) {
+  if (p2p) {  // each block straight into its place in the owner's receive buffer: after the sources before this rank
+    PushArgs pa{};
+    int nb = 0;
+    int64_t acc = 0;
+    for (int q = 0; q < W; q++) {
+      if (q == r) continue;
+      int64_t at = 0;  // (this rank's block in q's receive buffer: the blocks of the sources before it)
+      for (int s2 = 0; s2 < r; s2++)
+        if (s2 != q) at += rows_to(s2, q);
+      AL_CHECK((at + send_rows[q]) * H * 2 <= h->ep_peer_xr_bytes[q], ARTLITE_EDEVICE,
+               "expert parallelism: rank %d's rows for rank %d end past its receive buffer (%lld rows at %lld)", r, q,
+               (long long)send_rows[q], (long long)at);
+      pa.src[nb] = reinterpret_cast<const uint8_t*>(xp + send_base[q] * H);
+      pa.dst[nb] = h->ep_peer_xr[q] + at * H * 2;
+      pa.n16[nb] = acc;
+      acc += send_rows[q] * H * 2 / 16;
+      pa.flag[nb] = h->ep_peer_flags[q] + r;
+      nb++;
+    }
+    pa.n16[nb] = acc;
+    pa.nb = nb;
+    pa.epoch = epoch;
+    pa.done = h->ep_done.as<int>();
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(acc, 512 * 4), 64));
+    ep_push_kernel<<<grid, 512, 0, h->ep_st>>>(pa);
+    AL_LAUNCHED();
+  }
+  // the peers' rows are in (the main stream): their flags (peer-store), or the exchange stream's event (NCCL)
+  auto rows_in = [&](int c) -> int {
+    if (!p2p) {
+      AL_CUDA(cudaStreamWaitEvent(st, ev_r[c], 0));
+      return ARTLITE_OK;
+    }
+    ep_wait_kernel<<<1, 32, 0, st>>>(h->ep_flags.as<uint32_t>(), W, r, epoch, status, 40);
+    AL_LAUNCHED();
+    return ARTLITE_OK;
+  };
+  for (int c = 0; c < C && !p2p; c++) {
     AL_NCCL(N->groupStart());
     for (int q = 0; q < W; q++) {
       if (q == r) continue;
@@ -437,7 +650,7 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   quiet.ns = kStages;  // (no stage events inside the expert calls)
   const int jo = (W - 1) * El;
   if (regroup) {  // every row in: gathered expert-major, the experts, the outputs gathered back into xr's order
-    AL_CUDA(cudaStreamWaitEvent(st, ev_r[0], 0));
+    AL_TRY(rows_in(0));
     uint16_t* xe = h->xe.as<uint16_t>();
     const int32_t* idx = h->ep_idx.as<int32_t>();
     if (Rl) AL_TRY(launch_gather(xr, ARTLITE_BF16, idx, Rl, 1, H, xe, st, nullptr, 0, 0));
@@ -458,7 +671,7 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
     AL_TRY(mk.mark());
     const int Gc = (W - 1) * Ec;  // groups a chunk
     for (int c = 0; c < C; c++) {
-      AL_CUDA(cudaStreamWaitEvent(st, ev_r[c], 0));
+      AL_TRY(rows_in(c));
       int64_t rows = 0;
       for (int q = 0; q < W; q++)
         if (q != r) rows += h->ep_cr_rows[(size_t)q * C + c];
@@ -480,7 +693,34 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   const ncclDataType_t dt = ydt == ARTLITE_BF16 ? ncclBfloat16 : ncclFloat32;
   uint8_t* yo = static_cast<uint8_t*>(yrows);
   uint8_t* ys = h->ys.as<uint8_t>();
-  for (int c = 0; c < C; c++) {
+  if (p2p) {  // each source's outputs straight into its return buffer, where its dispatch order put the block for
+              // this rank (after its blocks for the ranks before this one)
+    AL_CUDA(cudaStreamWaitEvent(h->ep_st, ev_y[0], 0));
+    PushArgs pa{};
+    int nb = 0;
+    int64_t acc = 0;
+    for (int q = 0; q < W; q++) {
+      if (q == r) continue;
+      int64_t at = 0;
+      for (int q2 = 0; q2 < r; q2++) at += rows_to(q, q2);
+      AL_CHECK((at + h->ep_cr_rows[q]) * H * (int64_t)el <= h->ep_peer_ys_bytes[q], ARTLITE_EDEVICE,
+               "expert parallelism: rank %d's outputs for rank %d end past its return buffer", r, q);
+      pa.src[nb] = yo + h->ep_cr_pos[q] * H * el;
+      pa.dst[nb] = h->ep_peer_ys[q] + at * H * el;
+      pa.n16[nb] = acc;
+      acc += h->ep_cr_rows[q] * H * (int64_t)el / 16;
+      pa.flag[nb] = h->ep_peer_flags[q] + W + r;
+      nb++;
+    }
+    pa.n16[nb] = acc;
+    pa.nb = nb;
+    pa.epoch = epoch;
+    pa.done = h->ep_done.as<int>();
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(acc, 512 * 4), 64));
+    ep_push_kernel<<<grid, 512, 0, h->ep_st>>>(pa);
+    AL_LAUNCHED();
+  }
+  for (int c = 0; c < C && !p2p; c++) {
     AL_CUDA(cudaStreamWaitEvent(h->ep_st, ev_y[c], 0));
     AL_NCCL(N->groupStart());
     for (int q = 0; q < W; q++) {
@@ -496,6 +736,10 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
   }
   AL_CUDA(cudaEventRecord(ev_b, h->ep_st));
   AL_CUDA(cudaStreamWaitEvent(st, ev_b, 0));
+  if (p2p) {  // every owner's outputs for this rank's rows are in
+    ep_wait_kernel<<<1, 32, 0, st>>>(h->ep_flags.as<uint32_t>() + W, W, r, epoch, status, 41);
+    AL_LAUNCHED();
+  }
   AL_TRY(mk.mark());
   // 7: the combine of this rank's tokens (its own block read where its experts wrote it)
   CombineOwn own;
@@ -569,7 +813,7 @@ int artlite_moe_ep_init(artlite_moe* h, const void* unique_id, int bytes) {
   if (!N->commInitRankConfig) {
     AL_NCCL(N->commInitRank(&comm, h->d.ep_world, id, h->d.ep_rank));
     h->comm = comm;
-    return ARTLITE_OK;
+    return ep_p2p_setup(h, N, comm);
   }
   // non-blocking: the host's wait for every rank to join is bounded; past it the half-formed communicator is aborted
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
@@ -585,7 +829,12 @@ int artlite_moe_ep_init(artlite_moe* h, const void* unique_id, int bytes) {
     return rc;
   }
   h->comm = comm;
-  return ARTLITE_OK;
+  const int rs = ep_p2p_setup(h, N, comm);
+  if (rs != ARTLITE_OK) {  // (the peers' waits on this rank then fail too: the communicator is gone)
+    N->commAbort(comm);
+    h->comm = nullptr;
+  }
+  return rs;
 }
 
 }  // extern "C"

@@ -1,5 +1,6 @@
-"""Expert parallelism on 2 and 4 GPUs (NCCL, one process per GPU): each rank owns 1/N of the experts and its own tokens;
-the EP forward (token rows out by NCCL send / recv, local tcgen05 or GEMV experts, outputs back, local combine) must
+"""Expert parallelism on 2 and 4 GPUs (one process per GPU): each rank owns 1/N of the experts and its own tokens;
+the EP forward (token rows out by the peer-store kernels over NVLink, or by NCCL send / recv with expert chunks or
+ARTLITE_EP_EXCHANGE=nccl; local tcgen05 or GEMV experts, outputs back the same way, local combine) must
 equal, on every rank, the single-GPU block over the same tokens with all experts, with one or four expert chunks and
 with the rows regrouped expert-major before the experts (the default from 8 ranks, forced here), and with a shared
 expert (held whole by every rank, run on its own tokens). Skipped with fewer GPUs than ranks.
@@ -15,8 +16,9 @@ pytestmark = pytest.mark.gpu
 H, E, K, F = 512, 16, 4, 256
 
 
-def _rank(rank, world, uid, path, T, Tmax, chunks, regroup, shared, q):
+def _rank(rank, world, uid, path, T, Tmax, chunks, regroup, shared, q, exchange="p2p"):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["ARTLITE_EP_EXCHANGE"] = exchange
     os.environ["ARTLITE_EP_CHUNKS"] = str(chunks)
     os.environ["ARTLITE_EP_REGROUP"] = regroup
     os.environ["ARTLITE_EP_TIMEOUT_MS"] = "20000"
@@ -54,10 +56,11 @@ def _rank(rank, world, uid, path, T, Tmax, chunks, regroup, shared, q):
 
 
 @pytest.mark.parametrize("world", [2, 4])
-@pytest.mark.parametrize("path,T,chunks,regroup,shared", [("tc", 300, 1, "0", False), ("tc", 300, 4, "0", False),
-                                                          ("tc", 300, 1, "1", False), ("gemv", 7, 1, "0", False),
-                                                          ("tc", 300, 1, "0", True), ("gemv", 7, 1, "0", True)])
-def test_ep_matches_single_gpu(path, T, chunks, regroup, shared, world):
+@pytest.mark.parametrize("path,T,chunks,regroup,shared,exchange", [
+    ("tc", 300, 1, "0", False, "p2p"), ("tc", 300, 1, "0", False, "nccl"), ("tc", 300, 4, "0", False, "p2p"),
+    ("tc", 300, 1, "1", False, "p2p"), ("gemv", 7, 1, "0", False, "p2p"), ("tc", 300, 1, "0", True, "p2p"),
+    ("gemv", 7, 1, "0", True, "p2p")])
+def test_ep_matches_single_gpu(path, T, chunks, regroup, shared, exchange, world):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < world:
@@ -67,7 +70,8 @@ def test_ep_matches_single_gpu(path, T, chunks, regroup, shared, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     Tmax = T + 13 * (world - 1)
-    procs = [ctx.Process(target=_rank, args=(r, world, uid, path, T + 13 * r, Tmax, chunks, regroup, shared, q), daemon=True)
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, path, T + 13 * r, Tmax, chunks, regroup, shared, q,
+                                             exchange), daemon=True)
              for r in range(world)]
     for p in procs:
         p.start()
