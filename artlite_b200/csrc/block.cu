@@ -96,6 +96,8 @@ namespace artlite {
 
 int wait_deadline(cudaStream_t st, int timeout_ms) { return wait(st, timeout_ms); }
 
+bool mss_use(const artlite_moe& h, const ExpertWeights& W, int path, int x_dtype, int F);
+
 int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L) {
   const artlite_moe_desc& d = h.d;
   const bool tc = tc_supported(L.qtype, d.hidden, d.expert_ffn) && tc_supported(L.down_qtype, d.expert_ffn, d.hidden);
@@ -104,6 +106,9 @@ int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L) {
   // the fused decode kernel where it applies (up to 512 pairs), else tcgen05 for prefill-sized batches (on average 4
   // pairs an expert or more) and the GEMVs for decode batches
   if (decode_fused_ok(h, L, P / d.top_k)) return 1;
+  // decode-sized batches of layers the fused kernel does not take (Q4_K gate / up with a Q6_K down) stay on the
+  // small-batch tensor-core GEMVs up to 64 tokens
+  if (P <= 64 * (int64_t)d.top_k && mss_use(h, routed_weights(L), 1, d.act_dtype, d.expert_ffn)) return 1;
   return P >= 4 * (int64_t)h.E_local ? 2 : 1;
 }
 
@@ -155,7 +160,8 @@ bool mss_use(const artlite_moe& h, const ExpertWeights& W, int path, int x_dtype
     const char* v = getenv("ARTLITE_DECODE_MSS");
     return v && v[0] == '0';
   }();
-  return !off && path == 1 && W.ss_gate && mss_ok(W.qtype, W.down_qtype, x_dtype, h.d.hidden, F, true);
+  return !off && path == 1 && W.ss_gate && (W.ss_down || W.down_qtype == ARTLITE_Q6_K) &&
+         mss_ok(W.qtype, W.down_qtype, x_dtype, h.d.hidden, F, true);
 }
 
 void small_plan(const artlite_moe& h, const artlite_moe::Layer& L, int path, int64_t T, int* mult_gu, int* mult_dn) {
@@ -192,6 +198,9 @@ int run_experts(artlite_moe* h, const ExpertWeights& L, int path, const void* x,
     s.gate_map = L.ss_gate;
     s.up_map = L.ss_up;
     s.down_map = L.ss_down;
+    s.down_qtype = L.down_qtype;
+    s.down_raw = L.down;
+    s.rb_dn = L.rb_dn;
     s.H = H;
     s.F = F;
     s.E = E_run;
@@ -442,8 +451,8 @@ int artlite_moe_set_weights(artlite_moe* h, int layer, int qtype, const void* ga
     AL_TRY(make_raw_map(&L.dm_down, L.down.ptr, L.rb_dn, h->E_local * H, 144, 128));
     L.has_dm = true;
   }
-  L.has_ss = false;
-  if (L.has_dm && F % 32 == 0) {
+  L.has_ss = false;  // (the small-batch GEMVs' gate / up maps: Q4_K gate / up, whatever the down type)
+  if (qtype == ARTLITE_Q4_K && F % 32 == 0 && H % 128 == 0) {
     AL_TRY(make_raw_map(&L.ss_gate, L.gate.ptr, L.rb_gu, h->E_local * F, 144, 32));
     AL_TRY(make_raw_map(&L.ss_up, L.up.ptr, L.rb_gu, h->E_local * F, 144, 32));
     L.has_ss = true;

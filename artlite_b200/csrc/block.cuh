@@ -130,9 +130,8 @@ struct ExpertWeights {
   const CUtensorMap *ss_gate, *ss_up, *ss_down;  // the small-batch GEMVs' maps (null: none)
 };
 inline ExpertWeights routed_weights(const artlite_moe::Layer& L) {
-  const bool ss = L.has_ss && L.has_dm;
   return {L.qtype, L.down_qtype, L.gate.as<uint8_t>(), L.up.as<uint8_t>(), L.down.as<uint8_t>(), L.rb_gu, L.rb_dn,
-          ss ? &L.ss_gate : nullptr, ss ? &L.ss_up : nullptr, ss ? &L.dm_down : nullptr};
+          L.has_ss ? &L.ss_gate : nullptr, L.has_ss ? &L.ss_up : nullptr, L.has_dm ? &L.dm_down : nullptr};
 }
 inline ExpertWeights shared_weights(const artlite_moe::Layer& L) {
   return {L.sh_qtype, L.sh_down_qtype, L.sh_gate.as<uint8_t>(), L.sh_up.as<uint8_t>(), L.sh_down.as<uint8_t>(),

@@ -151,8 +151,8 @@ int ep_timeout_ms() { return env_ms("ARTLITE_EP_TIMEOUT_MS", 30000); }
 //
 // A push copies up to kMaxPeers blocks of rows from this GPU's memory into other GPUs' buffers (CUDA IPC mappings,
 // reached over NVLink by plain 16-byte loads and stores: no TMA, no multicast), then raises each destination's flag to
-// the forward's epoch: every CTA fences its stores at system scope and counts itself done; the last one releases the
-// flags (st.release.sys). A wait (one warp, a lane per source) acquires the flags of every peer at system scope, up to
+// the forward's epoch: every thread fences its own stores at system scope, then its CTA counts itself done; the last
+// CTA releases the flags (st.release.sys). A wait (one warp, a lane per source) acquires the flags of every peer at system scope, up to
 // a deadline (about 2 s of the GPU's global timer), after which it reports ARTLITE_ETIMEOUT in the status word and
 // returns: no wait here is unbounded. The blocks of a push never overlap; a buffer is written only between two
 // count exchanges that both of its owner's consecutive forwards take part in, so no push can reach a buffer that its
@@ -172,12 +172,25 @@ __global__ void __launch_bounds__(512) ep_push_kernel(const PushArgs a) {
   const int64_t total = a.n16[a.nb];
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int b = 0;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-    while (i >= a.n16[b + 1]) b++;
-    const int64_t j = i - a.n16[b];
-    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.src[b]) + j);
-    reinterpret_cast<uint4*>(a.dst[b])[j] = v;
+  // four 16-byte units a thread in flight (their loads issued before the stores), in increasing unit order
+  for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += 4 * stride) {
+    uint4 v[4];
+    int bb[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int64_t i = i0 + u * stride;
+      bb[u] = -1;
+      if (i < total) {
+        while (i >= a.n16[b + 1]) b++;
+        bb[u] = b;
+        v[u] = __ldcg(reinterpret_cast<const uint4*>(a.src[b]) + (i - a.n16[b]));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (bb[u] >= 0) reinterpret_cast<uint4*>(a.dst[bb[u]])[i0 + u * stride - a.n16[bb[u]]] = v[u];
   }
+  __threadfence_system();  // (every thread: its own stores to the peers' memory are visible system-wide first)
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
@@ -609,7 +622,7 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
     pa.nb = nb;
     pa.epoch = epoch;
     pa.done = h->ep_done.as<int>();
-    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(acc, 512 * 4), 64));
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(acc, 512 * 4), 128));
     ep_push_kernel<<<grid, 512, 0, h->ep_st>>>(pa);
     AL_LAUNCHED();
   }
@@ -716,7 +729,7 @@ int ep_forward_impl(artlite_moe* h, int layer, const void* xd, void* yd, int64_t
     pa.nb = nb;
     pa.epoch = epoch;
     pa.done = h->ep_done.as<int>();
-    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(acc, 512 * 4), 64));
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(acc, 512 * 4), 128));
     ep_push_kernel<<<grid, 512, 0, h->ep_st>>>(pa);
     AL_LAUNCHED();
   }

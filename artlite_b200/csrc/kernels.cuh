@@ -149,7 +149,7 @@ int launch_gather(const void* x, int x_dtype, const int32_t* perm, int64_t P, in
 // The small-batch tensor-core GEMVs (Q4_K, bf16 x): gate / up items of 32 output rows into h (fragment order + group
 // sums: hq, hs), down items of 128 output rows into fp32 y, both over the dispatch's pair groups of <= 8.
 struct MssLaunch {
-  const CUtensorMap *gate_map, *up_map, *down_map;  // raw rows: gate / up boxes of 32 rows, down boxes of 128 rows
+  const CUtensorMap *gate_map, *up_map, *down_map;  // raw rows: gate / up boxes of 32 rows, down boxes of 128 rows (Q4_K)
   int H, F, E, k;
   const void* x;  // bf16 token rows; pair d's row is perm[d] / k
   uint4* hq;      // h of the pairs in fragment order (F / 32 groups a row), then
@@ -160,6 +160,9 @@ struct MssLaunch {
   const int32_t* perm;
   int slots;  // token slots to stage: min(8, the most pairs an expert can get)
   DevStatus* status;
+  int down_qtype;          // ARTLITE_Q4_K (down_map) or ARTLITE_Q6_K (down_raw: E H rows of rb_dn bytes)
+  const uint8_t* down_raw;
+  int64_t rb_dn;
 };
 bool mss_ok(int qtype, int down_qtype, int x_dtype, int H, int F, bool has_maps);
 int mss_mult_gu(int F);

@@ -14,6 +14,14 @@
 // columns, fp32 rows out. The next item's weights are requested as soon as every warp is done with the current ones.
 // Every wait is bounded: on expiry the CTA reports ARTLITE_ETIMEOUT, waits (bounded) for its copies in flight and
 // leaves.
+//
+// Q6_K downs (Q4_K_M files: Q4_K gate / up, Q6_K down; the reference's q6_k, dequant.cpp:83-101) take their own down
+// kernel. An item's 128 raw rows are one contiguous range (rows of 210 B a super-block need not be 16-byte pitched,
+// but 128 of them are 26,880 B a column, a multiple of 16), so one bulk copy brings the whole item. The gate / up kernel
+// then writes h in the natural k order of the mma (lane t of a 32-value group holding values 2t, 2t + 1, 2t + 8, 2t + 9
+// and the same + 16), so that each m16n8k16 step covers exactly one 16-value Q6_K scale group: the A values are
+// bf16(q - 32) (exact: (q | 0x4300) is 128 + q, minus 160 in bf16), and each step's sum is scaled once, d sc_j,
+// before it joins the row's fp32 sum.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -47,14 +55,18 @@ struct MssArgs {
   const int32_t* perm;
   int slots;           // token slots staged (min(8, the most pairs an expert can get))
   DevStatus* status;
+  int natural;         // gu: h in the mma's natural k order (for a Q6_K down), else the Q4_K tile's order
+  const uint8_t* raw;  // Q6_K down: the raw rows, rb bytes a row
+  int64_t rb;
 };
 
-// shared memory: weights | x slots | group sums | per-warp partial sums | h tile | scale tables | mbarrier
+// shared memory: weights | x slots | group sums | per-warp partial sums | h tile | scale tables | mbarrier | the item
+// scan and the dispatch offsets (E + 1 each: the items are found in shared memory, not by dependent L2 loads)
 struct Layout {
-  int w_bytes, x_stride, x_off, s_off, red_off, hb_off, tab_off, bar_off, total;
+  int w_bytes, x_stride, x_off, s_off, red_off, hb_off, tab_off, bar_off, off_off, uo_off, total;
 };
 
-__host__ __device__ inline Layout layout(bool gu, int SB, int slots) {
+__host__ __device__ inline Layout layout(bool gu, int SB, int slots, int E) {
   Layout l;
   l.w_bytes = gu ? 2 * SB * kGuRows * 144 : SB * kDnRows * 144;
   l.x_stride = SB * 512 + 16;  // (a slot's row, padded so that the 8 slots' fragment loads fall on distinct banks)
@@ -64,7 +76,9 @@ __host__ __device__ inline Layout layout(bool gu, int SB, int slots) {
   l.hb_off = l.red_off + 8 * 32 * 4 * 4;
   l.tab_off = l.hb_off + 8 * kGuRows * 4;
   l.bar_off = l.tab_off + 8 * 16 * ms::kTabRow * 8;
-  l.total = l.bar_off + 16;
+  l.off_off = l.bar_off + 16;
+  l.uo_off = l.off_off + 8 * (E + 1);
+  l.total = l.uo_off + 4 * (E + 1);
   return l;
 }
 
@@ -73,19 +87,21 @@ struct ItemS {
   int64_t d0;
 };
 
-__device__ __forceinline__ ItemS item_of(const MssArgs& a, int i, int rows_item) {
+// item i from the shared copies of the item scan (uo) and the dispatch offsets (offs)
+__device__ __forceinline__ ItemS item_of(const MssArgs& a, const int32_t* uo, const int64_t* offs, int i,
+                                         int rows_item) {
   int lo = 0, hi = a.E;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (a.uo[mid] <= i) lo = mid; else hi = mid;
+    if (uo[mid] <= i) lo = mid; else hi = mid;
   }
   const int ntile = a.N / rows_item;
-  const int li = i - a.uo[lo], tg = li / ntile;
+  const int li = i - uo[lo], tg = li / ntile;
   ItemS it;
   it.e = lo;
   it.rt = li - tg * ntile;
-  it.d0 = a.offsets[lo] + (int64_t)tg * kGemvTokens;
-  it.nt = (int)min64(kGemvTokens, a.offsets[lo + 1] - it.d0);
+  it.d0 = offs[lo] + (int64_t)tg * kGemvTokens;
+  it.nt = (int)min64(kGemvTokens, offs[lo + 1] - it.d0);
   return it;
 }
 
@@ -125,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 2) mss_kernel(const __grid_constant_
   griddep_launch();
   const int SB = a.K >> 8, G = a.K >> 5;
   const int slots = a.slots;
-  const Layout L = layout(GU, SB, slots);
+  const Layout L = layout(GU, SB, slots, a.E);
   uint8_t* w = sm;
   uint8_t* xs = sm + L.x_off;
   float* ss = reinterpret_cast<float*>(sm + L.s_off);
@@ -134,19 +150,25 @@ __global__ void __launch_bounds__(kThreads, 2) mss_kernel(const __grid_constant_
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L.bar_off);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float* tab = reinterpret_cast<float*>(sm + L.tab_off) + warp * 16 * ms::kTabRow * 2;
-  const int total = a.uo[a.E];
   const int rows_item = GU ? kGuRows : kDnRows;
   if ((ms::su32(sm) & 127u) != 0) {  // (TMA destinations: never issued to a misaligned buffer)
     if (threadIdx.x == 0) report(a.status, ARTLITE_EUNSUPPORTED, 128, 0, 0);
     return;
   }
+  int64_t* offs = reinterpret_cast<int64_t*>(sm + L.off_off);
+  int32_t* uo = reinterpret_cast<int32_t*>(sm + L.uo_off);
+  for (int e = threadIdx.x; e <= a.E; e += kThreads) {  // (one round of independent loads)
+    uo[e] = __ldcg(a.uo + e);
+    offs[e] = __ldcg(a.offsets + e);
+  }
   if (threadIdx.x == 0) ms::mbar_init(bar, 1);
   __syncthreads();
+  const int total = uo[a.E];
   int i = blockIdx.x;
   if (i >= total) return;
   unsigned parity = 0;
   bool pending = false;  // (thread 0: a request not yet waited for)
-  ItemS it = item_of(a, i, rows_item);
+  ItemS it = item_of(a, uo, offs, i, rows_item);
   if (threadIdx.x == 0) request<GU>(a, it, SB, w, bar), pending = true;
   for (; i < total; i += gridDim.x) {
     // x of the item's pairs, in fragment order with group sums (an item never has more pairs than the staged slots:
@@ -206,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 2) mss_kernel(const __grid_constant_
     const ItemS cur = it;
     const int nxt = i + gridDim.x;
     if (nxt < total) {
-      it = item_of(a, nxt, rows_item);
+      it = item_of(a, uo, offs, nxt, rows_item);
       if (threadIdx.x == 0) request<GU>(a, it, SB, w, bar), pending = true;
     }
     const int g = lane >> 2, t = lane & 3;
@@ -221,16 +243,32 @@ __global__ void __launch_bounds__(kThreads, 2) mss_kernel(const __grid_constant_
       __syncthreads();
       if (threadIdx.x < 32) {  // (token n, 8-row quarter tq): 8 h values in fragment order, and the group sum
         const int n = threadIdx.x >> 2, tq = threadIdx.x & 3;
-        const float4 h0 = *reinterpret_cast<const float4*>(hb + n * kGuRows + 8 * tq);
-        const float4 h1 = *reinterpret_cast<const float4*>(hb + n * kGuRows + 8 * tq + 4);
-        const float v[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        const float* hn = hb + n * kGuRows;
+        float v[8];
+        if (a.natural) {  // values 2 tq, 2 tq + 1, 2 tq + 8, 2 tq + 9, and the same + 16
+#pragma unroll
+          for (int j = 0; j < 4; j++) v[2 * j] = hn[2 * tq + 8 * j], v[2 * j + 1] = hn[2 * tq + 8 * j + 1];
+        } else {
+          const float4 h0 = *reinterpret_cast<const float4*>(hn + 8 * tq);
+          const float4 h1 = *reinterpret_cast<const float4*>(hn + 8 * tq + 4);
+          v[0] = h0.x, v[1] = h0.y, v[2] = h0.z, v[3] = h0.w, v[4] = h1.x, v[5] = h1.y, v[6] = h1.z, v[7] = h1.w;
+        }
         float part = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
         part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
         part += __shfl_xor_sync(0xFFFFFFFFu, part, 2);
         if (n < cur.nt && n < slots) {
           const int Go = a.N >> 5;
           const int64_t pr = cur.d0 + n;
-          a.hq_out[(pr * Go + cur.rt) * 4 + tq] = ms::arrange(v);
+          uint4 o;
+          if (a.natural) {  // (bf16 pairs in k order: the B registers of the group's two steps)
+            uint32_t b[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) b[j] = __float_as_uint(v[j]) >> 16;
+            o = make_uint4(b[0] | b[1] << 16, b[2] | b[3] << 16, b[4] | b[5] << 16, b[6] | b[7] << 16);
+          } else {
+            o = ms::arrange(v);
+          }
+          a.hq_out[(pr * Go + cur.rt) * 4 + tq] = o;
           if (tq == 0) a.hs_out[pr * Go + cur.rt] = part;
         }
       }
@@ -250,11 +288,160 @@ __global__ void __launch_bounds__(kThreads, 2) mss_kernel(const __grid_constant_
   if (threadIdx.x == 0 && pending && !ms::mbar_test(bar, parity)) ms::mbar_wait(bar, parity, a.status);
 }
 
+// ---------------------------------------------------------------- Q6_K downs
+
+// shared memory of the Q6_K down kernel: the item's raw rows (128 x rb, 16-byte aligned) | x slots | mbarrier | the
+// item scan and the dispatch offsets
+struct Layout6 {
+  int w_bytes, x_stride, x_off, bar_off, off_off, uo_off, total;
+};
+__host__ __device__ inline Layout6 layout6(int64_t rb, int SB, int slots, int E) {
+  Layout6 l;
+  l.w_bytes = (int)(kDnRows * rb);
+  l.x_stride = SB * 512 + 16;
+  l.x_off = (l.w_bytes + 127) & ~127;
+  l.bar_off = l.x_off + slots * l.x_stride;
+  l.off_off = l.bar_off + 16;
+  l.uo_off = l.off_off + 8 * (E + 1);
+  l.total = l.uo_off + 4 * (E + 1);
+  return l;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   ms::su32(dst)),
+               "l"(src), "r"(bytes), "r"(ms::su32(bar))
+               : "memory");
+}
+
+// the two bytes at p (2-byte aligned) spread into the low bytes of the two 16-bit halves
+__device__ __forceinline__ uint32_t spread2(const uint8_t* p) {
+  return __byte_perm((uint32_t)*reinterpret_cast<const uint16_t*>(p), 0u, 0x4140u);
+}
+
+// One warp's 16 rows (rows g and g + 8 of lane (g, t) at r0 / r1, rb bytes a row) x one super-block column c of
+// the staged x (natural k order): y (rows g, g + 8 x tokens 2t, 2t + 1) += sum over the 16 scale groups j of
+// d sc_j (sum_k (q_k - 32) x_k). Group j = 16-value half (j & 1) of 32-group j / 2 = (h, jj): 128 h + 32 jj + l
+// (dequant.cpp:83-101): q = (nibble jj / 2 of ql[64 h + 32 (jj & 1) + l] | crumb jj of qh[32 h + l] << 4).
+__device__ __forceinline__ void tile6_sb(const uint8_t* r0, const uint8_t* r1, const uint8_t* xs, int x_stride,
+                                         int slots, int c, int lane, float (&y)[4]) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* b0 = r0 + 210 * c;
+  const uint8_t* b1 = r1 + 210 * c;
+  const float d0 = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(b0 + 208)));
+  const float d1 = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(b1 + 208)));
+  const uint4* xr = reinterpret_cast<const uint4*>(xs + (g < slots ? g : 0) * x_stride) + c * 32 + t;
+  const __nv_bfloat162 m160 = __floats2bfloat162_rn(-160.0f, -160.0f);
+#pragma unroll
+  for (int grp = 0; grp < 8; grp++) {  // the 32-groups (h, jj) of the column
+    const int h = grp >> 2, jj = grp & 3;
+    const uint4 bx = xr[4 * grp];      // (this lane's x of the group: both steps)
+    const int qlo = 64 * h + 32 * (jj & 1) + 2 * t, qho = 128 + 32 * h + 2 * t;
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+      const int l = 16 * half;
+      uint32_t a[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) {  // (a0: row g, k 2t; a1: row g + 8, k 2t; a2: row g, k 2t + 8; a3: row g + 8)
+        const uint8_t* b = (r & 1) ? b1 : b0;
+        const int k8 = (r >> 1) * 8;
+        const uint32_t ql = spread2(b + qlo + l + k8), qh = spread2(b + qho + l + k8);
+        const uint32_t nib = (jj & 2) ? (ql >> 4) & 0x000F000Fu : ql & 0x000F000Fu;
+        const uint32_t v = (nib | (((qh >> (2 * jj)) & 0x00030003u) << 4)) | 0x43004300u;  // bf16 128 + q
+        __nv_bfloat162 w = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&v), m160);  // q - 32, exact
+        a[r] = *reinterpret_cast<const uint32_t*>(&w);
+      }
+      float acc[4] = {0, 0, 0, 0};
+      ms::mma_bf16(acc, a, half ? bx.z : bx.x, half ? bx.w : bx.y);
+      const int j = 2 * grp + half;  // (the scale index: 16-value group j of the super-block)
+      const float s0 = __fmul_rn(d0, (float)(int8_t)b0[192 + j]), s1 = __fmul_rn(d1, (float)(int8_t)b1[192 + j]);
+      y[0] = fmaf(s0, acc[0], y[0]);
+      y[1] = fmaf(s0, acc[1], y[1]);
+      y[2] = fmaf(s1, acc[2], y[2]);
+      y[3] = fmaf(s1, acc[3], y[3]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 2) mss_q6_down_kernel(const __grid_constant__ MssArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  griddep_wait();
+  griddep_launch();
+  const int SB = a.K >> 8, G = a.K >> 5;
+  const int slots = a.slots;
+  const Layout6 L = layout6(a.rb, SB, slots, a.E);
+  uint8_t* w = sm;
+  uint8_t* xs = sm + L.x_off;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L.bar_off);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if ((ms::su32(sm) & 127u) != 0) {  // (bulk-copy destinations: never issued to a misaligned buffer)
+    if (threadIdx.x == 0) report(a.status, ARTLITE_EUNSUPPORTED, 128, 0, 0);
+    return;
+  }
+  int64_t* offs = reinterpret_cast<int64_t*>(sm + L.off_off);
+  int32_t* uo = reinterpret_cast<int32_t*>(sm + L.uo_off);
+  for (int e = threadIdx.x; e <= a.E; e += kThreads) {
+    uo[e] = __ldcg(a.uo + e);
+    offs[e] = __ldcg(a.offsets + e);
+  }
+  if (threadIdx.x == 0) ms::mbar_init(bar, 1);
+  __syncthreads();
+  const int total = uo[a.E];
+  const uint32_t item_bytes = (uint32_t)(kDnRows * a.rb);
+  int i = blockIdx.x;
+  if (i >= total) return;
+  unsigned parity = 0;
+  bool pending = false;
+  auto request = [&](const ItemS& it) {  // (one thread) the item's 128 rows: one contiguous range
+    ms::mbar_expect(bar, item_bytes);
+    bulk_load(w, a.raw + ((int64_t)it.e * a.N + (int64_t)it.rt * kDnRows) * a.rb, item_bytes, bar);
+  };
+  ItemS it = item_of(a, uo, offs, i, kDnRows);
+  if (threadIdx.x == 0) request(it), pending = true;
+  for (; i < total; i += gridDim.x) {
+    if (it.nt > slots && threadIdx.x == 0) report(a.status, ARTLITE_EDEVICE, it.nt, slots, 3);
+    const int ns = it.nt < slots ? it.nt : slots;
+    for (int u = threadIdx.x; u < ns * G * 4; u += kThreads) {
+      const int n = u / (G * 4), r = u - n * G * 4;
+      reinterpret_cast<uint4*>(xs + n * L.x_stride)[r] = __ldcg(a.hq + (it.d0 + n) * G * 4 + r);
+    }
+    __syncthreads();
+    const bool ok = __syncthreads_and(ms::mbar_wait(bar, parity, a.status));
+    if (!ok) break;
+    parity ^= 1u;
+    if (threadIdx.x == 0) pending = false;
+    float y[4] = {0, 0, 0, 0};
+    const int g = lane >> 2, t = lane & 3;
+    const uint8_t* r0 = w + (warp * 16 + g) * a.rb;
+    const uint8_t* r1 = r0 + 8 * a.rb;
+    for (int c = 0; c < SB; c++) tile6_sb(r0, r1, xs, L.x_stride, slots, c, lane, y);
+    __syncthreads();  // (every warp is done with the weights and x of this item)
+    const ItemS cur = it;
+    const int nxt = i + gridDim.x;
+    if (nxt < total) {
+      it = item_of(a, uo, offs, nxt, kDnRows);
+      if (threadIdx.x == 0) request(it), pending = true;
+    }
+    const int64_t row = (int64_t)cur.rt * kDnRows + warp * 16 + g;
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const int n = 2 * t + q;
+      if (n < cur.nt && n < slots) {
+        a.y[(cur.d0 + n) * a.N + row] = y[q];
+        a.y[(cur.d0 + n) * a.N + row + 8] = y[2 + q];
+      }
+    }
+    __syncthreads();  // (the x slots are free again)
+  }
+  if (threadIdx.x == 0 && pending && !ms::mbar_test(bar, parity)) ms::mbar_wait(bar, parity, a.status);
+}
+
 }  // namespace
 
 bool mss_ok(int qtype, int down_qtype, int x_dtype, int H, int F, bool has_maps) {
-  return has_maps && qtype == ARTLITE_Q4_K && down_qtype == ARTLITE_Q4_K && x_dtype == ARTLITE_BF16 && H % 512 == 0 &&
-         H / 256 <= kMaxSB && F % 256 == 0 && F / 256 <= kMaxSBd && F % kGuRows == 0 && H % kDnRows == 0;
+  return has_maps && qtype == ARTLITE_Q4_K && (down_qtype == ARTLITE_Q4_K || down_qtype == ARTLITE_Q6_K) &&
+         x_dtype == ARTLITE_BF16 && H % 512 == 0 && H / 256 <= kMaxSB && F % 256 == 0 && F / 256 <= kMaxSBd &&
+         F % kGuRows == 0 && H % kDnRows == 0;
 }
 int mss_mult_gu(int F) { return F / kGuRows; }
 int mss_mult_dn(int H) { return H / kDnRows; }
@@ -265,8 +452,10 @@ int launch_mss(const MssLaunch& s, bool gu, cudaStream_t st) {
   AL_CUDA(cudaGetDevice(&dev));
   AL_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   MssArgs a{};
-  a.m0 = gu ? *s.gate_map : *s.down_map;
-  if (gu) a.m1 = *s.up_map;
+  AL_CHECK(gu ? s.gate_map && s.up_map : s.down_map || s.down_qtype == ARTLITE_Q6_K, ARTLITE_EINVAL,
+           "small gemv: no tensor map for the %s rows", gu ? "gate / up" : "down");
+  if (gu) a.m0 = *s.gate_map, a.m1 = *s.up_map;
+  else if (s.down_map) a.m0 = *s.down_map;  // (a Q6_K down has none: its rows are bulk-copied)
   a.K = gu ? s.H : s.F;
   a.N = gu ? s.F : s.H;
   a.E = s.E;
@@ -282,7 +471,21 @@ int launch_mss(const MssLaunch& s, bool gu, cudaStream_t st) {
   a.perm = s.perm;
   a.slots = s.slots;
   a.status = s.status;
-  const Layout l = layout(gu, a.K >> 8, s.slots);
+  a.natural = s.down_qtype == ARTLITE_Q6_K;
+  if (!gu && s.down_qtype == ARTLITE_Q6_K) {  // (the Q6_K down kernel: whole items by one bulk copy)
+    a.raw = s.down_raw;
+    a.rb = s.rb_dn;
+    AL_CHECK(a.rb == (int64_t)(a.K / 256) * 210 && ((uintptr_t)a.raw % 16) == 0, ARTLITE_EINVAL,
+             "small gemv: Q6_K rows of %lld bytes", (long long)a.rb);
+    const Layout6 l6 = layout6(a.rb, a.K >> 8, s.slots, s.E);
+    const size_t smem6 = (size_t)l6.total;
+    AL_CUDA(cudaFuncSetAttribute(mss_q6_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem6));
+    int per_sm6 = 0;
+    AL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm6, mss_q6_down_kernel, kThreads, smem6));
+    AL_CHECK(per_sm6 >= 1, ARTLITE_EUNSUPPORTED, "small gemv: %zu B of shared memory", smem6);
+    return launch_pdl(mss_q6_down_kernel, dim3((unsigned)(per_sm6 * sms)), dim3(kThreads), smem6, st, a);
+  }
+  const Layout l = layout(gu, a.K >> 8, s.slots, s.E);
   const size_t smem = (size_t)l.total;
   auto kern = gu ? mss_kernel<true> : mss_kernel<false>;
   AL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

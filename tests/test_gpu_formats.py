@@ -56,9 +56,24 @@ def test_q4_k_m_prefill_shape(down):
     assert moe_np.rel_max(ref[tok], want) <= 1e-4
 
 
-@pytest.mark.parametrize("down,T", [("Q6_K", 16), ("Q6_K", 300), ("Q5_K", 16), ("Q5_K", 5)])
+@pytest.mark.parametrize("down,T", [("Q6_K", 16), ("Q6_K", 300), ("Q5_K", 16), ("Q5_K", 5), ("Q6_K", 1), ("Q6_K", 4),
+                                    ("Q6_K", 64)])
 def test_mixed_down_decode_and_prefill(down, T):
     """Q4_K gate / up with a Q6_K or Q5_K down through the block's automatic path choice, decode and prefill sizes."""
     layer, x, _ = moe_np.make_block(92 + T, T, qtype="Q4_K", down_qtype=down, E=32, H=1024, F=512)
     y, ids, w, _ = run_checked(layer, x, T, "auto")
     assert moe_np.rel_max(y, oracle_y(layer, x, ids, w)) <= BF16_TOL
+
+
+@pytest.mark.parametrize("T", [1, 16, 64])
+def test_q4_k_m_decode_shape(T):
+    """A Q4_K_M-style layer (Q4_K gate / up, Q6_K down) at the benchmark's decode shape (H=2048, E=128, K=8, F=768) on
+    the small-batch tensor-core GEMVs (the Q6_K down kernel: whole items by one bulk copy, h in the mma's natural k
+    order), every token against the torch fp32 reference, which is pinned to the NumPy oracle on a stride."""
+    layer, x, _ = moe_np.make_block(93 + T, T, qtype="Q4_K", down_qtype="Q6_K")
+    y, ids, w, took = run_checked(layer, x, T, "auto")
+    assert took == "gemv"
+    ref = torch_moe_ffn(layer, x, ids, w)
+    assert moe_np.rel_max(y, ref) <= BF16_TOL
+    tok = np.arange(0, T, max(1, T // 4))
+    assert moe_np.rel_max(ref[tok], oracle_y(layer, x, ids, w, tokens=tok)) <= 1e-4
