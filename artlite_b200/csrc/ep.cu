@@ -361,7 +361,8 @@ int ep_allgather_host(artlite_moe* h, Nccl* N, ncclComm_t comm, const void* mine
 
 // The peer-store exchange's set-up (every rank takes part): the CUDA IPC handles of each rank's receive buffer, return
 // buffer and flags go to every rank, which maps its peers' (NVLink peer access); it is used only if every rank wants
-// it (ARTLITE_EP_EXCHANGE=nccl keeps NCCL send / recv; so do expert chunks) and every rank mapped every peer.
+// it (by default at two ranks; ARTLITE_EP_EXCHANGE=p2p or nccl forces either way; expert chunks keep NCCL) and every
+// rank mapped every peer.
 int ep_p2p_setup(artlite_moe* h, Nccl* N, ncclComm_t comm) {
   const int W = h->d.ep_world, r = h->d.ep_rank;
   const char* v = getenv("ARTLITE_EP_EXCHANGE");
@@ -374,7 +375,9 @@ int ep_p2p_setup(artlite_moe* h, Nccl* N, ncclComm_t comm) {
   memset(&m, 0, sizeof m);
   m.xr_bytes = (int64_t)h->xr.bytes;
   m.ys_bytes = (int64_t)h->ys.bytes;
-  m.ok = !(v && !strcmp(v, "nccl")) && h->ep_chunks == 1 && W <= kMaxPeers &&
+  // (the default: the peer stores at two ranks, where they measured faster; NCCL from four, where they did not)
+  const bool want = v && !strcmp(v, "p2p") ? true : v && !strcmp(v, "nccl") ? false : W == 2;
+  m.ok = want && h->ep_chunks == 1 && W <= kMaxPeers &&
          cudaIpcGetMemHandle(&m.hx, h->xr.ptr) == cudaSuccess && cudaIpcGetMemHandle(&m.hy, h->ys.ptr) == cudaSuccess &&
          cudaIpcGetMemHandle(&m.hf, h->ep_flags.ptr) == cudaSuccess;
   cudaGetLastError();  // (a refusal above is an answer, not an error)

@@ -344,15 +344,19 @@ def run_config(args) -> None:
 # the reference's own MoE model's decode shape (Qwen3.6-35B-A3B, qwen35moe: 256 experts, top-8, FFN 512, a gated
 # shared expert of FFN 512; tests/moe/ref.py:43-60)
 QWEN35 = {"name": "qwen35moe", "H": 2048, "E": 256, "K": 8, "F": 512, "Fs": 512}
+# the Q4_K_M layout of the reference's MoE files (Q4_K gate / up, Q6_K downs: tests/moe/test_prefill.py:1-5) at the
+# benchmark's decode shape
+Q4KM = {"name": "decode-q4_k_m", "H": 2048, "E": 128, "K": 8, "F": 768, "Fs": 0, "down": "Q6_K"}
 
 
 def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "auto", shape: dict | None = None) -> list[dict]:
     """benchmark config 2 on one GPU: decode batches B = 1, 4, 16, 64 of the Q4_K block (bf16 x), each forward a CUDA
     graph, over `layers` layers in turn (their touched experts far exceed L2). One dict per B: tokens/s, and the
     HBM roofline of the bytes a forward must read (U touched experts x 2,654,208 B + the fp32 router 1,048,576 B).
-    `shape` (H, E, K, F and a shared expert's Fs) measures another block shape the same way (the shared expert's rows
-    and its gate vector are part of every forward's bytes). The block's device status word is read after the timed
-    steps (raises on a kernel-reported error)."""
+    `shape` (H, E, K, F and a shared expert's Fs; "down": "Q6_K" for the Q4_K_M layout, Q4_K gate / up with Q6_K downs)
+    measures another block shape the same way (the shared expert's rows and its gate vector are part of every
+    forward's bytes). The block's device status word is read after the timed steps (raises on a kernel-reported
+    error)."""
     import torch
     from artlite_b200.moe.block import MoEBlock
     dev = torch.device("cuda", 0)
@@ -360,6 +364,7 @@ def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "a
     L = layers
     sh = shape or {"name": "decode-q4_k", "H": H, "E": E, "K": K, "F": F, "Fs": 0}
     h_, e_, k_, f_, fs = sh["H"], sh["E"], sh["K"], sh["F"], sh["Fs"]
+    dq = sh.get("down", "Q4_K")
     block = MoEBlock(hidden=h_, n_experts=e_, top_k=k_, expert_ffn=f_, max_tokens=max(batches), n_layers=L,
                      act_dtype="bf16", device=0, path=path)
     g = torch.Generator(device=dev)
@@ -373,11 +378,21 @@ def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "a
             raw[..., o:o + 2] = d.view(torch.uint8).view(rows, n, 2)
         return raw.view(rows, n * 144)
 
+    def q6k(rows, cols):  # (210-byte super-blocks: 192 bytes of uniform codes, int8 scales -32..31, d |N(0, 0.002)|)
+        n = cols // 256
+        raw = torch.randint(0, 256, (rows, n, 210), dtype=torch.uint8, generator=g, device=dev)
+        sc = torch.randint(-32, 32, (rows, n, 16), dtype=torch.int16, generator=g, device=dev)
+        raw[..., 192:208] = sc.to(torch.int8).view(torch.uint8)
+        d = (torch.randn((rows, n), generator=g, device=dev) * 0.002).abs().half()
+        raw[..., 208:210] = d.view(torch.uint8).view(rows, n, 2)
+        return raw.view(rows, n * 210)
+
     for layer in range(L):
-        gate, up, down = q4k(e_ * f_, h_), q4k(e_ * f_, h_), q4k(e_ * h_, f_)
+        gate, up = q4k(e_ * f_, h_), q4k(e_ * f_, h_)
+        down = q6k(e_ * h_, f_) if dq == "Q6_K" else q4k(e_ * h_, f_)
         router = torch.randn((e_, h_), generator=g, device=dev) * 0.02
         block.set_weights(layer, gate=gate.data_ptr(), up=up.data_ptr(), down=down.data_ptr(),
-                          router=router.data_ptr(), qtype="Q4_K")
+                          router=router.data_ptr(), qtype="Q4_K", down_qtype=dq)
         if fs:
             sg, su, sd = q4k(fs, h_), q4k(fs, h_), q4k(h_, fs)
             ginp = torch.randn((h_,), generator=g, device=dev) * 0.02
@@ -416,7 +431,7 @@ def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "a
         block.sync()  # (the device status word: raises if a kernel reported an error)
         ms_layer = e0.elapsed_time(e1) / (steps * L)
         U = float(np.mean(touched))
-        per_expert = 3 * f_ * h_ * 144 // 256  # (Q4_K: 144 bytes per 256 values)
+        per_expert = 2 * f_ * h_ * 144 // 256 + f_ * h_ * (210 if dq == "Q6_K" else 144) // 256  # (bytes per 256)
         nbytes = U * per_expert + e_ * h_ * 4 + (3 * fs * h_ * 144 // 256 + h_ * 4 if fs else 0)
         gbs = nbytes / (ms_layer / 1000.0) / 1e9
         out.append({"workload": f"{sh['name']}-b{B}", "batch": B, "us_per_layer": ms_layer * 1000.0,
@@ -433,7 +448,7 @@ def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "a
 
 def run_decode(args) -> None:
     for line in measure_decode(args.batches, args.layers, args.steps, args.warmup, args.path,
-                               QWEN35 if args.qwen35 else None):
+                               QWEN35 if args.qwen35 else Q4KM if args.q4_k_m else None):
         print(json.dumps(line), flush=True)
 
 
@@ -451,6 +466,7 @@ def main() -> None:
     ap.add_argument("--no-extras", action="store_true", help="skip the decode sweep and config 3 of the default line")
     ap.add_argument("--decode", action="store_true", help="benchmark config 2 (decode batches, Q4_K) instead")
     ap.add_argument("--qwen35", action="store_true", help="with --decode: the qwen35moe shape (E 256, F 512, shared)")
+    ap.add_argument("--q4-k-m", action="store_true", help="with --decode: Q4_K gate / up with Q6_K downs")
     ap.add_argument("--config", type=int, choices=[3, 5], help="benchmark config 3 or 5 (one GPU) instead")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"], help="expert path of --decode")
     ap.add_argument("--batches", type=int, nargs="+", default=[1, 4, 16, 64], help="decode batches of --decode")
@@ -605,6 +621,10 @@ def main() -> None:
             f"B{d['batch']}": {k: d[k] for k in ("us_per_layer", "tokens_per_s", "experts_touched", "roofline", "path",
                                                  "layers", "steps", "clocks")}
             for d in measure_decode([1, 16, 64], 8, 20, 3, shape=QWEN35)}
+        extras["q4_k_m_decode"] = {
+            f"B{d['batch']}": {k: d[k] for k in ("us_per_layer", "tokens_per_s", "experts_touched", "roofline", "path",
+                                                 "layers", "steps", "clocks")}
+            for d in measure_decode([1, 16, 64], 8, 20, 3, shape=Q4KM)}
         c3 = measure_config(3, 4, 10, 3)[0]
         extras["config3"] = {k: c3.get(k) for k in ("workload", "ms_per_layer", "tokens_per_s", "path", "roofline",
                                                     "layer_roofline", "stage_ms_mean", "layers", "steps", "clocks")}
