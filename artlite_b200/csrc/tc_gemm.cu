@@ -42,13 +42,19 @@ constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at the B200's clocks
 
 __host__ __device__ constexpr int chunk_bytes(int qt) {  // raw bytes of 256 values of a row
   return qt == ARTLITE_Q8_0 ? 272 : (qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_K) ? 144 : qt == ARTLITE_Q5_K ? 176
-       : qt == ARTLITE_Q6_K ? 210 : 0;
+       : qt == ARTLITE_Q6_K ? 210 : qt == ARTLITE_Q3_K ? 110 : 0;
 }
 // a raw stage row in shared memory: the chunk's bytes (TMA formats), or for Q6_K (whose rows need not be 16-byte
 // pitched, so no tensor map can describe them) the 16-byte-aligned 224-byte window around the 210-byte super-block,
 // copied by the copy warp, in rows 240 bytes apart (16-byte loads of 8 consecutive rows fall in distinct banks)
-__host__ __device__ constexpr int raw_pitch(int qt) { return qt == ARTLITE_Q6_K ? 240 : chunk_bytes(qt);
+__host__ __device__ constexpr int raw_pitch(int qt) {
+  return qt == ARTLITE_Q6_K ? 240 : qt == ARTLITE_Q3_K ? 144 : chunk_bytes(qt);
 }
+// the formats whose rows the copy warp brings (Q6_K, 210 B, and Q3_K, 110 B, a super-block: rows need not be 16-byte
+// pitched), and the 16-byte copies of a row's window (the block plus the up to 14 bytes before it from the 16-byte
+// boundary at or below its start: Q6_K 224 bytes, Q3_K 128)
+__host__ __device__ constexpr bool windowed(int qt) { return qt == ARTLITE_Q6_K || qt == ARTLITE_Q3_K; }
+__host__ __device__ constexpr int window_chunks(int qt) { return qt == ARTLITE_Q6_K ? 14 : qt == ARTLITE_Q3_K ? 8 : 0; }
 
 // raw weight stages: three of 18 KB for the 144-byte formats, two of 34 KB for Q8_0 (shared memory)
 __host__ __device__ constexpr int raw_stages(int qt) { return qt == ARTLITE_Q8_0 || qt == ARTLITE_Q6_K ? 2 : 3; }
@@ -58,6 +64,7 @@ struct Params {
   const uint8_t* gw0;  // the raw rows in global memory (gate / down; up), for the Q6_K copy warp
   const uint8_t* gw1;
   int64_t rb;          // their row bytes
+  int cb;              // raw bytes of 256 values (a super-block)
   const int64_t* offsets;
   const int32_t* wexp;  // (may be null) the weight expert of each row group
   const int32_t* toff;  // [E + 1] tiles per expert (ceil(n_e / 256) * MT), scanned
@@ -205,7 +212,7 @@ __device__ __forceinline__ uintptr_t raw_src(const Params& p, const Tile& T, int
     base = p.gw0;
     r = (int64_t)T.we * p.N + BM * m + row;
   }
-  return reinterpret_cast<uintptr_t>(base + r * p.rb + (int64_t)kc * 210);
+  return reinterpret_cast<uintptr_t>(base + r * p.rb + (int64_t)kc * p.cb);
 }
 
 // ---------------------------------------------------------------- dequant of one 64-value step into bf16 pairs
@@ -377,6 +384,37 @@ __device__ __forceinline__ void dq_q6_k_block(const uint8_t* win, int off, int s
   }
 }
 
+// Q3_K values 64 sub + 32 H .. + 31 of the super-block that starts at byte off of the window win (the reference's
+// q3_k, dequant.cpp:103-117): 32-group g = 2 sub + H = (n, j) = (g / 4, g % 4); its value i: q = crumb j of
+// qs[32 n + i] | bit (4 n + j) of hmask[i] << 2, times a = d (scale - 32) of its 16-value sub-block 2 g + i / 16 (the
+// 6-bit scale: low nibble of byte s, s < 8, or the high nibble of byte s - 8, top crumb from byte 8 + s % 4 at bit
+// 2 (s / 4)), as (q - 4) a (fp32, each rounded once: exact)
+template <int H>
+__device__ __forceinline__ void dq_q3_k_block(const uint8_t* win, int off, int sub, uint32_t (&o)[16]) {
+  const int g = 2 * sub + H, n = g >> 2, j = g & 3;
+  const float d = __half2float(__ushort_as_half((unsigned short)(q6_word(win, off + 108) & 0xFFFFu)));
+  float a[2];
+#pragma unroll
+  for (int u = 0; u < 2; u++) {
+    const int sb = 2 * g + u;
+    const int lo = sb < 8 ? win[off + 96 + sb] & 15 : win[off + 96 + sb - 8] >> 4;
+    const int top = (win[off + 104 + (sb & 3)] >> (2 * (sb >> 2))) & 3;
+    a[u] = __fmul_rn(d, (float)((lo | top << 4) - 32));
+  }
+  const uint64_t s0 = dup2(a[0]), s1 = dup2(a[1]);
+  const uint64_t bias = dup2(-8388612.0f);  // -(2^23 + 4)
+#pragma unroll
+  for (int k = 0; k < 8; k++) {  // values 4k .. 4k + 3
+    const uint32_t qs = q6_word(win, off + 32 + 32 * n + 4 * k), hm = q6_word(win, off + 4 * k);
+    const uint32_t v = ((qs >> (2 * j)) & 0x03030303u) | (((hm >> (4 * n + j)) & 0x01010101u) << 2);
+    uint64_t p0, p1;
+    magic4(v, p0, p1);
+    const uint64_t sc = k < 4 ? s0 : s1;
+    o[2 * k] = bf16x2(mul2(add2(p0, bias), sc));
+    o[2 * k + 1] = bf16x2(mul2(add2(p1, bias), sc));
+  }
+}
+
 // the 16-byte chunks [lo, hi] of a row's stage bytes that block / group 2 sub + h of a 256-value chunk reads
 template <int QT, int H>
 struct BlockSpan {
@@ -528,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
       mbar_init(&sm->empty[i], 1);
     }
     for (int i = 0; i < R; i++) {
-      mbar_init(&sm->raw_full[i], QT == ARTLITE_Q6_K ? 32 : 1);  // (Q6_K: the copy warp's lanes; else the TMA)
+      mbar_init(&sm->raw_full[i], windowed(QT) ? 32 : 1);  // (Q6_K / Q3_K: the copy warp's lanes; else the TMA)
       mbar_init(&sm->raw_empty[i], 256);
     }
     for (int i = 0; i < 2; i++) {
@@ -575,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
         if (++s == SS) s = 0, sph ^= 1;
       }
     }
-  } else if (warp == 0 && lane == 1 && QT != ARTLITE_Q6_K) {
+  } else if (warp == 0 && lane == 1 && !windowed(QT)) {
     // ---------------- producer of the raw weight rows (R stages of 256 values, ahead of the B stages)
     int r = 0, rph = 0;
     for (int t = t0; t < total; t += tstep) {
@@ -645,8 +683,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
       for (int kc = 0; kc < p.K / KC; kc++) {
         if (!wait(&sm->abort, &sm->raw_full[r], rph, p.status, 6)) goto out;
         const uint4* src = reinterpret_cast<const uint4*>(sR + r * BM * RPITCH + raw_row * RPITCH);
-        int q6off = 0;  // (Q6_K: where the row's super-block starts in its window)
-        if constexpr (QT == ARTLITE_Q6_K) q6off = (int)(raw_src<GU>(p, tile_of(p, t), NPEER, crank, raw_row, kc) & 15);
+        int q6off = 0;  // (Q6_K / Q3_K: where the row's super-block starts in its window)
+        if constexpr (windowed(QT)) q6off = (int)(raw_src<GU>(p, tile_of(p, t), NPEER, crank, raw_row, kc) & 15);
 #pragma unroll
         for (int sub = 0; sub < KC / BK; sub++) {
           const int step = n + sub, s = step % SS;
@@ -657,6 +695,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
           if constexpr (QT == ARTLITE_Q6_K) {
             if (h == 0) dq_q6_k_block<0>(reinterpret_cast<const uint8_t*>(src), q6off, sub, o);
             else dq_q6_k_block<1>(reinterpret_cast<const uint8_t*>(src), q6off, sub, o);
+          } else if constexpr (QT == ARTLITE_Q3_K) {
+            if (h == 0) dq_q3_k_block<0>(reinterpret_cast<const uint8_t*>(src), q6off, sub, o);
+            else dq_q3_k_block<1>(reinterpret_cast<const uint8_t*>(src), q6off, sub, o);
           } else {
             if (h == 0) dequant_block<QT, 0>(src, w, sub, o);
             else dequant_block<QT, 1>(src, w, sub, o);
@@ -678,10 +719,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
       }
     }
   } else if (warp == 14) {
-    // ---------------- Q6_K: the copy warp. Each lane copies four rows' windows (the 224 bytes from the 16-byte boundary
-    // at or below the row's 210-byte super-block) with 16-byte cp.async, then arrives on the stage's full barrier when
-    // its copies have landed
-    if constexpr (QT == ARTLITE_Q6_K) {
+    // ---------------- Q6_K / Q3_K: the copy warp. Each lane copies four rows' windows (from the 16-byte boundary at or
+    // below the row's super-block: 224 bytes for Q6_K, 128 for Q3_K) with 16-byte cp.async, then arrives on the stage's
+    // full barrier when its copies have landed
+    if constexpr (windowed(QT)) {
       int r = 0, rph = 0;
       for (int t = t0; t < total; t += tstep) {
         const Tile T = tile_of(p, t);
@@ -694,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
             const uintptr_t g = raw_src<GU>(p, T, NPEER, crank, row, kc) & ~(uintptr_t)15;
             const uint32_t d0 = smem_u32(dst + row * RPITCH);
 #pragma unroll
-            for (int c = 0; c < 14; c++)
+            for (int c = 0; c < window_chunks(QT); c++)
               asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d0 + 16 * c), "l"(g + 16 * c) : "memory");
           }
           asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sm->raw_full[r])) : "memory");
@@ -1023,7 +1064,7 @@ bool tc_use_pair(int N, bool gu) {
 int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
   AL_CHECK(tc_supported(a.qtype, a.K, a.N), ARTLITE_EUNSUPPORTED, "tc gemm: type %d K %d N %d", a.qtype, a.K, a.N);
   // (Q6_K rows need not be 16-byte pitched: the copy warp reads 16-byte-aligned windows; the TMA formats' rows must be)
-  AL_CHECK((a.qtype == ARTLITE_Q6_K || a.row_bytes % 16 == 0) &&
+  AL_CHECK((tc::windowed(a.qtype) || a.row_bytes % 16 == 0) &&
                a.row_bytes == (int64_t)a.K / tc::KC * tc::chunk_bytes(a.qtype), ARTLITE_EINVAL,
            "tc gemm: row bytes %lld", (long long)a.row_bytes);
   AL_CHECK(((uintptr_t)a.w0 % 16) == 0 && (!gu || ((uintptr_t)a.w1 % 16) == 0) && ((uintptr_t)a.x % 16) == 0,
@@ -1036,7 +1077,7 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
   tc::Params p{};
   const int cb = tc::chunk_bytes(a.qtype);
   const int64_t wrows = (int64_t)(a.wE > 0 ? a.wE : a.E) * a.N;
-  if (a.qtype != ARTLITE_Q6_K) {
+  if (!tc::windowed(a.qtype)) {
     AL_TRY(make_map(&p.map_w0, a.w0, a.row_bytes / 2, wrows, cb / 2, gu ? 64 : tc::BM, false));
     if (gu) AL_TRY(make_map(&p.map_w1, a.w1, a.row_bytes / 2, wrows, cb / 2, 64, false));
     else p.map_w1 = p.map_w0;
@@ -1044,6 +1085,7 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
   p.gw0 = static_cast<const uint8_t*>(a.w0);
   p.gw1 = static_cast<const uint8_t*>(gu ? a.w1 : a.w0);
   p.rb = a.row_bytes;
+  p.cb = cb;
   AL_TRY(make_map(&p.map_x, a.x, a.K, a.x_rows, tc::BK, pair ? tc::BNMAX / 2 : tc::BNMAX, true));
   AL_TRY(launch_unit_scan(a.counts, a.E, tc::BNMAX, MT, static_cast<int32_t*>(a.sched), st));
   p.offsets = a.offsets;
@@ -1091,6 +1133,7 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
     AL_TC_CASE(ARTLITE_Q4_K)
     AL_TC_CASE(ARTLITE_Q5_K)
     AL_TC_CASE(ARTLITE_Q6_K)
+    AL_TC_CASE(ARTLITE_Q3_K)
     default: break;
   }
 #undef AL_TC_CASE

@@ -30,10 +30,12 @@ def run_checked(layer, x, T, path, k=8):
 
 
 @pytest.mark.parametrize("qtype,down", [("Q5_K", "Q5_K"), ("Q4_K", "Q5_K"), ("Q5_K", "Q4_K"), ("Q4_0", "Q5_K"),
-                                        ("Q8_0", "Q5_K"), ("Q6_K", "Q6_K"), ("Q4_K", "Q6_K"), ("Q8_0", "Q6_K")])
+                                        ("Q8_0", "Q5_K"), ("Q6_K", "Q6_K"), ("Q4_K", "Q6_K"), ("Q8_0", "Q6_K"),
+                                        ("Q3_K", "Q3_K"), ("Q4_K", "Q3_K"), ("Q3_K", "Q6_K")])
 def test_tcgen05_q5_k_q6_k_and_mixed(qtype, down):
-    """Q5_K and Q6_K on the tensor cores, alone and mixed with the other formats (E=16, H=512, F=256, T=200: ragged
-    groups; Q6_K rows of 420 and 210 bytes, not 16-byte pitched, through the copy warp)."""
+    """Q5_K, Q6_K and Q3_K on the tensor cores, alone and mixed with the other formats (E=16, H=512, F=256, T=200:
+    ragged groups; Q6_K rows of 420 and 210 bytes and Q3_K rows of 220 and 110 bytes, not 16-byte pitched, through the
+    copy warp)."""
     layer, x, _ = moe_np.make_block(90, 200, qtype=qtype, down_qtype=down, E=16, H=512, F=256)
     y, ids, w, took = run_checked(layer, x, 200, "tc")
     assert took == "tc"
@@ -76,4 +78,18 @@ def test_q4_k_m_decode_shape(T):
     ref = torch_moe_ffn(layer, x, ids, w)
     assert moe_np.rel_max(y, ref) <= BF16_TOL
     tok = np.arange(0, T, max(1, T // 4))
+    assert moe_np.rel_max(ref[tok], oracle_y(layer, x, ids, w, tokens=tok)) <= 1e-4
+
+
+def test_q3_k_prefill_shape():
+    """Q3_K experts (the reference's low-bit MoE files: dequant.cpp:103-117) at a prefill size of the benchmark's shape
+    (T=2048, H=2048, E=128, K=8, F=768) on the tensor cores, every token against the torch fp32 reference, which is
+    pinned to the NumPy oracle on a stride."""
+    T = 2048
+    layer, x, _ = moe_np.make_block(95, T, qtype="Q3_K")
+    y, ids, w, took = run_checked(layer, x, T, "auto")
+    assert took == "tc"
+    ref = torch_moe_ffn(layer, x, ids, w)
+    assert moe_np.rel_max(y, ref) <= BF16_TOL
+    tok = np.arange(0, T, 128)
     assert moe_np.rel_max(ref[tok], oracle_y(layer, x, ids, w, tokens=tok)) <= 1e-4
