@@ -333,32 +333,44 @@ __device__ __forceinline__ void tile6_sb(const uint8_t* r0, const uint8_t* r1, c
   const uint4* xr = reinterpret_cast<const uint4*>(xs + (g < slots ? g : 0) * x_stride) + c * 32 + t;
   const __nv_bfloat162 m160 = __floats2bfloat162_rn(-160.0f, -160.0f);
 #pragma unroll
-  for (int grp = 0; grp < 8; grp++) {  // the 32-groups (h, jj) of the column
-    const int h = grp >> 2, jj = grp & 3;
-    const uint4 bx = xr[4 * grp];      // (this lane's x of the group: both steps)
-    const int qlo = 64 * h + 32 * (jj & 1) + 2 * t, qho = 128 + 32 * h + 2 * t;
+  for (int h = 0; h < 2; h++) {
+    uint4 bx[4];  // (this lane's x of the four 32-groups (h, jj): both steps each)
+#pragma unroll
+    for (int jj = 0; jj < 4; jj++) bx[jj] = xr[4 * (4 * h + jj)];
 #pragma unroll
     for (int half = 0; half < 2; half++) {
-      const int l = 16 * half;
-      uint32_t a[4];
+      const int l = 16 * half + 2 * t;
+      uint32_t a[4][4];  // [jj][register]: a qh pair serves the four crumbs, a ql pair both nibbles
 #pragma unroll
       for (int r = 0; r < 4; r++) {  // (a0: row g, k 2t; a1: row g + 8, k 2t; a2: row g, k 2t + 8; a3: row g + 8)
         const uint8_t* b = (r & 1) ? b1 : b0;
         const int k8 = (r >> 1) * 8;
-        const uint32_t ql = spread2(b + qlo + l + k8), qh = spread2(b + qho + l + k8);
-        const uint32_t nib = (jj & 2) ? (ql >> 4) & 0x000F000Fu : ql & 0x000F000Fu;
-        const uint32_t v = (nib | (((qh >> (2 * jj)) & 0x00030003u) << 4)) | 0x43004300u;  // bf16 128 + q
-        __nv_bfloat162 w = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&v), m160);  // q - 32, exact
-        a[r] = *reinterpret_cast<const uint32_t*>(&w);
+        const uint32_t qh = spread2(b + 128 + 32 * h + l + k8);
+#pragma unroll
+        for (int p = 0; p < 2; p++) {
+          const uint32_t ql = spread2(b + 64 * h + 32 * p + l + k8);
+#pragma unroll
+          for (int hi = 0; hi < 2; hi++) {
+            const int jj = p + 2 * hi;
+            const uint32_t nib = ((hi ? ql >> 4 : ql) & 0x000F000Fu) | 0x43004300u;
+            const uint32_t crumb = jj == 0 ? qh << 4 : jj == 1 ? qh << 2 : jj == 2 ? qh : qh >> 2;
+            const uint32_t v = (crumb & 0x00300030u) | nib;  // bf16 128 + q
+            __nv_bfloat162 w = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&v), m160);  // q - 32, exact
+            a[jj][r] = *reinterpret_cast<const uint32_t*>(&w);
+          }
+        }
       }
-      float acc[4] = {0, 0, 0, 0};
-      ms::mma_bf16(acc, a, half ? bx.z : bx.x, half ? bx.w : bx.y);
-      const int j = 2 * grp + half;  // (the scale index: 16-value group j of the super-block)
-      const float s0 = __fmul_rn(d0, (float)(int8_t)b0[192 + j]), s1 = __fmul_rn(d1, (float)(int8_t)b1[192 + j]);
-      y[0] = fmaf(s0, acc[0], y[0]);
-      y[1] = fmaf(s0, acc[1], y[1]);
-      y[2] = fmaf(s1, acc[2], y[2]);
-      y[3] = fmaf(s1, acc[3], y[3]);
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) {
+        float acc[4] = {0, 0, 0, 0};
+        ms::mma_bf16(acc, a[jj], half ? bx[jj].z : bx[jj].x, half ? bx[jj].w : bx[jj].y);
+        const int j = 2 * (4 * h + jj) + half;  // (the scale index: 16-value group j of the super-block)
+        const float s0 = __fmul_rn(d0, (float)(int8_t)b0[192 + j]), s1 = __fmul_rn(d1, (float)(int8_t)b1[192 + j]);
+        y[0] = fmaf(s0, acc[0], y[0]);
+        y[1] = fmaf(s0, acc[1], y[1]);
+        y[2] = fmaf(s1, acc[2], y[2]);
+        y[3] = fmaf(s1, acc[3], y[3]);
+      }
     }
   }
 }

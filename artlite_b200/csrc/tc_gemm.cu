@@ -8,10 +8,11 @@
 //         and the matching 16 up rows (TMEM lanes 32q + l: l < 16 gate feature 16q + l, l >= 16 up feature 16q + l - 16);
 //         out h[(token), f] = silu(g) u in bf16 (ref.swiglu, tests/moe/ref.py:21-24).
 //   down  A = 128 down rows; out y[(token), n] in bf16.
-// Warp roles (448 threads, one CTA per SM, persistent over a static round-robin of tiles):
+// Warp roles (480 threads, one CTA per SM or one two-CTA cluster per SM pair, persistent over a static round-robin of
+// tiles):
 //   warp 0      TMA producer: raw weight bytes (2D tensor map over the GGUF rows, 16-bit elements, 256 K-values
-//               per stage: 144 B a row for Q4_0 / Q4_K, 272 B for Q8_0) and the token rows (bf16, 128-byte swizzle);
-//               it also allocates and frees the 512 TMEM columns.
+//               per stage: 144 B a row for Q4_0 / Q4_K, 176 B for Q5_K, 272 B for Q8_0) and the token rows (bf16,
+//               128-byte swizzle); it also allocates and frees the 512 TMEM columns.
 //   warp 1      MMA issuer: tcgen05.mma kind::f16 (bf16 x bf16 -> fp32), one thread; tcgen05.commit frees stages.
 //   warps 2-9   dequant, every warp on every step in step order: thread (h, i) decodes values 32 h .. 32 h + 31 of
 //               A row i of each 64-value step (h = 0 for warps 2-5, 1 for warps 6-9) from only that block's raw bytes;
@@ -21,6 +22,8 @@
 //               barrier in order (a parity wait that skipped phases would have to infer them from other barriers,
 //               whose arrivals from the tensor core are not ordered for an observer).
 //   warps 10-13 epilogue: tcgen05.ld of 32 columns at a time, SwiGLU (gu) or the plain rows (down), bf16 stores.
+//   warp 14     (Q6_K, Q3_K) the copy warp: rows of 210 / 110 B a super-block are not 16-byte pitched, so no tensor map
+//               describes them; 16-byte cp.async copies of each row's 16-byte-aligned window instead of the TMA.
 // Every mbarrier wait is bounded (kWaitCycles): on expiry the CTA records ARTLITE_ETIMEOUT in the status word, stops
 // issuing, lets copies and MMAs already issued land, frees its TMEM and exits.
 #include <cuda.h>
