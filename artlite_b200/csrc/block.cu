@@ -444,12 +444,15 @@ int artlite_moe_set_weights(artlite_moe* h, int layer, int qtype, const void* ga
   AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.gate.ptr) + gu_bytes, 0, 64, h->st));
   AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.up.ptr) + gu_bytes, 0, 64, h->st));
   AL_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(L.down.ptr) + dn_bytes, 0, 64, h->st));
-  L.has_dm = false;
-  if (qtype == ARTLITE_Q4_K && down_qtype == ARTLITE_Q4_K && F % 64 == 0 && H % 128 == 0) {
+  L.has_dm = L.has_dm_gu = false;
+  if (qtype == ARTLITE_Q4_K && F % 64 == 0 && H % 128 == 0) {
     AL_TRY(make_raw_map(&L.dm_gate, L.gate.ptr, L.rb_gu, h->E_local * F, 144, 64));
     AL_TRY(make_raw_map(&L.dm_up, L.up.ptr, L.rb_gu, h->E_local * F, 144, 64));
-    AL_TRY(make_raw_map(&L.dm_down, L.down.ptr, L.rb_dn, h->E_local * H, 144, 128));
-    L.has_dm = true;
+    L.has_dm_gu = true;
+    if (down_qtype == ARTLITE_Q4_K) {
+      AL_TRY(make_raw_map(&L.dm_down, L.down.ptr, L.rb_dn, h->E_local * H, 144, 128));
+      L.has_dm = true;
+    }
   }
   L.has_ss = false;  // (the small-batch GEMVs' gate / up maps: Q4_K gate / up, whatever the down type)
   if (qtype == ARTLITE_Q4_K && F % 32 == 0 && H % 128 == 0) {

@@ -22,7 +22,8 @@ struct artlite_moe {
     int64_t rb_gu = 0, rb_dn = 0;
     // Q4_K: tensor maps of the raw rows for the fused decode kernel (gate / up: boxes of 64 rows, down: 128 rows,
     // one 144-byte super-block wide)
-    bool has_dm = false;
+    bool has_dm = false;     // the fused decode kernel's maps of gate, up and down (Q4_K everywhere)
+    bool has_dm_gu = false;  // those of gate and up (Q4_K gate / up, any down type)
     CUtensorMap dm_gate, dm_up, dm_down;
     // and for the small-batch GEMVs (mss.cu): gate / up boxes of 32 rows (down: dm_down)
     bool has_ss = false;

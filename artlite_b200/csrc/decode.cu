@@ -1,6 +1,9 @@
 // The fused decode-batch forward: one cooperative kernel per layer for small batches on the GEMV path (8 <= T, or
-// 16 <= T where the small-batch tensor-core GEMVs of mss.cu apply; T k <= 512 pairs, E <= 256, Q4_0 / Q8_0 / Q4_K weights, one type for gate / up / down, no shared expert). It runs
-// the same steps as the separate kernels of a forward, in phases separated by grid barriers:
+// 16 <= T where the small-batch tensor-core GEMVs of mss.cu apply; T k <= 512 pairs, E <= 256, Q4_0 / Q8_0 / Q4_K
+// weights, and Q4_K gate / up with Q6_K downs; a Q4_K shared expert rides along as one more expert). It runs the same
+// steps as the separate kernels of a forward, in phases separated by grid barriers (for Q4_K layers without a shared
+// expert, by default, the kernel ends after phase 3 and the small-batch down kernel of mss.cu and the combine follow
+// as two more launches: faster than phases 4-5 here, and the only way for Q6_K downs):
 //   1. router logits (router.cu's semantics: fp32 products, fp32 sums, + bias): register-blocked 4 tokens x 4 experts
 //      a warp over a quarter of H (router_tiles), or a warp per (token, expert) for other shapes; for Q4_K also the
 //      tokens' x in the streaming GEMV's fragment order (ms.cuh);
@@ -107,6 +110,10 @@ struct DecodeArgs {
   uint4* shq;
   float *shs, *shy, *sh_s;
   const int32_t* iota;
+  // gu_only: the kernel ends after gate / up, h written in the mma's natural k order (natural) for the small-batch
+  // Q6_K down kernel that follows (Q4_K_M layers), and CTA 0 writes the down items' scan to unit_dn
+  int gu_only, natural;
+  int32_t* unit_dn;
   void* out;
   GridBar* bar;
   DevStatus* status;
@@ -416,6 +423,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
       if (local) a.ids[p] = ids_s[p], a.w[p] = w_s[p];
     }
     for (int e = threadIdx.x; e <= E; e += kThreads) a.offsets[e] = offs[e];
+    if (a.gu_only)
+      for (int e = threadIdx.x; e <= E; e += kThreads) a.unit_dn[e] = uo_dn[e];
   }
   // ---- 3. gate / up
   {
@@ -436,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     const int total = routed + sh_items;
     const int i0 = (int)((int64_t)blockIdx.x * total / gridDim.x), i1 = (int)((int64_t)(blockIdx.x + 1) * total / gridDim.x);
     if constexpr (kMs) {
-      ms::Gemv m{&a.mg, &a.mu, a.H, a.F, E, a.K, a.xq, a.xs, a.hq, a.hs, nullptr};
+      ms::Gemv m{&a.mg, &a.mu, a.H, a.F, E, a.K, a.xq, a.xs, a.hq, a.hs, nullptr, a.natural};
       ms::run<true>(m, uo_gu, offs, perm_s, reinterpret_cast<uint8_t*>(xs), pp, i0, min(i1, routed), a.status);
       if (i1 > routed) {  // (the shared expert: one expert, every token a pair of its own, in token order)
         sh_uo[0] = 0, sh_uo[1] = sh_items, sh_off[0] = 0, sh_off[1] = a.T;
@@ -449,6 +458,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
       rq::run_items<QG, true>(g, a.R_gu, uo_gu, offs, perm_s, xs, i0, i1);
     }
   }
+  if (a.gu_only) return;  // (the down kernel and the combine follow as separate launches)
   if (!grid_sync(a.bar, a.status, 3)) return;
   // ---- 4. down
   {
@@ -571,6 +581,12 @@ bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t 
   // tokens with the register-decoding GEMVs, below 16 with the small-batch tensor-core ones (measured at B = 8: 110 us
   // against the fused kernel's 117; at B = 16: 170 against 161)
   const int64_t t_min = t_set ? t_set : mss_use(h, routed_weights(L), 1, d.act_dtype, d.expert_ffn) ? 16 : 8;
+  if (L.qtype == ARTLITE_Q4_K && L.down_qtype == ARTLITE_Q6_K)  // (Q4_K_M: the kernel through gate / up, then the
+                                                                 // small-batch Q6_K down kernel and the combine)
+    return !off && !L.has_shared && T >= t_min && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts &&
+           h.E_local == d.n_experts && L.has_dm_gu && d.act_dtype == ARTLITE_BF16 && d.hidden % 512 == 0 &&
+           d.expert_ffn % 256 == 0 && mss_use(h, routed_weights(L), 1, d.act_dtype, d.expert_ffn) &&
+           decode_smem(L.qtype, d.hidden, d.expert_ffn) <= 113 * 1024;
   const bool shared_ok = !L.has_shared || (L.sh_has_dm && L.qtype == ARTLITE_Q4_K && L.has_dm && L.sh_F % 256 == 0);
   return !off && shared_ok && T >= t_min && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts && h.E_local == d.n_experts &&
          rq_type(L.qtype) && L.down_qtype == L.qtype && d.hidden % 256 == 0 && d.expert_ffn % 256 == 0 &&
@@ -606,8 +622,8 @@ int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, vo
   a.rb_dn = L.rb_dn;
   a.R_gu = gemv_rq_rows_per_warp(L.qtype, d.hidden, true);
   a.R_dn = gemv_rq_rows_per_warp(L.down_qtype, d.expert_ffn, false);
-  a.mult_gu = (int)cdiv(d.expert_ffn, a.R_gu * rq::kWarps);
-  a.mult_dn = (int)cdiv(d.hidden, a.R_dn * rq::kWarps);
+  a.mult_gu = a.R_gu > 0 ? (int)cdiv(d.expert_ffn, a.R_gu * rq::kWarps) : 0;
+  a.mult_dn = a.R_dn > 0 ? (int)cdiv(d.hidden, a.R_dn * rq::kWarps) : 0;  // (a Q6_K down: no register GEMV)
   if (L.qtype == ARTLITE_Q4_K) {
     a.mult_gu = d.expert_ffn / 64;
     a.mult_dn = d.hidden / 128;
@@ -646,6 +662,20 @@ int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, vo
     a.sh_s = h->sh_s.as<float>();
     a.iota = h->sh_iota.as<int32_t>();
   }
+  const bool mixed = L.qtype == ARTLITE_Q4_K && L.down_qtype == ARTLITE_Q6_K;
+  // the down projection and the combine as separate launches after the fused kernel's gate / up (the small-batch
+  // down kernel's whole items per CTA, each item's rows requested as the warps finish the previous one, measured
+  // faster than the fused kernel's down phase: Q4_K B = 16 161 -> 154 us, B = 64 224 -> 216 us; Q6_K downs always:
+  // the fused kernel has no Q6_K phase); ARTLITE_DECODE_SPLIT=0 keeps Q4_K downs (and a shared expert's) in the kernel
+  static const bool split_off = [] {
+    const char* v = getenv("ARTLITE_DECODE_SPLIT");
+    return v && v[0] == '0';
+  }();
+  const bool split = mixed || (L.qtype == ARTLITE_Q4_K && L.down_qtype == ARTLITE_Q4_K && !L.has_shared && L.has_dm &&
+                               !split_off);
+  a.gu_only = split ? 1 : 0;
+  a.natural = mixed ? 1 : 0;
+  a.unit_dn = h->unit_dn.as<int32_t>();
   const size_t smem = decode_smem(L.qtype, d.hidden, d.expert_ffn);
   auto go = [&](auto kern) -> int {
     AL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -669,6 +699,29 @@ int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, vo
     count_launch();
     return ARTLITE_OK;
   };
+  if (split) {  // gate / up in the fused kernel, then the small-batch down kernel and the combine
+    AL_TRY(go(decode_kernel<ARTLITE_Q4_K, ARTLITE_Q4_K, kMaxExperts / 32>));
+    MssLaunch s{};
+    s.down_map = mixed ? nullptr : &L.dm_down;
+    s.H = d.hidden;
+    s.F = d.expert_ffn;
+    s.E = d.n_experts;
+    s.k = d.top_k;
+    s.hq = a.hq;
+    s.hs = a.hs;
+    s.y = a.y;
+    s.unit_dn = a.unit_dn;
+    s.offsets = a.offsets;
+    s.perm = a.perm;
+    s.slots = (int)std::min<int64_t>(kGemvTokens, T);  // (a token's k pairs go to distinct experts)
+    s.status = a.status;
+    s.down_qtype = L.down_qtype;
+    s.down_raw = a.down;
+    s.rb_dn = L.rb_dn;
+    AL_TRY(launch_mss(s, false, st));
+    return launch_combine(a.y, ARTLITE_F32, a.slot, a.w, T, d.top_k, d.hidden, y, d.act_dtype, st, CombineOwn{},
+                          CombineShared{}, res);
+  }
 #define AL_DEC(QG, QD) \
   if (L.qtype == QG && L.down_qtype == QD) return go(decode_kernel<QG, QD, kMaxExperts / 32>);
   AL_DEC(ARTLITE_Q4_0, ARTLITE_Q4_0)

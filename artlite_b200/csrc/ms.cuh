@@ -123,6 +123,7 @@ struct Gemv {
   uint4* hq;
   float* hs;
   float* y;
+  int natural;  // gu: h in the mma's natural k order (for a Q6_K down kernel), else this tile's order
 };
 
 struct Pipe {  // the CTA's stages: full mbarriers (the copies landed: one arrival + bytes) and the parity each thread
@@ -358,9 +359,16 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
         __syncthreads();  // (the other buffer: free since the previous item's barrier)
         if (threadIdx.x < 64) {  // (n, group of 32 rows, t): 8 h values in fragment order, and the group sum
           const int n = threadIdx.x >> 3, grp = (threadIdx.x >> 2) & 1, tq = threadIdx.x & 3;
-          const float4 h0 = *reinterpret_cast<const float4*>(hb + n * 64 + grp * 32 + 8 * tq);
-          const float4 h1 = *reinterpret_cast<const float4*>(hb + n * 64 + grp * 32 + 8 * tq + 4);
-          const float v[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+          const float* hg = hb + n * 64 + grp * 32;
+          float v[8];
+          if (a.natural) {  // values 2 tq, 2 tq + 1, 2 tq + 8, 2 tq + 9 and the same + 16, as bf16 pairs in that order
+#pragma unroll
+            for (int j = 0; j < 4; j++) v[2 * j] = hg[2 * tq + 8 * j], v[2 * j + 1] = hg[2 * tq + 8 * j + 1];
+          } else {
+            const float4 h0 = *reinterpret_cast<const float4*>(hg + 8 * tq);
+            const float4 h1 = *reinterpret_cast<const float4*>(hg + 8 * tq + 4);
+            v[0] = h0.x, v[1] = h0.y, v[2] = h0.z, v[3] = h0.w, v[4] = h1.x, v[5] = h1.y, v[6] = h1.z, v[7] = h1.w;
+          }
           float part = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
           part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
           part += __shfl_xor_sync(0xFFFFFFFFu, part, 2);
@@ -368,7 +376,16 @@ __device__ __forceinline__ void run(const Gemv& a, const int32_t* uo, const int6
             const int Go = a.N >> 5;
             const int64_t pr = it.d0 + n;
             const int og = it.rt * 2 + grp;
-            a.hq[(pr * Go + og) * 4 + tq] = arrange(v);
+            uint4 o;
+            if (a.natural) {
+              uint32_t b[8];
+#pragma unroll
+              for (int j = 0; j < 8; j++) b[j] = __float_as_uint(v[j]) >> 16;  // (v are bf16 values)
+              o = make_uint4(b[0] | b[1] << 16, b[2] | b[3] << 16, b[4] | b[5] << 16, b[6] | b[7] << 16);
+            } else {
+              o = arrange(v);
+            }
+            a.hq[(pr * Go + og) * 4 + tq] = o;
             if (tq == 0) a.hs[pr * Go + og] = part;
           }
         }
