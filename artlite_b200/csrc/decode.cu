@@ -580,7 +580,11 @@ bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t 
   // below the threshold the separate kernels, whose GEMVs spread finer items over the whole grid, are faster: below 8
   // tokens with the register-decoding GEMVs, below 16 with the small-batch tensor-core ones (measured at B = 8: 110 us
   // against the fused kernel's 117; at B = 16: 170 against 161)
-  const int64_t t_min = t_set ? t_set : mss_use(h, routed_weights(L), 1, d.act_dtype, d.expert_ffn) ? 16 : 8;
+  // (layers whose down runs as the separate small-batch kernel after the kernel's gate / up: from 10 tokens, between
+  // the measured B = 8, chain 105 against 110 us, and B = 12, 142 against 130 us)
+  const bool splits = !L.has_shared && L.qtype == ARTLITE_Q4_K && (L.down_qtype == ARTLITE_Q6_K || L.has_dm);
+  const bool mss = mss_use(h, routed_weights(L), 1, d.act_dtype, d.expert_ffn);
+  const int64_t t_min = t_set ? t_set : mss ? (splits ? 10 : 16) : 8;
   if (L.qtype == ARTLITE_Q4_K && L.down_qtype == ARTLITE_Q6_K)  // (Q4_K_M: the kernel through gate / up, then the
                                                                  // small-batch Q6_K down kernel and the combine)
     return !off && !L.has_shared && T >= t_min && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts &&
