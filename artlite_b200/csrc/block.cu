@@ -650,6 +650,12 @@ int artlite_moe_set_shared(artlite_moe* h, int layer, int ffn, int qtype, const 
     AL_TRY(h->sh_hq.reserve(std::max(h->sh_hq.bytes, (size_t)(sizeof(uint16_t) * T * F + sizeof(float) * T * (F / 32)))));
     L.sh_has_dm = true;
   }
+  L.sh_has_ss = false;  // (decode batches below the fused kernel: the shared expert on the small-batch GEMVs)
+  if (qtype == ARTLITE_Q4_K && F % 32 == 0 && H % 128 == 0) {
+    AL_TRY(make_raw_map(&L.sh_ss_gate, L.sh_gate.ptr, L.sh_rb_gu, F, 144, 32));
+    AL_TRY(make_raw_map(&L.sh_ss_up, L.sh_up.ptr, L.sh_rb_gu, F, 144, 32));
+    L.sh_has_ss = true;
+  }
   L.has_shared = true;
   return wait(h->st, 0);
 }

@@ -42,6 +42,8 @@ struct artlite_moe {
     // Q4_K shared experts: tensor maps of its raw rows for the fused decode kernel (as dm_* for the routed experts)
     bool sh_has_dm = false;
     CUtensorMap sh_dm_gate, sh_dm_up, sh_dm_down;
+    bool sh_has_ss = false;           // the small-batch GEMVs' gate / up maps of the shared expert (Q4_K gate / up)
+    CUtensorMap sh_ss_gate, sh_ss_up;
   };
   std::vector<Layer> layers;
   // workspaces
@@ -136,7 +138,8 @@ inline ExpertWeights routed_weights(const artlite_moe::Layer& L) {
 }
 inline ExpertWeights shared_weights(const artlite_moe::Layer& L) {
   return {L.sh_qtype, L.sh_down_qtype, L.sh_gate.as<uint8_t>(), L.sh_up.as<uint8_t>(), L.sh_down.as<uint8_t>(),
-          L.sh_rb_gu, L.sh_rb_dn, nullptr, nullptr, nullptr};
+          L.sh_rb_gu, L.sh_rb_dn, L.sh_has_ss ? &L.sh_ss_gate : nullptr, L.sh_has_ss ? &L.sh_ss_up : nullptr,
+          L.sh_has_dm ? &L.sh_dm_down : nullptr};
 }
 // the small-batch tensor-core GEMVs apply (GEMV path, Q4_K with maps, bf16 x; ARTLITE_DECODE_MSS=0 turns them off)
 bool mss_use(const artlite_moe& h, const ExpertWeights& W, int path, int x_dtype, int F);

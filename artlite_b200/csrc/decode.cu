@@ -582,9 +582,11 @@ bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t 
   // against the fused kernel's 117; at B = 16: 170 against 161)
   // (layers whose down runs as the separate small-batch kernel after the kernel's gate / up: from 10 tokens, between
   // the measured B = 8, chain 105 against 110 us, and B = 12, 142 against 130 us)
+  // (a layer with a shared expert the kernel carries: from 3 tokens, between the measured qwen35moe B = 2, chain 55.7
+  // against 61.5 us, and B = 4, 73.6 against 70.3 us; the chain runs the shared expert as a separate row group)
   const bool splits = !L.has_shared && L.qtype == ARTLITE_Q4_K && (L.down_qtype == ARTLITE_Q6_K || L.has_dm);
   const bool mss = mss_use(h, routed_weights(L), 1, d.act_dtype, d.expert_ffn);
-  const int64_t t_min = t_set ? t_set : mss ? (splits ? 10 : 16) : 8;
+  const int64_t t_min = t_set ? t_set : L.has_shared && mss ? 3 : mss ? (splits ? 10 : 16) : 8;
   if (L.qtype == ARTLITE_Q4_K && L.down_qtype == ARTLITE_Q6_K)  // (Q4_K_M: the kernel through gate / up, then the
                                                                  // small-batch Q6_K down kernel and the combine)
     return !off && !L.has_shared && T >= t_min && T * d.top_k <= kMaxPairs && d.n_experts <= kMaxExperts &&
