@@ -22,8 +22,8 @@
 //               barrier in order (a parity wait that skipped phases would have to infer them from other barriers,
 //               whose arrivals from the tensor core are not ordered for an observer).
 //   warps 10-13 epilogue: tcgen05.ld of 32 columns at a time, SwiGLU (gu) or the plain rows (down), bf16 stores.
-//   warp 14     (Q6_K, Q3_K) the copy warp: rows of 210 / 110 B a super-block are not 16-byte pitched, so no tensor map
-//               describes them; 16-byte cp.async copies of each row's 16-byte-aligned window instead of the TMA.
+//   warp 14     (Q6_K, Q3_K, IQ4_XS) the copy warp: rows of 210 / 110 / 136 B a super-block are not 16-byte pitched,
+//               so no tensor map describes them; 16-byte cp.async copies of each row's 16-byte-aligned window instead.
 // Every mbarrier wait is bounded (kWaitCycles): on expiry the CTA records ARTLITE_ETIMEOUT in the status word, stops
 // issuing, lets copies and MMAs already issued land, frees its TMEM and exits.
 #include <cuda.h>
@@ -44,20 +44,24 @@ constexpr int kThreads = 480;  // 15 warps: producer, MMA, 8 dequant, 4 epilogue
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at the B200's clocks
 
 __host__ __device__ constexpr int chunk_bytes(int qt) {  // raw bytes of 256 values of a row
-  return qt == ARTLITE_Q8_0 ? 272 : (qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_K) ? 144 : qt == ARTLITE_Q5_K ? 176
-       : qt == ARTLITE_Q6_K ? 210 : qt == ARTLITE_Q3_K ? 110 : 0;
+  return qt == ARTLITE_Q8_0 ? 272 : (qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_K || qt == ARTLITE_IQ4_NL) ? 144
+       : qt == ARTLITE_Q5_K ? 176 : qt == ARTLITE_Q6_K ? 210 : qt == ARTLITE_Q3_K ? 110 : qt == ARTLITE_IQ4_XS ? 136 : 0;
 }
 // a raw stage row in shared memory: the chunk's bytes (TMA formats), or for Q6_K (whose rows need not be 16-byte
 // pitched, so no tensor map can describe them) the 16-byte-aligned 224-byte window around the 210-byte super-block,
 // copied by the copy warp, in rows 240 bytes apart (16-byte loads of 8 consecutive rows fall in distinct banks)
 __host__ __device__ constexpr int raw_pitch(int qt) {
-  return qt == ARTLITE_Q6_K ? 240 : qt == ARTLITE_Q3_K ? 144 : chunk_bytes(qt);
+  return qt == ARTLITE_Q6_K ? 240 : qt == ARTLITE_Q3_K ? 144 : qt == ARTLITE_IQ4_XS ? 176 : chunk_bytes(qt);
 }
-// the formats whose rows the copy warp brings (Q6_K, 210 B, and Q3_K, 110 B, a super-block: rows need not be 16-byte
-// pitched), and the 16-byte copies of a row's window (the block plus the up to 14 bytes before it from the 16-byte
-// boundary at or below its start: Q6_K 224 bytes, Q3_K 128)
-__host__ __device__ constexpr bool windowed(int qt) { return qt == ARTLITE_Q6_K || qt == ARTLITE_Q3_K; }
-__host__ __device__ constexpr int window_chunks(int qt) { return qt == ARTLITE_Q6_K ? 14 : qt == ARTLITE_Q3_K ? 8 : 0; }
+// the formats whose rows the copy warp brings (Q6_K, 210 B, Q3_K, 110 B, IQ4_XS, 136 B a super-block: rows need not be
+// 16-byte pitched), and the 16-byte copies of a row's window (the block plus the up to 14 bytes before it from the
+// 16-byte boundary at or below its start: Q6_K 224 bytes, Q3_K 128, IQ4_XS 160)
+__host__ __device__ constexpr bool windowed(int qt) {
+  return qt == ARTLITE_Q6_K || qt == ARTLITE_Q3_K || qt == ARTLITE_IQ4_XS;
+}
+__host__ __device__ constexpr int window_chunks(int qt) {
+  return qt == ARTLITE_Q6_K ? 14 : qt == ARTLITE_Q3_K ? 8 : qt == ARTLITE_IQ4_XS ? 10 : 0;
+}
 
 // raw weight stages: three of 18 KB for the 144-byte formats, two of 34 KB for Q8_0 (shared memory)
 __host__ __device__ constexpr int raw_stages(int qt) { return qt == ARTLITE_Q8_0 || qt == ARTLITE_Q6_K ? 2 : 3; }
@@ -418,15 +422,67 @@ __device__ __forceinline__ void dq_q3_k_block(const uint8_t* win, int off, int s
   }
 }
 
+// the IQ4_NL / IQ4_XS code values (dequant.cpp:119, ggml's non-linear grid) + 128, as bytes: four code indices (bytes
+// < 16) to four grid bytes by two byte permutes over the 16-entry table in four registers, picked per byte by bit 3
+__device__ __forceinline__ uint32_t iq4_bytes(uint32_t idx) {
+  constexpr uint32_t G0 = 0x3F2D1801u, G1 = 0x766A5D4Fu, G2 = 0xA6998D81u, G3 = 0xF1D9C5B5u;  // 1, 24, 45, ... 241
+  const uint32_t x = idx & 0x07070707u;
+  const uint32_t s = x | (x >> 4);                            // (byte 0: i0 | i1 << 4, byte 2: i2 | i3 << 4)
+  const uint32_t sel = (s & 0xFFu) | ((s >> 8) & 0xFF00u);    // (the four indices & 7 as selector nibbles)
+  const uint32_t lo = __byte_perm(G0, G1, sel), hi = __byte_perm(G2, G3, sel);
+  const uint32_t m = ((idx >> 3) & 0x01010101u) * 0xFFu;
+  return (lo & ~m) | (hi & m);
+}
+
+// IQ4_NL block at byte o of the stage's row bytes (dequant.cpp:121-126: Q4_0's layout): 32 values d grid[q]
+__device__ __forceinline__ void dq_iq4_nl_block(const uint32_t* w, int o, uint32_t* o16) {
+  const uint64_t d = dup2(half_at(w, o)), off = dup2(-8388736.0f);  // -(2^23 + 128)
+  uint32_t q[4];
+  words16(w, o + 2, q);
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    uint64_t a, b, c, e;
+    magic4(iq4_bytes(q[k] & 0x0F0F0F0Fu), a, b);         // values 4k .. 4k + 3 (low nibbles)
+    magic4(iq4_bytes((q[k] >> 4) & 0x0F0F0F0Fu), c, e);  // values 16 + 4k .. (high nibbles)
+    o16[2 * k] = bf16x2(mul2(d, add2(a, off)));
+    o16[2 * k + 1] = bf16x2(mul2(d, add2(b, off)));
+    o16[8 + 2 * k] = bf16x2(mul2(d, add2(c, off)));
+    o16[8 + 2 * k + 1] = bf16x2(mul2(d, add2(e, off)));
+  }
+}
+
+// IQ4_XS values 64 sub + 32 H .. + 31 of the super-block at byte off of the window (dequant.cpp:128-140): 32-group
+// g = 2 sub + H with ls = nibble (g % 2) of byte 4 + g / 2 | crumb g of the u16 at byte 2 << 4, w = (d (ls - 32)) grid[q]
+// over its 16 code bytes at 8 + 16 g in Q4_0's order
+template <int H>
+__device__ __forceinline__ void dq_iq4_xs_block(const uint8_t* win, int off, int sub, uint32_t (&o)[16]) {
+  const int g = 2 * sub + H;
+  const uint32_t w0 = q6_word(win, off);  // (d, then the high scale crumbs)
+  const float d = __half2float(__ushort_as_half((unsigned short)(w0 & 0xFFFFu)));
+  const int ls = ((win[off + 4 + (g >> 1)] >> (4 * (g & 1))) & 15) | (int)((w0 >> (16 + 2 * g)) & 3u) << 4;
+  const uint64_t dl = dup2(__fmul_rn(d, (float)(ls - 32))), bias = dup2(-8388736.0f);  // -(2^23 + 128)
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const uint32_t qw = q6_word(win, off + 8 + 16 * g + 4 * k);
+    uint64_t a, b, c, e;
+    magic4(iq4_bytes(qw & 0x0F0F0F0Fu), a, b);
+    magic4(iq4_bytes((qw >> 4) & 0x0F0F0F0Fu), c, e);
+    o[2 * k] = bf16x2(mul2(dl, add2(a, bias)));
+    o[2 * k + 1] = bf16x2(mul2(dl, add2(b, bias)));
+    o[8 + 2 * k] = bf16x2(mul2(dl, add2(c, bias)));
+    o[8 + 2 * k + 1] = bf16x2(mul2(dl, add2(e, bias)));
+  }
+}
+
 // the 16-byte chunks [lo, hi] of a row's stage bytes that block / group 2 sub + h of a 256-value chunk reads
 template <int QT, int H>
 struct BlockSpan {
   static constexpr int b(int sub) { return 2 * sub + H; }
   static constexpr int lo(int sub) {
-    return QT == ARTLITE_Q4_0 ? (18 * b(sub)) / 16 : QT == ARTLITE_Q8_0 ? (34 * b(sub)) / 16 : 0;
+    return QT == ARTLITE_Q4_0 || QT == ARTLITE_IQ4_NL ? (18 * b(sub)) / 16 : QT == ARTLITE_Q8_0 ? (34 * b(sub)) / 16 : 0;
   }
   static constexpr int hi(int sub) {
-    return QT == ARTLITE_Q4_0 ? (18 * b(sub) + 17) / 16
+    return QT == ARTLITE_Q4_0 || QT == ARTLITE_IQ4_NL ? (18 * b(sub) + 17) / 16
          : QT == ARTLITE_Q8_0 ? (34 * b(sub) + 33) / 16
          : QT == ARTLITE_Q4_K ? 0 : 2;  // (Q4_K: the header; Q5_K: the header and qh)
   }
@@ -452,6 +508,7 @@ __device__ __forceinline__ void dequant_block(const uint4* src, uint32_t* w, int
   }
   const int b = 2 * sub + H;
   if constexpr (QT == ARTLITE_Q4_0) dq_q4_0_block(w, 18 * b, o);
+  else if constexpr (QT == ARTLITE_IQ4_NL) dq_iq4_nl_block(w, 18 * b, o);
   else if constexpr (QT == ARTLITE_Q8_0) dq_q8_0_block(w, 34 * b, o);
   else if constexpr (QT == ARTLITE_Q5_K) dq_q5_k_group(w, b, o);
   else dq_q4_k_group(w, b, o);
@@ -462,7 +519,7 @@ __device__ __forceinline__ void dequant_block(const uint4* src, uint32_t* w, int
 // the kernel's shared-memory pipeline depth: A + B stages and raw weight stages, per format and mode
 __host__ __device__ constexpr int b_stage_bytes(bool pair) { return pair ? B_BYTES / 2 : B_BYTES; }
 __host__ __device__ constexpr int ab_stages(int qt, bool pair) {
-  return pair ? (qt == ARTLITE_Q8_0 || qt == ARTLITE_Q5_K || qt == ARTLITE_Q6_K ? 4 : 5) : 3;
+  return pair ? (qt == ARTLITE_Q8_0 || qt == ARTLITE_Q5_K || qt == ARTLITE_Q6_K || qt == ARTLITE_IQ4_XS ? 4 : 5) : 3;
 }
 // the epilogue's transpose buffers: per epilogue warp 32 token rows of up to 32 bf16 values, rows 80 bytes apart
 // (16-byte row reads of 8 consecutive lanes fall in distinct banks)
@@ -701,6 +758,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_gemm(const __grid_const
           } else if constexpr (QT == ARTLITE_Q3_K) {
             if (h == 0) dq_q3_k_block<0>(reinterpret_cast<const uint8_t*>(src), q6off, sub, o);
             else dq_q3_k_block<1>(reinterpret_cast<const uint8_t*>(src), q6off, sub, o);
+          } else if constexpr (QT == ARTLITE_IQ4_XS) {
+            if (h == 0) dq_iq4_xs_block<0>(reinterpret_cast<const uint8_t*>(src), q6off, sub, o);
+            else dq_iq4_xs_block<1>(reinterpret_cast<const uint8_t*>(src), q6off, sub, o);
           } else {
             if (h == 0) dequant_block<QT, 0>(src, w, sub, o);
             else dequant_block<QT, 1>(src, w, sub, o);
@@ -1137,6 +1197,8 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
     AL_TC_CASE(ARTLITE_Q5_K)
     AL_TC_CASE(ARTLITE_Q6_K)
     AL_TC_CASE(ARTLITE_Q3_K)
+    AL_TC_CASE(ARTLITE_IQ4_NL)
+    AL_TC_CASE(ARTLITE_IQ4_XS)
     default: break;
   }
 #undef AL_TC_CASE
