@@ -11,8 +11,8 @@
 // Warp roles (480 threads, one CTA per SM or one two-CTA cluster per SM pair, persistent over a static round-robin of
 // tiles):
 //   warp 0      TMA producer: raw weight bytes (2D tensor map over the GGUF rows, 16-bit elements, 256 K-values
-//               per stage: 144 B a row for Q4_0 / Q4_K, 176 B for Q5_K, 272 B for Q8_0) and the token rows (bf16,
-//               128-byte swizzle); it also allocates and frees the 512 TMEM columns.
+//               per stage: 144 B a row for Q4_0 / Q4_K / IQ4_NL, 160 B for Q4_1, 176 B for Q5_K, 272 B for Q8_0) and
+//               the token rows (bf16, 128-byte swizzle); it also allocates and frees the 512 TMEM columns.
 //   warp 1      MMA issuer: tcgen05.mma kind::f16 (bf16 x bf16 -> fp32), one thread; tcgen05.commit frees stages.
 //   warps 2-9   dequant, every warp on every step in step order: thread (h, i) decodes values 32 h .. 32 h + 31 of
 //               A row i of each 64-value step (h = 0 for warps 2-5, 1 for warps 6-9) from only that block's raw bytes;
@@ -45,7 +45,8 @@ constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at the B200's clocks
 
 __host__ __device__ constexpr int chunk_bytes(int qt) {  // raw bytes of 256 values of a row
   return qt == ARTLITE_Q8_0 ? 272 : (qt == ARTLITE_Q4_0 || qt == ARTLITE_Q4_K || qt == ARTLITE_IQ4_NL) ? 144
-       : qt == ARTLITE_Q5_K ? 176 : qt == ARTLITE_Q6_K ? 210 : qt == ARTLITE_Q3_K ? 110 : qt == ARTLITE_IQ4_XS ? 136 : 0;
+       : qt == ARTLITE_Q5_K ? 176 : qt == ARTLITE_Q6_K ? 210 : qt == ARTLITE_Q3_K ? 110 : qt == ARTLITE_IQ4_XS ? 136
+       : qt == ARTLITE_Q4_1 ? 160 : 0;
 }
 // a raw stage row in shared memory: the chunk's bytes (TMA formats), or for Q6_K (whose rows need not be 16-byte
 // pitched, so no tensor map can describe them) the 16-byte-aligned 224-byte window around the 210-byte super-block,
@@ -291,6 +292,24 @@ __device__ __forceinline__ void dq_q4_0_block(const uint32_t* w, int o, uint32_t
   }
 }
 
+// Q4_1 block at byte o (dequant.cpp:49-56: 20 B per 32, d, m, then Q4_0's nibble layout): 32 values d q + m (a product
+// and a sum, each rounded once)
+__device__ __forceinline__ void dq_q4_1_block(const uint32_t* w, int o, uint32_t* o16) {
+  const uint64_t d = dup2(half_at(w, o)), m = dup2(half_at(w, o + 2)), off = dup2(-8388608.0f);  // -2^23
+  uint32_t q[4];
+  words16(w, o + 4, q);
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    uint64_t a, b, c, e;
+    magic4(q[k] & 0x0F0F0F0Fu, a, b);
+    magic4((q[k] >> 4) & 0x0F0F0F0Fu, c, e);
+    o16[2 * k] = bf16x2(add2(mul2(d, add2(a, off)), m));
+    o16[2 * k + 1] = bf16x2(add2(mul2(d, add2(b, off)), m));
+    o16[8 + 2 * k] = bf16x2(add2(mul2(d, add2(c, off)), m));
+    o16[8 + 2 * k + 1] = bf16x2(add2(mul2(d, add2(e, off)), m));
+  }
+}
+
 // Q8_0 block at byte o: 32 values d q (q int8: biased by 128 into a byte, then the magic)
 __device__ __forceinline__ void dq_q8_0_block(const uint32_t* w, int o, uint32_t* o16) {
   const uint64_t d = dup2(half_at(w, o)), off = dup2(-8388736.0f);  // -(2^23 + 128)
@@ -479,10 +498,12 @@ template <int QT, int H>
 struct BlockSpan {
   static constexpr int b(int sub) { return 2 * sub + H; }
   static constexpr int lo(int sub) {
-    return QT == ARTLITE_Q4_0 || QT == ARTLITE_IQ4_NL ? (18 * b(sub)) / 16 : QT == ARTLITE_Q8_0 ? (34 * b(sub)) / 16 : 0;
+    return QT == ARTLITE_Q4_0 || QT == ARTLITE_IQ4_NL ? (18 * b(sub)) / 16 : QT == ARTLITE_Q8_0 ? (34 * b(sub)) / 16
+         : QT == ARTLITE_Q4_1 ? (20 * b(sub)) / 16 : 0;
   }
   static constexpr int hi(int sub) {
     return QT == ARTLITE_Q4_0 || QT == ARTLITE_IQ4_NL ? (18 * b(sub) + 17) / 16
+         : QT == ARTLITE_Q4_1 ? (20 * b(sub) + 19) / 16
          : QT == ARTLITE_Q8_0 ? (34 * b(sub) + 33) / 16
          : QT == ARTLITE_Q4_K ? 0 : 2;  // (Q4_K: the header; Q5_K: the header and qh)
   }
@@ -509,6 +530,7 @@ __device__ __forceinline__ void dequant_block(const uint4* src, uint32_t* w, int
   const int b = 2 * sub + H;
   if constexpr (QT == ARTLITE_Q4_0) dq_q4_0_block(w, 18 * b, o);
   else if constexpr (QT == ARTLITE_IQ4_NL) dq_iq4_nl_block(w, 18 * b, o);
+  else if constexpr (QT == ARTLITE_Q4_1) dq_q4_1_block(w, 20 * b, o);
   else if constexpr (QT == ARTLITE_Q8_0) dq_q8_0_block(w, 34 * b, o);
   else if constexpr (QT == ARTLITE_Q5_K) dq_q5_k_group(w, b, o);
   else dq_q4_k_group(w, b, o);
@@ -519,7 +541,11 @@ __device__ __forceinline__ void dequant_block(const uint4* src, uint32_t* w, int
 // the kernel's shared-memory pipeline depth: A + B stages and raw weight stages, per format and mode
 __host__ __device__ constexpr int b_stage_bytes(bool pair) { return pair ? B_BYTES / 2 : B_BYTES; }
 __host__ __device__ constexpr int ab_stages(int qt, bool pair) {
-  return pair ? (qt == ARTLITE_Q8_0 || qt == ARTLITE_Q5_K || qt == ARTLITE_Q6_K || qt == ARTLITE_IQ4_XS ? 4 : 5) : 3;
+  return pair ? (qt == ARTLITE_Q8_0 || qt == ARTLITE_Q5_K || qt == ARTLITE_Q6_K || qt == ARTLITE_IQ4_XS ||
+                         qt == ARTLITE_Q4_1
+                     ? 4
+                     : 5)
+              : 3;
 }
 // the epilogue's transpose buffers: per epilogue warp 32 token rows of up to 32 bf16 values, rows 80 bytes apart
 // (16-byte row reads of 8 consecutive lanes fall in distinct banks)
@@ -1198,6 +1224,7 @@ int launch_tc_gemm(const TcGemmArgs& a, bool gu, cudaStream_t st) {
     AL_TC_CASE(ARTLITE_Q6_K)
     AL_TC_CASE(ARTLITE_Q3_K)
     AL_TC_CASE(ARTLITE_IQ4_NL)
+    AL_TC_CASE(ARTLITE_Q4_1)
     AL_TC_CASE(ARTLITE_IQ4_XS)
     default: break;
   }

@@ -32,11 +32,12 @@ def run_checked(layer, x, T, path, k=8):
 @pytest.mark.parametrize("qtype,down", [("Q5_K", "Q5_K"), ("Q4_K", "Q5_K"), ("Q5_K", "Q4_K"), ("Q4_0", "Q5_K"),
                                         ("Q8_0", "Q5_K"), ("Q6_K", "Q6_K"), ("Q4_K", "Q6_K"), ("Q8_0", "Q6_K"),
                                         ("Q3_K", "Q3_K"), ("Q4_K", "Q3_K"), ("Q3_K", "Q6_K"), ("IQ4_NL", "IQ4_NL"),
-                                        ("IQ4_XS", "IQ4_XS"), ("Q4_K", "IQ4_XS"), ("IQ4_NL", "Q6_K")])
+                                        ("IQ4_XS", "IQ4_XS"), ("Q4_K", "IQ4_XS"), ("IQ4_NL", "Q6_K"), ("Q4_1", "Q4_1"),
+                                        ("Q4_1", "Q6_K")])
 def test_tcgen05_q5_k_q6_k_and_mixed(qtype, down):
-    """Q5_K, Q6_K, Q3_K, IQ4_NL and IQ4_XS on the tensor cores, alone and mixed with the other formats (E=16, H=512,
-    F=256, T=200: ragged groups; Q6_K, Q3_K and IQ4_XS rows (420 / 210, 220 / 110, 272 / 136 bytes) are not 16-byte
-    pitched and go through the copy warp; the IQ4 code values by byte permutes)."""
+    """Q5_K, Q6_K, Q3_K, IQ4_NL, IQ4_XS and Q4_1 on the tensor cores, alone and mixed with the other formats (E=16,
+    H=512, F=256, T=200: ragged groups; Q6_K, Q3_K and IQ4_XS rows (420 / 210, 220 / 110, 272 / 136 bytes) are not
+    16-byte pitched and go through the copy warp; the IQ4 code values by byte permutes)."""
     layer, x, _ = moe_np.make_block(90, 200, qtype=qtype, down_qtype=down, E=16, H=512, F=256)
     y, ids, w, took = run_checked(layer, x, 200, "tc")
     assert took == "tc"
