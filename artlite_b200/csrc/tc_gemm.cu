@@ -263,6 +263,23 @@ __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// bytes i and j of w, each placed in byte kPos (1 or 2) of a word whose byte 3 is kExp and whose other bytes are 0:
+// with kExp the top byte of the float 2^E (its exponent's low bit 0), the floats 2^E + byte 2^(E - 23 + 8 kPos)
+template <uint32_t kExp, int kPos>
+__device__ __forceinline__ uint64_t under2(uint32_t w, int i, int j) {
+  // selector nibbles: kPos takes byte i (j) of w, byte 3 takes operand byte 4 (kExp), the rest operand byte 5 (0)
+  const uint32_t si = kPos == 1 ? (0x4505u | (uint32_t)i << 4) : (0x4055u | (uint32_t)i << 8);
+  const uint32_t sj = kPos == 1 ? (0x4505u | (uint32_t)j << 4) : (0x4055u | (uint32_t)j << 8);
+  const uint32_t a = __byte_perm(w, kExp, si), b = __byte_perm(w, kExp, sj);
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
+  return r;
+}
 __device__ __forceinline__ uint32_t bf16x2(uint64_t v) {
   float a, b;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
@@ -275,20 +292,23 @@ __device__ __forceinline__ void words16(const uint32_t* w, int o, uint32_t (&q)[
     q[k] = (o & 2) ? __funnelshift_r(w[(o >> 2) + k], w[(o >> 2) + k + 1], 16) : w[(o >> 2) + k];
 }
 
-// Q4_0 block at byte o of the stage's row bytes: 32 values (q - 8) d as 16 bf16 pairs into o16
+// Q4_0 block at byte o of the stage's row bytes: 32 values (q - 8) d as 16 bf16 pairs into o16. A low nibble q in
+// byte 2 under the exponent byte 0x43 is the float 128 + q; a high nibble left in place (bits 4-7 of byte 1) under
+// 0x45 is 2048 + q. One fused multiply-add a pair, (128 + q) d - 136 d or (2048 + q) d - 2056 d, is (q - 8) d
+// exactly: 136 d and 2056 d are exact products (at most 20 significant bits), and so is the single rounding of the
+// exact result (q - 8) d (at most 15 bits); then one rounding to bf16, as the reference's fp32 value rounded
 __device__ __forceinline__ void dq_q4_0_block(const uint32_t* w, int o, uint32_t* o16) {
-  const uint64_t d = dup2(half_at(w, o)), off = dup2(-8388616.0f);  // -(2^23 + 8)
+  const float df = half_at(w, o);
+  const uint64_t d = dup2(df), clo = dup2(-136.0f * df), chi = dup2(-2056.0f * df);
   uint32_t q[4];
   words16(w, o + 2, q);
 #pragma unroll
   for (int k = 0; k < 4; k++) {
-    uint64_t a, b, c, e;
-    magic4(q[k] & 0x0F0F0F0Fu, a, b);          // values 4k .. 4k + 3 (low nibbles)
-    magic4((q[k] >> 4) & 0x0F0F0F0Fu, c, e);   // values 16 + 4k .. 16 + 4k + 3 (high nibbles)
-    o16[2 * k] = bf16x2(mul2(add2(a, off), d));
-    o16[2 * k + 1] = bf16x2(mul2(add2(b, off), d));
-    o16[8 + 2 * k] = bf16x2(mul2(add2(c, off), d));
-    o16[8 + 2 * k + 1] = bf16x2(mul2(add2(e, off), d));
+    const uint32_t lo = q[k] & 0x0F0F0F0Fu, hi = q[k] & 0xF0F0F0F0u;
+    o16[2 * k] = bf16x2(fma2(under2<0x43u, 2>(lo, 0, 1), d, clo));  // values 4k, 4k + 1 (low nibbles)
+    o16[2 * k + 1] = bf16x2(fma2(under2<0x43u, 2>(lo, 2, 3), d, clo));
+    o16[8 + 2 * k] = bf16x2(fma2(under2<0x45u, 1>(hi, 0, 1), d, chi));  // values 16 + 4k, .. (high nibbles)
+    o16[8 + 2 * k + 1] = bf16x2(fma2(under2<0x45u, 1>(hi, 2, 3), d, chi));
   }
 }
 
@@ -310,7 +330,8 @@ __device__ __forceinline__ void dq_q4_1_block(const uint32_t* w, int o, uint32_t
   }
 }
 
-// Q8_0 block at byte o: 32 values d q (q int8: biased by 128 into a byte, then the magic)
+// Q8_0 block at byte o: 32 values d q (q int8: biased by 128 into a byte, then the magic). (Q4_0's fused
+// multiply-add form, (32768 + b) d - 32896 d, is exact here too, but measured slower: config 3 0.596 -> 0.64 ms.)
 __device__ __forceinline__ void dq_q8_0_block(const uint32_t* w, int o, uint32_t* o16) {
   const uint64_t d = dup2(half_at(w, o)), off = dup2(-8388736.0f);  // -(2^23 + 128)
 #pragma unroll
