@@ -112,14 +112,30 @@ int expert_path(const artlite_moe& h, int64_t P, const artlite_moe::Layer& L) {
   return P >= 4 * (int64_t)h.E_local ? 2 : 1;
 }
 
+// the norm done inside the kernel that first reads the rows (ARTLITE_NORM_FUSE=0: the norm kernel first, always;
+// read at each forward, so that a benchmark can time both in one process)
+static bool norm_fusion_on() {
+  const char* v = getenv("ARTLITE_NORM_FUSE");
+  return !(v && v[0] == '0');
+}
+
+int run_norm(artlite_moe* h, const NormIn& n, void* xn, int64_t T, cudaStream_t st) {
+  return launch_norm(n.x, h->d.act_dtype, n.w, n.w_dtype, n.eps, T, h->d.hidden, xn, st);
+}
+
 int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* xd, int64_t T, cudaStream_t st,
-                       Marker& mk, int mult_gu, int mult_dn) {
+                       Marker& mk, int mult_gu, int mult_dn, const NormIn* norm) {
   const artlite_moe_desc& d = h->d;
   const int H = d.hidden, E = d.n_experts, K = d.top_k;
   if (T > 0) {
+    // the norm in the CTA-per-expert router where it applies, else the norm kernel first
+    const bool fuse = norm && router_small_ok(T, H) && router_small_norms(T, H, d.act_dtype) && norm_fusion_on();
+    if (norm && !fuse) AL_TRY(run_norm(h, *norm, const_cast<void*>(xd), T, st));
+    NormFuse nf{};
+    if (fuse) nf = {norm->x, norm->w, norm->w_dtype, norm->eps};
     if (router_small_ok(T, H))
       AL_TRY(launch_router_small(xd, d.act_dtype, L.router.ptr, L.router_qtype, L.has_bias ? L.bias.as<float>() : nullptr,
-                                 T, H, E, h->logits.as<float>(), st));
+                                 T, H, E, h->logits.as<float>(), st, fuse ? &nf : nullptr));
     else if (L.n_planes)
       AL_TRY(launch_router_tc(static_cast<const uint16_t*>(xd), L.planes.as<uint16_t>(), L.n_planes,
                               L.has_bias ? L.bias.as<float>() : nullptr, T, H, E, T, h->logits.as<float>(),
@@ -495,24 +511,33 @@ int artlite_moe_forward(artlite_moe* h, int layer, const void* x, void* y, int64
   void* yd = y_dev ? y : h->yout.ptr;
   Marker mk{h, layer, st};
   AL_TRY(mk.mark());
-  const void* res = nullptr;  // (a layer with a norm: its input, added back to the output)
+  // a layer with a norm: its input is added back to the output (res); the normed rows go to xn, normed by the first
+  // kernel that reads them where it can (the fused decode kernel, the CTA-per-expert router), else by the norm kernel
+  const void* res = nullptr;
+  NormIn norm;
   if (L.has_norm && T > 0) {
-    AL_TRY(launch_norm(xd, d.act_dtype, L.norm_w.ptr, L.norm_dtype, L.norm_eps, T, H, h->xn.ptr, st));
+    norm = NormIn{xd, L.norm_w.ptr, L.norm_dtype, L.norm_eps};
     res = xd;
     xd = h->xn.ptr;
   }
+  const NormIn* nin = norm.x ? &norm : nullptr;
   if (h->E_local < E) {
+    if (nin) AL_TRY(run_norm(h, norm, h->xn.ptr, T, st));
     AL_TRY(ep_forward(h, layer, xd, yd, T, st, mk, res));
   } else {
     const int path = expert_path(*h, P, L);
     h->last_path = path;
     h->paths[layer] = path;
     if (path == 1 && decode_fused_ok(*h, L, T)) {
-      AL_TRY(launch_decode(h, L, xd, yd, T, st, res));
+      if (nin && !norm_fusion_on()) {
+        AL_TRY(run_norm(h, norm, h->xn.ptr, T, st));
+        nin = nullptr;
+      }
+      AL_TRY(launch_decode(h, L, xd, yd, T, st, res, nin));
     } else {
       int mult_gu, mult_dn;
       small_plan(*h, L, path, T, &mult_gu, &mult_dn);
-      AL_TRY(route_and_dispatch(h, L, xd, T, st, mk, mult_gu, mult_dn));
+      AL_TRY(route_and_dispatch(h, L, xd, T, st, mk, mult_gu, mult_dn, nin));
       void* yrows;
       int ydt;
       AL_TRY(run_experts(h, routed_weights(L), path, xd, d.act_dtype, false, h->perm.as<int32_t>(), K, P, E,

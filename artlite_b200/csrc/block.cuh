@@ -148,8 +148,20 @@ bool mss_use(const artlite_moe& h, const ExpertWeights& W, int path, int x_dtype
 // logits / ids / w / offsets / perm / slot / counts
 // mult_gu > 0: the decode-sized path (the small router when it applies, routing and dispatch in one kernel, which also
 // writes the GEMVs' unit scans: mult_gu / mult_dn items per expert and token group)
+// A layer's input norm, when the forward has one: the raw rows x, the weight w (H values of w_dtype) and eps; the
+// normed rows go to the handle's xn buffer, which the forward passes on as its x. The kernel that first reads the rows
+// norms them where it can (the fused decode kernel, the CTA-per-expert router); otherwise the norm kernel runs first.
+struct NormIn {
+  const void* x = nullptr;
+  const void* w = nullptr;
+  int w_dtype = 0;
+  double eps = 0;
+};
+int run_norm(artlite_moe* h, const NormIn& n, void* xn, int64_t T, cudaStream_t st);
+
+// norm (may be null): the layer's input norm, x its output buffer (the norm fused into the router where it can be)
 int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* x, int64_t T, cudaStream_t st,
-                       Marker& mk, int mult_gu = 0, int mult_dn = 0);
+                       Marker& mk, int mult_gu = 0, int mult_dn = 0, const NormIn* norm = nullptr);
 
 // F_run (0: the block's expert_ffn) the experts' width; y_out (null: the handle's y buffer) where the output rows go.
 // wexp (device, may be null): the weight expert of each of the E_run row groups (expert parallelism: a group is one
@@ -185,7 +197,8 @@ void ep_destroy(artlite_moe* h);
 
 // the fused decode-batch forward (decode.cu): whether it applies, and the launch (x, y device, act dtype)
 bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t T);
+// norm (may be null): the layer's input norm, done in the kernel's phase 0 with x its output buffer
 int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, void* y, int64_t T, cudaStream_t st,
-                  const void* res = nullptr);
+                  const void* res = nullptr, const NormIn* norm = nullptr);
 
 }  // namespace artlite

@@ -72,20 +72,6 @@ void DevBuf::release() {
 
 namespace {
 
-// the current device, restored on scope exit
-struct DeviceGuard {
-  int prev = -1;
-  int set(int dev) {
-    AL_CUDA(cudaGetDevice(&prev));
-    if (dev >= 0 && dev != prev) AL_CUDA(cudaSetDevice(dev));
-    return ARTLITE_OK;
-  }
-  ~DeviceGuard() {
-    int cur;
-    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-  }
-};
-
 // An argument buffer: used in place when it is device memory aligned to `align`, else staged in a device buffer.
 struct Arg {
   explicit Arg(DevBuf& b) : buf(b) {}

@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "norm.cuh"
 
 namespace artlite {
 
@@ -124,41 +125,13 @@ int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float*
                     out_dtype, own, sh, res);
 }
 
-// RMSNorm as the reference's float32 numpy (tests/np_ops.py:27-32): the mean of the squares in float64, x over
-// sqrt(mean + eps) in float64 rounded to float32, times w in float32; a CTA per row, stored in x's dtype
+// the layer's input norm as its own pass (norm.cuh): four rows a CTA (their loads, sums and reductions interleaved)
 __global__ void __launch_bounds__(256) norm_kernel(const void* x, int x_dtype, const void* w, int w_dtype, double eps,
-                                                   int H, void* out) {
-  __shared__ double part[8];
-  __shared__ double den;
+                                                   int64_t T, int H, void* out) {
   griddep_wait();
   griddep_launch();
-  const int64_t t = blockIdx.x;
-  double s = 0.0;
-  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
-    float v[8];
-    load8(x, x_dtype, t * H + c, v);
-#pragma unroll
-    for (int j = 0; j < 8; j++) s = fma((double)v[j], (double)v[j], s);
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double tot = 0.0;
-    for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += part[i];
-    den = sqrt(tot / H + eps);
-  }
-  __syncthreads();
-  const double d = den;
-  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
-    float v[8], g[8];
-    load8(x, x_dtype, t * H + c, v);
-    load8(w, w_dtype, c, g);
-#pragma unroll
-    for (int j = 0; j < 8; j++) v[j] = __fmul_rn((float)((double)v[j] / d), g[j]);
-    store8(out, x_dtype, t * H + c, v);
-  }
+  const int64_t r0 = (int64_t)blockIdx.x * 4;
+  nrm::norm_rows<4>(x, x_dtype, w, w_dtype, eps, H, r0, (int)min64(4, T - r0), out);
 }
 
 int launch_norm(const void* x, int x_dtype, const void* w, int w_dtype, double eps, int64_t T, int H, void* out,
@@ -166,7 +139,7 @@ int launch_norm(const void* x, int x_dtype, const void* w, int w_dtype, double e
   AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "norm: H %d (a multiple of 8)", H);
   AL_CHECK(w_dtype == ARTLITE_F32 || w_dtype == ARTLITE_BF16, ARTLITE_EINVAL, "norm: weight type %d", w_dtype);
   if (T == 0) return ARTLITE_OK;
-  return launch_pdl(norm_kernel, dim3((unsigned)T), dim3(256), 0, st, x, x_dtype, w, w_dtype, eps, H, out);
+  return launch_pdl(norm_kernel, dim3((unsigned)cdiv(T, 4)), dim3(256), 0, st, x, x_dtype, w, w_dtype, eps, T, H, out);
 }
 
 // a grid-stride loop over 16-byte chunks of the output rows (8 values each): row i of xp = token perm[i] / k of x

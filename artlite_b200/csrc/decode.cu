@@ -4,6 +4,8 @@
 // steps as the separate kernels of a forward, in phases separated by grid barriers (for Q4_K layers without a shared
 // expert, by default, the kernel ends after phase 3 and the small-batch down kernel of mss.cu and the combine follow
 // as two more launches: faster than phases 4-5 here, and the only way for Q6_K downs):
+//   0. with the layer's input norm: CTA b norms rows b, b + G, .. of the raw input into x (norm.cuh, the norm kernel's
+//      arithmetic), one count a row; every CTA waits for all T rows (bounded), so no norm launch precedes the kernel;
 //   1. router logits (router.cu's semantics: fp32 products, fp32 sums, + bias): register-blocked 4 tokens x 4 experts
 //      a warp over a quarter of H (router_tiles), or a warp per (token, expert) for other shapes; for Q4_K also the
 //      tokens' x in the streaming GEMV's fragment order (ms.cuh);
@@ -26,6 +28,7 @@
 #include "kernels.cuh"
 #include "route.cuh"
 #include "ms.cuh"
+#include "norm.cuh"
 #include "rq.cuh"
 
 namespace artlite {
@@ -38,7 +41,8 @@ constexpr long long kBarrierCycles = 4000000000LL;  // about 2 s
 
 struct GridBar {
   unsigned count, gen;
-  unsigned pad[14];
+  unsigned norm_cnt;  // rows normed in this launch (phase 0; zeroed by CTA 0 after barrier 1)
+  unsigned pad[13];
   int tb_done[kMaxPairs / 4];  // per block of 4 tokens: router units finished (the last one routes the tokens)
 };
 
@@ -101,6 +105,11 @@ struct DecodeArgs {
   int32_t *counts, *perm, *slot;
   float *h, *y;
   const void* res;  // rows added last to the output (the residual of a layer with a norm), or null
+  // a layer's input norm (x_in set): phase 0 norms the raw rows x_in into x (norm.cuh), CTA b rows b, b + G, ..
+  const void* x_in;
+  const void* norm_w;
+  int norm_dtype;
+  double norm_eps;
   // the shared expert (Q4_K, ref.shared_expert): its raw rows' maps, width, gate vector (fp32, or null: ungated), its
   // h rows (fragment order) and sums, its output rows (fp32, T x H), the per-token gates, 0 .. T - 1
   bool shared;
@@ -275,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     const int64_t rbytes = (int64_t)a.E * a.H * (a.router_dtype == ARTLITE_F32 ? 4 : 2);
     const int64_t xbytes = (int64_t)a.T * a.H * (a.x_dtype == ARTLITE_BF16 ? 2 : 4);
+    const void* xsrc = a.x_in ? a.x_in : a.x;
     const int64_t rc = ((rbytes + gridDim.x - 1) / gridDim.x + 15) & ~(int64_t)15;
     const int64_t r0 = rc * blockIdx.x;
     if (r0 < rbytes)
@@ -283,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     const int64_t xc = ((xbytes + gridDim.x - 1) / gridDim.x + 15) & ~(int64_t)15;
     const int64_t x0 = xc * blockIdx.x;
     if (x0 < xbytes)
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const uint8_t*>(a.x) + x0),
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const uint8_t*>(xsrc) + x0),
                    "r"((uint32_t)min64(xc, xbytes - x0)) : "memory");
   }
   griddep_wait();
@@ -303,6 +313,14 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
       *pp.issued = 0;
       *pp.failed = 0;
     }
+  }
+  // ---- 0. the layer's input norm: the rows normed into x, every CTA waits for all T (one count a row)
+  if (a.x_in) {
+    unsigned mine = 0;
+    for (int t = blockIdx.x; t < a.T; t += gridDim.x, mine++)
+      nrm::norm_rows<1>(a.x_in, a.x_dtype, a.norm_w, a.norm_dtype, a.norm_eps, a.H, t, 1, const_cast<void*>(a.x));
+    nrm::norm_publish(&a.bar->norm_cnt, mine);
+    if (!nrm::norm_wait(&a.bar->norm_cnt, (unsigned)a.T, a.status, 8)) return;
   }
   // ---- 1. router logits (and the tokens' x in fragment order)
   const bool tiles = a.H % 512 == 0 && E % 4 == 0;
@@ -349,6 +367,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     }
   }
   if (!grid_sync(a.bar, a.status, 1)) return;
+  if (a.x_in && blockIdx.x == 0 && threadIdx.x == 0) atomicExch(&a.bar->norm_cnt, 0u);  // (every CTA is past its wait)
   // ---- 2. routing and the dispatch
   const bool local = a.T <= rq::kWarps;  // every CTA routes all tokens itself
   {
@@ -602,7 +621,7 @@ bool decode_fused_ok(const artlite_moe& h, const artlite_moe::Layer& L, int64_t 
 }
 
 int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, void* y, int64_t T, cudaStream_t st,
-                  const void* res) {
+                  const void* res, const NormIn* norm) {
   const artlite_moe_desc& d = h->d;
   if (!h->bar.ptr) {
     AL_TRY(h->bar.reserve(sizeof(GridBar)));
@@ -653,6 +672,12 @@ int launch_decode(artlite_moe* h, const artlite_moe::Layer& L, const void* x, vo
   a.y = h->y.as<float>();
   a.out = y;
   a.res = res;
+  if (norm) {
+    a.x_in = norm->x;
+    a.norm_w = norm->w;
+    a.norm_dtype = norm->w_dtype;
+    a.norm_eps = norm->eps;
+  }
   a.bar = h->bar.as<GridBar>();
   a.status = h->status.as<DevStatus>();
   a.shared = L.has_shared;

@@ -82,8 +82,19 @@ int launch_router(const void* x, int x_dtype, const void* w, int w_dtype, const 
 // the same for decode-sized batches (T <= kRouterSmallTokens, H % 4 == 0): a warp per (token, expert) over the grid
 constexpr int kRouterSmallTokens = 256;
 bool router_small_ok(int64_t T, int H);
+// a layer's input norm done by the kernel that first reads its rows (norm.cuh): x_in the raw rows, w (H values of
+// w_dtype) and eps the norm; the normed rows go to the kernel's x buffer
+struct NormFuse {
+  const void* x_in;
+  const void* w;
+  int w_dtype;
+  double eps;
+};
+// whether launch_router_small can norm its rows itself (the CTA-per-expert form, H % 256 == 0 and T <= 16, with the
+// batch's rows in a CTA's shared memory: at most 128 KiB)
+bool router_small_norms(int64_t T, int H, int x_dtype);
 int launch_router_small(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H,
-                        int E, float* logits, cudaStream_t st);
+                        int E, float* logits, cudaStream_t st, const NormFuse* norm = nullptr);
 
 // ---------------------------------------------------------------- gemv.cu (CUDA-core dequant path)
 struct ExpertGemvArgs {

@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "norm.cuh"
 
 namespace artlite {
 
@@ -131,7 +132,7 @@ __device__ __forceinline__ void load8(const void* p, int dtype, int64_t i, float
   }
 }
 
-// The same for H % 256 == 0: a CTA per expert, its 8 warps splitting H (each lane 8 consecutive values of every
+// The same for H % 256 == 0 and T <= 16: a CTA per expert, its 8 warps splitting H (each lane 8 consecutive values of every
 // 256-wide slice its warp owns), tokens in chunks of 8. The router row is read once per CTA and every expert's CTA
 // runs at once, so a one-token batch's 1 MB of router weights is read by E SMs in one round of loads; the warps'
 // partial sums meet in shared memory and add in a fixed order, + bias.
@@ -148,7 +149,7 @@ __device__ __forceinline__ void router_cta_expert(const void* x, int x_dtype, co
       for (int i = 0; i < 8; i++) {
         if (t0 + i < T) {
           float xv[8];
-          load8(x, x_dtype, (t0 + i) * H + c, xv);
+          nrm::ld8p(x, x_dtype, (t0 + i) * H + c, xv);  // (global rows, or the CTA's normed rows in shared memory)
 #pragma unroll
           for (int j = 0; j < 8; j++) acc[i] = fmaf(wv[j], xv[j], acc[i]);
         }
@@ -172,23 +173,48 @@ __device__ __forceinline__ void router_cta_expert(const void* x, int x_dtype, co
   }
 }
 
+// With the layer's input norm (norm.x_in set): every CTA norms the batch's raw rows into its own shared memory
+// (norm.cuh norm_rows_cta: the T rows are a few KB each, so the copy per CTA is cheaper than any wait for another
+// CTA) and reads them from there; CTA b < T also stores normed row b to x for the kernels that follow
 __global__ void __launch_bounds__(256) router_cta_kernel(const void* x, int x_dtype, const void* w, int w_dtype,
-                                                         const float* bias, int64_t T, int H, int E, float* logits) {
+                                                         const float* bias, int64_t T, int H, int E, float* logits,
+                                                         NormFuse norm) {
+  extern __shared__ __align__(16) uint8_t xsm[];
   __shared__ float part[8][8];
   griddep_wait();
   griddep_launch();
-  for (int e = blockIdx.x; e < E; e += gridDim.x) router_cta_expert(x, x_dtype, w, w_dtype, bias, T, H, E, logits, e, part);
+  const void* xr = x;
+  if (norm.x_in) {
+    const int64_t rb = (int64_t)H * (w_dtype == ARTLITE_F32 ? 4 : 2);  // (H % 256 == 0: a multiple of 16 bytes)
+    if (threadIdx.x == 0 && blockIdx.x < E)  // the expert's router row into L2 while the rows are normed
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const uint8_t*>(w) + blockIdx.x * rb),
+                   "r"((uint32_t)rb) : "memory");
+    nrm::norm_rows_cta(norm.x_in, x_dtype, norm.w, norm.w_dtype, norm.eps, H, (int)T, xsm,
+                       blockIdx.x < T ? (int)blockIdx.x : -1, const_cast<void*>(x));
+    xr = xsm;
+  }
+  for (int e = blockIdx.x; e < E; e += gridDim.x) router_cta_expert(xr, x_dtype, w, w_dtype, bias, T, H, E, logits, e, part);
 }
 
 bool router_small_ok(int64_t T, int H) { return T <= kRouterSmallTokens && H % 4 == 0; }
+constexpr int kNormSmem = 128 * 1024;
+bool router_small_norms(int64_t T, int H, int x_dtype) {
+  return T <= nrm::kRowsCta && H % 256 == 0 && T * H * (x_dtype == ARTLITE_BF16 ? 2 : 4) <= kNormSmem;
+}
 
 int launch_router_small(const void* x, int x_dtype, const void* w, int w_dtype, const float* bias, int64_t T, int H,
-                        int E, float* logits, cudaStream_t st) {
+                        int E, float* logits, cudaStream_t st, const NormFuse* norm) {
   AL_CHECK(router_small_ok(T, H), ARTLITE_EINVAL, "router_small: T %lld H %d", (long long)T, H);
+  AL_CHECK(!norm || router_small_norms(T, H, x_dtype), ARTLITE_EINVAL, "router_small: no fused norm at T %lld H %d",
+           (long long)T, H);
   if (T == 0) return ARTLITE_OK;
-  if (H % 256 == 0 && T <= 16)
-    return launch_pdl(router_cta_kernel, dim3((unsigned)E), dim3(256), 0, st, x, x_dtype, w, w_dtype, bias, T, H, E,
-                      logits);
+  if (H % 256 == 0 && T <= 16) {
+    const size_t smem = norm ? (size_t)T * H * (x_dtype == ARTLITE_BF16 ? 2 : 4) : 0;
+    if (smem > 48 * 1024)
+      AL_CUDA(cudaFuncSetAttribute(router_cta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kNormSmem));
+    return launch_pdl(router_cta_kernel, dim3((unsigned)E), dim3(256), smem, st, x, x_dtype, w, w_dtype, bias, T, H, E,
+                      logits, norm ? *norm : NormFuse{});
+  }
   const int64_t warps = T * E;
   const unsigned grid = (unsigned)std::min<int64_t>(cdiv(warps, 8), (int64_t)kNumSMs * 8);
   return launch_pdl(router_small_kernel, dim3(grid), dim3(256), 0, st, x, x_dtype, w, w_dtype, bias, T, H, E, logits);

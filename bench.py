@@ -353,10 +353,10 @@ def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "a
     """benchmark config 2 on one GPU: decode batches B = 1, 4, 16, 64 of the Q4_K block (bf16 x), each forward a CUDA
     graph, over `layers` layers in turn (their touched experts far exceed L2). One dict per B: tokens/s, and the
     HBM roofline of the bytes a forward must read (U touched experts x 2,654,208 B + the fp32 router 1,048,576 B).
-    `shape` (H, E, K, F and a shared expert's Fs; "down": "Q6_K" for the Q4_K_M layout, Q4_K gate / up with Q6_K downs)
-    measures another block shape the same way (the shared expert's rows and its gate vector are part of every
-    forward's bytes). The block's device status word is read after the timed steps (raises on a kernel-reported
-    error)."""
+    `shape` (H, E, K, F and a shared expert's Fs; "down": "Q6_K" for the Q4_K_M layout, Q4_K gate / up with Q6_K downs;
+    "norm": each layer with its input norm and residual, artlite_moe_set_norm) measures another block shape the same
+    way (the shared expert's rows and its gate vector are part of every forward's bytes). The block's device status
+    word is read after the timed steps (raises on a kernel-reported error)."""
     import torch
     from artlite_b200.moe.block import MoEBlock
     dev = torch.device("cuda", 0)
@@ -393,6 +393,10 @@ def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "a
         router = torch.randn((e_, h_), generator=g, device=dev) * 0.02
         block.set_weights(layer, gate=gate.data_ptr(), up=up.data_ptr(), down=down.data_ptr(),
                           router=router.data_ptr(), qtype="Q4_K", down_qtype=dq)
+        if sh.get("norm"):  # (the layer's input norm and residual: y = x + moe(rms_norm(x, w)))
+            wn = 1.0 + 0.1 * torch.randn((h_,), generator=g, device=dev)
+            block.set_norm(layer, wn.data_ptr(), eps=1e-6, dtype="F32")
+            del wn
         if fs:
             sg, su, sd = q4k(fs, h_), q4k(fs, h_), q4k(h_, fs)
             ginp = torch.randn((h_,), generator=g, device=dev) * 0.02
@@ -432,7 +436,8 @@ def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "a
         ms_layer = e0.elapsed_time(e1) / (steps * L)
         U = float(np.mean(touched))
         per_expert = 2 * f_ * h_ * 144 // 256 + f_ * h_ * (210 if dq == "Q6_K" else 144) // 256  # (bytes per 256)
-        nbytes = U * per_expert + e_ * h_ * 4 + (3 * fs * h_ * 144 // 256 + h_ * 4 if fs else 0)
+        nbytes = U * per_expert + e_ * h_ * 4 + (3 * fs * h_ * 144 // 256 + h_ * 4 if fs else 0) + \
+            (h_ * 4 if sh.get("norm") else 0)
         gbs = nbytes / (ms_layer / 1000.0) / 1e9
         out.append({"workload": f"{sh['name']}-b{B}", "batch": B, "us_per_layer": ms_layer * 1000.0,
                     "tokens_per_s": B / (ms_layer / 1000.0), "experts_touched": U,
@@ -447,8 +452,11 @@ def measure_decode(batches, layers: int, steps: int, warmup: int, path: str = "a
 
 
 def run_decode(args) -> None:
-    for line in measure_decode(args.batches, args.layers, args.steps, args.warmup, args.path,
-                               QWEN35 if args.qwen35 else Q4KM if args.q4_k_m else None):
+    shape = QWEN35 if args.qwen35 else Q4KM if args.q4_k_m else None
+    if args.norm:
+        shape = dict(shape or {"name": "decode-q4_k", "H": H, "E": E, "K": K, "F": F, "Fs": 0}, norm=True)
+        shape["name"] += "-norm"
+    for line in measure_decode(args.batches, args.layers, args.steps, args.warmup, args.path, shape):
         print(json.dumps(line), flush=True)
 
 
@@ -467,6 +475,7 @@ def main() -> None:
     ap.add_argument("--decode", action="store_true", help="benchmark config 2 (decode batches, Q4_K) instead")
     ap.add_argument("--qwen35", action="store_true", help="with --decode: the qwen35moe shape (E 256, F 512, shared)")
     ap.add_argument("--q4-k-m", action="store_true", help="with --decode: Q4_K gate / up with Q6_K downs")
+    ap.add_argument("--norm", action="store_true", help="with --decode: each layer with its input norm and residual")
     ap.add_argument("--config", type=int, choices=[3, 5], help="benchmark config 3 or 5 (one GPU) instead")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"], help="expert path of --decode")
     ap.add_argument("--batches", type=int, nargs="+", default=[1, 4, 16, 64], help="decode batches of --decode")
@@ -625,6 +634,18 @@ def main() -> None:
             f"B{d['batch']}": {k: d[k] for k in ("us_per_layer", "tokens_per_s", "experts_touched", "roofline", "path",
                                                  "layers", "steps", "clocks")}
             for d in measure_decode([1, 16, 64], 8, 20, 3, shape=Q4KM)}
+        # the qwen35moe layer with its input norm and residual: the norm inside the first kernel that reads the rows,
+        # and (ARTLITE_NORM_FUSE=0) the norm kernel first
+        qn = dict(QWEN35, name="qwen35moe-norm", norm=True)
+        extras["qwen35moe_decode_norm"] = {
+            f"B{d['batch']}": {k: d[k] for k in ("us_per_layer", "tokens_per_s", "roofline", "path", "clocks")}
+            for d in measure_decode([1, 16, 64], 8, 20, 3, shape=qn)}
+        os.environ["ARTLITE_NORM_FUSE"] = "0"
+        try:
+            extras["qwen35moe_decode_norm_kernel"] = {f"B{d['batch']}": {"us_per_layer": d["us_per_layer"]}
+                                                      for d in measure_decode([1, 16, 64], 8, 20, 3, shape=qn)}
+        finally:
+            del os.environ["ARTLITE_NORM_FUSE"]
         c3 = measure_config(3, 4, 10, 3)[0]
         extras["config3"] = {k: c3.get(k) for k in ("workload", "ms_per_layer", "tokens_per_s", "path", "roofline",
                                                     "layer_roofline", "stage_ms_mean", "layers", "steps", "clocks")}

@@ -245,11 +245,14 @@ def test_forward_graph_matches_forward(path, T):
     b.close()
 
 
-@pytest.mark.parametrize("path,T,act", [("tc", 300, "bf16"), ("gemv", 5, "bf16"), ("gemv", 24, "bf16"), ("gemv", 16, "f32")])
+@pytest.mark.parametrize("path,T,act", [("tc", 300, "bf16"), ("gemv", 1, "bf16"), ("gemv", 5, "bf16"),
+                                        ("gemv", 24, "bf16"), ("gemv", 64, "bf16"), ("gemv", 3, "f32"),
+                                        ("gemv", 16, "f32")])
 def test_norm_and_residual(path, T, act):
     """A layer with its input norm and residual (artlite_moe_set_norm): y = x + moe(rms_norm(x, w, eps)), against
     np_ops.rms_norm restated and ref.moe_ffn on the normed rows (rounded to the activation dtype, as the block routes
-    and computes on them); the separate kernels, the small-batch and fused decode kernels and the tcgen05 path."""
+    and computes on them); the norm in the CTA-per-expert router (T <= 16 below the fused kernel) and in the fused
+    decode kernel's first phase, and the norm kernel before the tcgen05 path."""
     qtype = "Q4_K" if act == "bf16" else "Q4_0"
     layer, x, _ = moe_np.make_block(80 + T, T, qtype=qtype, E=16, H=512, F=256, x_bf16=act == "bf16")
     wn = (1.0 + 0.1 * np.random.default_rng(5).standard_normal(layer.H)).astype(np.float32)
@@ -269,6 +272,79 @@ def test_norm_and_residual(path, T, act):
     want = xf + moe_np.moe_ffn(xn, ids, w, expert_fn(layer))
     got = moe_np.bf16_to_f32(y) if act == "bf16" else y
     assert moe_np.rel_max(got, want) <= (BF16_TOL if act == "bf16" or path == "tc" else FP32_TOL)
+
+
+@pytest.mark.parametrize("act", ["f32", "bf16"])
+@pytest.mark.parametrize("T", [1, 5, 12, 16, 40, 300])
+def test_norm_rows_exact(act, T):
+    """The normed rows bit for bit against np_ops.rms_norm restated: a router equal to the identity (E = H = 256) makes
+    each logit one normed value exactly, on every path that norms: the CTA-per-expert router (up to 16 tokens below the
+    fused kernel), the fused decode kernel's phase 0, the norm kernel (prefill sizes). Random rows, and (f32) rows of
+    equal values under an eps sweep that puts v / d within a few float64 units of a float32 midpoint, where the norm's
+    one-product division must fall back to the division itself."""
+    import dataclasses
+    layer, x, _ = moe_np.make_block(900 + T, T, qtype="Q4_0", E=256, H=256, F=256, x_bf16=act == "bf16")
+    layer = dataclasses.replace(layer, router=np.eye(256, dtype=np.float32))
+    b = make_block(layer, T, act=act, path="auto")
+    wn = (1.0 + 0.1 * np.random.default_rng(9).standard_normal(256)).astype(np.float32)
+    b.set_norm(0, wn, eps=1e-6)
+    b.forward(x)
+    want = moe_np.rms_norm(x_f32(x), wn, 1e-6)
+    if act == "bf16":
+        want = moe_np.bf16_to_f32(moe_np.to_bf16_bits(want))
+    assert np.array_equal(b.debug(T)["logits"].view(np.uint32), want.view(np.uint32))
+    if act == "f32":
+        x3 = np.full((T, 256), 3.0, np.float32)
+        ones = np.ones(256, np.float32)
+        for j in range(0, 26):
+            eps = 9.0 * 2.0 ** -24 + j * 2.0 ** -49
+            b.set_norm(0, ones, eps=eps)
+            b.forward(x3)
+            want = moe_np.rms_norm(x3, ones, eps)
+            assert np.array_equal(b.debug(T)["logits"].view(np.uint32), want.view(np.uint32)), j
+    b.close()
+
+
+def _norm_case(qtype, down, act, T, shared):
+    layer, x, _ = moe_np.make_block(500 + T, T, qtype=qtype, down_qtype=down or "", E=16, H=512, F=256,
+                                    x_bf16=act == "bf16")
+    b = make_block(layer, T, act=act, path="gemv")
+    b.set_norm(0, (1.0 + 0.1 * np.random.default_rng(6).standard_normal(layer.H)).astype(np.float32), eps=1e-5)
+    if shared:
+        rng = np.random.default_rng(7)
+        b.set_shared(0, gate=moe_np.random_blocks(rng, "Q4_K", 256, 512), up=moe_np.random_blocks(rng, "Q4_K", 256, 512),
+                     down=moe_np.random_blocks(rng, "Q4_K", 512, 256), ffn=256, qtype="Q4_K",
+                     gate_inp=(rng.standard_normal(512) * 0.02).astype(np.float32))
+    return b, x
+
+
+@pytest.mark.parametrize("qtype,down,act,T,shared", [
+    ("Q4_K", None, "bf16", 1, False), ("Q4_K", None, "bf16", 5, False), ("Q4_K", None, "bf16", 16, False),
+    ("Q4_K", None, "bf16", 40, False), ("Q4_K", "Q6_K", "bf16", 16, False), ("Q4_K", None, "bf16", 4, True),
+    ("Q4_0", None, "f32", 3, False), ("Q4_0", None, "f32", 12, False), ("Q8_0", None, "bf16", 24, False)])
+def test_norm_fused_equals_norm_kernel(monkeypatch, qtype, down, act, T, shared):
+    """The norm done inside the kernel that first reads the rows (the CTA-per-expert router, the fused decode
+    kernel's phase 0; with a shared expert and a Q6_K down too) gives the norm kernel's output bit for bit
+    (ARTLITE_NORM_FUSE=0: the norm kernel first), on repeated forwards and on graph replays (the norm's counters
+    start from zero every launch)."""
+    import torch
+    b, x = _norm_case(qtype, down, act, T, shared)
+    monkeypatch.setenv("ARTLITE_NORM_FUSE", "0")
+    want = b.forward(x)
+    want_lg = b.debug(T)["logits"]
+    monkeypatch.delenv("ARTLITE_NORM_FUSE")
+    for _ in range(3):
+        got = b.forward(x)
+        assert np.array_equal(got.view(np.uint32 if act == "f32" else np.uint16),
+                              want.view(np.uint32 if act == "f32" else np.uint16))
+        assert np.array_equal(b.debug(T)["logits"].view(np.uint32), want_lg.view(np.uint32))
+    xd = torch.from_numpy(x.view(np.int16 if act == "bf16" else np.int32)).cuda()
+    yd = torch.empty_like(xd)
+    for _ in range(3):
+        b.forward_graph(xd.data_ptr(), yd.data_ptr(), T)
+        b.sync()
+        assert np.array_equal(yd.cpu().numpy(), want.view(np.int16 if act == "bf16" else np.int32))
+    b.close()
 
 
 @pytest.mark.parametrize("T,gated", [(16, True), (64, True), (24, False)])
