@@ -157,6 +157,7 @@ int route_and_dispatch(artlite_moe* h, const artlite_moe::Layer& L, const void* 
   da.slot = h->slot.as<int32_t>();
   da.counts = h->counts.as<int32_t>();
   da.status = h->status.as<DevStatus>();
+  da.blk_pairs = kDispatchBlockPairsFwd;
   if (mult_gu > 0 && T > 0) {  // decode-sized: one kernel, with the GEMVs' unit scans
     da.unit_rows = kGemvTokens;
     da.unit_mult = mult_gu;
@@ -398,7 +399,7 @@ int artlite_moe_create(const artlite_moe_desc* desc, artlite_moe** out) {
   AL_TRY(h->perm.reserve(sizeof(int32_t) * P));
   AL_TRY(h->slot.reserve(sizeof(int32_t) * P));
   AL_TRY(h->counts.reserve(sizeof(int32_t) * E));
-  AL_TRY(h->blk.reserve(dispatch_scratch_bytes(P, E)));
+  AL_TRY(h->blk.reserve(dispatch_scratch_bytes(P, E, kDispatchBlockPairsFwd)));
   AL_TRY(h->unit_gu.reserve(sizeof(int32_t) * (E + 1)));
   AL_TRY(h->unit_dn.reserve(sizeof(int32_t) * (E + 1)));
   AL_TRY(h->status.reserve(sizeof(DevStatus)));

@@ -1,13 +1,17 @@
 // Dispatch: the (token, slot) pairs grouped by expert, stable in pair order, as moe_plan's histogram / prefix scan /
-// permute (csrc/artlite/moe_host.cpp:203-215), in three kernels over blocks of kDispatchBlockPairs pairs:
+// permute (csrc/artlite/moe_host.cpp:203-215), in three kernels over blocks of blk_pairs pairs (4096; the forward's
+// 1024, for more CTAs and fewer rounds a CTA):
 //   count   per block, a shared-memory histogram of its pairs' experts (ids checked: an id outside [0, E) is reported
 //           through the status word as moe_plan's "expert id {x} of {E}" error, :247);
-//   scan    per expert the exclusive scan over blocks, then over experts (offsets), the units of work per expert and
-//           their scan, the compacted list of experts with pairs;
+//   scan    per expert the exclusive scan over blocks (segments of blocks summed in parallel, the segments' prefix,
+//           then each segment's blocks in order), then over experts (offsets), the units of work per expert and their
+//           scan, the compacted list of experts with pairs;
 //   rank    per block, in rounds of 256 pairs in order: within a warp the rank among lanes of the same expert
 //           (__match_any_sync), across the round's warps a prefix of per-warp counts, across rounds a running count:
 //           a pair's place = offsets[e] + block base[e] + running[e] + warp prefix + lane rank (stable).
 // Then the reference plan's chunk deal (moe_host.cpp:216-234) for the drop-in artlite_moe_plan.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "route.cuh"
@@ -15,17 +19,21 @@
 namespace artlite {
 
 
-size_t dispatch_scratch_bytes(int64_t P, int E) {
-  const int64_t nblk = P ? cdiv(P, kDispatchBlockPairs) : 1;
+size_t dispatch_scratch_bytes(int64_t P, int E, int blk_pairs) {
+  const int64_t nblk = P ? cdiv(P, blk_pairs) : 1;
   return sizeof(int32_t) * (size_t)nblk * E;
+}
+
+__device__ __forceinline__ int64_t blk_pairs(const DispatchArgs& a) {
+  return a.blk_pairs ? a.blk_pairs : kDispatchBlockPairs;
 }
 
 __global__ void __launch_bounds__(512) dispatch_count(DispatchArgs a) {
   extern __shared__ int32_t hist[];
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
-  const int64_t p0 = (int64_t)blockIdx.x * kDispatchBlockPairs;
-  const int64_t p1 = min(p0 + kDispatchBlockPairs, a.P);
+  const int64_t p0 = (int64_t)blockIdx.x * blk_pairs(a);
+  const int64_t p1 = min(p0 + blk_pairs(a), a.P);
   for (int64_t p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
     const int32_t x = a.ids[p];
     if (x < 0 || x >= a.E)
@@ -37,38 +45,57 @@ __global__ void __launch_bounds__(512) dispatch_count(DispatchArgs a) {
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) a.blk_counts[(int64_t)blockIdx.x * a.E + e] = hist[e];
 }
 
+// threads (segment sg, expert e): blockDim.x = Ep nseg (Ep = E rounded up to 32); segment sg takes blocks
+// [sg per, (sg + 1) per): its total, the segments' prefix per expert, then its blocks' exclusive counts in place
 __global__ void __launch_bounds__(1024) dispatch_scan(DispatchArgs a, int nblk) {
   __shared__ int64_t s64[32];
   __shared__ int32_t s32[32];
-  const int e = threadIdx.x;  // blockDim.x >= E
-  int64_t run = 0;
+  __shared__ int64_t seg[1024];
+  const int Ep = (a.E + 31) & ~31, nseg = blockDim.x / Ep;
+  const int e = threadIdx.x % Ep, sg = threadIdx.x / Ep;
+  const int per = (nblk + nseg - 1) / nseg, b0 = min(nblk, sg * per), b1 = min(nblk, b0 + per);
+  int32_t* col = a.blk_counts + e;
+  int64_t t = 0;
+  if (e < a.E) {
+#pragma unroll 4
+    for (int b = b0; b < b1; b++) t += col[(int64_t)b * a.E];
+  }
+  seg[threadIdx.x] = t;
+  __syncthreads();
+  int64_t run = 0, pre = 0;  // (run: all segments, pre: those before sg)
+  for (int s2 = 0; s2 < nseg; s2++) {
+    const int64_t v = seg[s2 * Ep + e];
+    run += v;
+    if (s2 < sg) pre += v;
+  }
   if (e < a.E)
-    for (int b = 0; b < nblk; b++) {
-      int32_t* c = a.blk_counts + (int64_t)b * a.E + e;
-      const int32_t v = *c;
-      *c = (int32_t)run;
-      run += v;
+    for (int b = b0; b < b1; b++) {
+      const int32_t v = col[(int64_t)b * a.E];
+      col[(int64_t)b * a.E] = (int32_t)pre;
+      pre += v;
     }
+  if (sg > 0) run = 0;  // (the expert-level scans below: one value an expert, from segment 0's threads)
   int64_t tot64;
   const int64_t off = block_exclusive_scan<int64_t>(e < a.E ? run : 0, s64, &tot64);
-  if (e < a.E) {
+  const bool own = sg == 0 && e < a.E;
+  if (own) {
     a.offsets[e] = off;
     if (a.counts) a.counts[e] = (int32_t)run;
   }
-  if (e == 0) a.offsets[a.E] = tot64;
+  if (threadIdx.x == 0) a.offsets[a.E] = tot64;
   if (a.unit_off) {
-    const int32_t u = (e < a.E && a.unit_rows > 0) ? (int32_t)((run + a.unit_rows - 1) / a.unit_rows) * a.unit_mult : 0;
+    const int32_t u = (own && a.unit_rows > 0) ? (int32_t)((run + a.unit_rows - 1) / a.unit_rows) * a.unit_mult : 0;
     int32_t tot;
     const int32_t uo = block_exclusive_scan<int32_t>(u, s32, &tot);
-    if (e < a.E) a.unit_off[e] = uo;
-    if (e == 0) a.unit_off[a.E] = tot;
+    if (own) a.unit_off[e] = uo;
+    if (threadIdx.x == 0) a.unit_off[a.E] = tot;
   }
   if (a.active) {
     int32_t tot;
-    const int32_t has = (e < a.E && run > 0) ? 1 : 0;
+    const int32_t has = (own && run > 0) ? 1 : 0;
     const int32_t at = block_exclusive_scan<int32_t>(has, s32, &tot);
     if (has) a.active[at] = e;
-    if (e == 0) *a.n_active = tot;
+    if (threadIdx.x == 0) *a.n_active = tot;
   }
 }
 
@@ -79,8 +106,8 @@ __global__ void __launch_bounds__(256) dispatch_rank(DispatchArgs a) {
   for (int i = threadIdx.x; i < 9 * a.E; i += blockDim.x) sm[i] = 0;
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t p0 = (int64_t)blockIdx.x * kDispatchBlockPairs;
-  const int64_t p1 = min(p0 + kDispatchBlockPairs, a.P);
+  const int64_t p0 = (int64_t)blockIdx.x * blk_pairs(a);
+  const int64_t p1 = min(p0 + blk_pairs(a), a.P);
   const int32_t* base = a.blk_counts + (int64_t)blockIdx.x * a.E;
   const unsigned lt = (1u << lane) - 1u;
   for (int64_t r0 = p0; r0 < p1; r0 += 256) {
@@ -111,13 +138,14 @@ __global__ void __launch_bounds__(256) dispatch_rank(DispatchArgs a) {
 
 int launch_dispatch(const DispatchArgs& a, cudaStream_t st) {
   AL_CHECK(a.E >= 1 && a.E <= 1024, ARTLITE_EUNSUPPORTED, "dispatch: E %d (this build: E <= 1024)", a.E);
-  const int nblk = a.P ? (int)cdiv(a.P, kDispatchBlockPairs) : 0;
+  const int nblk = a.P ? (int)cdiv(a.P, a.blk_pairs ? a.blk_pairs : kDispatchBlockPairs) : 0;
   if (nblk) {
     dispatch_count<<<nblk, 512, a.E * sizeof(int32_t), st>>>(a);
     AL_LAUNCHED();
   }
-  const int threads = (int)cdiv(a.E, 32) * 32;
-  dispatch_scan<<<1, threads, 0, st>>>(a, nblk);
+  const int Ep = (int)cdiv(a.E, 32) * 32;
+  const int nseg = std::max(1, std::min(1024 / Ep, nblk));
+  dispatch_scan<<<1, Ep * nseg, 0, st>>>(a, nblk);
   AL_LAUNCHED();
   if (nblk) {
     const size_t smem = 9 * (size_t)a.E * sizeof(int32_t);

@@ -42,9 +42,11 @@ struct DispatchArgs {
   int32_t* active;
   int32_t* n_active;
   DevStatus* status;
+  int blk_pairs;  // pairs a block of the count and rank kernels (0: kDispatchBlockPairs)
 };
 constexpr int kDispatchBlockPairs = 4096;
-size_t dispatch_scratch_bytes(int64_t P, int E);
+constexpr int kDispatchBlockPairsFwd = 1024;  // the forward's: more blocks, fewer rounds a block
+size_t dispatch_scratch_bytes(int64_t P, int E, int blk_pairs = kDispatchBlockPairs);
 int launch_dispatch(const DispatchArgs& a, cudaStream_t st);
 // decode-sized batches: the routing (r) and the dispatch (a, its unit scan and a second one: mult2 / unit_off2) in one
 // CTA; r.ids is a.ids

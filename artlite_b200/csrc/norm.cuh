@@ -9,7 +9,6 @@
 #pragma once
 
 #include <cuda_bf16.h>
-#include <string.h>
 
 #include "common.cuh"
 
@@ -62,18 +61,17 @@ __device__ __forceinline__ void st8(void* p, int dtype, int64_t i, const float (
   }
 }
 
-// float(v / d) as the float64 division rounded to float32, from r = 1 / d (float64): q = v r is within 3 units in
-// the last place of the division's float64 result (two roundings of 2^-53 each against one), so both round to the
-// same float32 unless q lies within 4 units of a float32 rounding boundary (its 29 discarded bits within 4 of 2^28)
-// or outside the normal float32 range (tiny, huge, not finite): then the division itself. q = +-0 (v = +-0, or
-// d = inf) is the division's result exactly.
+// float(v / d) as the float64 division rounded to float32, from r = 1 / d (float64, correctly rounded; d positive,
+// normal and finite): q0 = v r, then two corrections q += (v - q d) r, each remainder by one fused multiply-add. The
+// first leaves q within one unit in the last place of v / d; from such a q and a correctly rounded reciprocal, one
+// correction gives the correctly rounded quotient (Markstein's theorem), so q2 is the division's float64 result bit for
+// bit, and its rounding to float32 the reference's. No overflow or underflow is reachable: v is a float, d lies in
+// [2^-149, 2^128]. For v = +-0 the corrections lose the zero's sign: q0 keeps it.
 __host__ __device__ __forceinline__ float div_to_f32(double v, double d, double r) {
-  const double q = v * r;
-  uint64_t b;
-  memcpy(&b, &q, sizeof b);
-  const uint32_t low = (uint32_t)b & 0x1FFFFFFFu, e = (uint32_t)(b >> 52) & 0x7FFu;
-  const bool fast = ((low - 0x0FFFFFFCu > 8u) && e >= 1023u - 125u && e <= 1023u + 126u) || (b << 1) == 0;
-  return fast ? (float)q : (float)(v / d);
+  const double q0 = v * r;
+  const double q1 = fma(fma(-q0, d, v), r, q0);
+  const double q2 = fma(fma(-q1, d, v), r, q1);
+  return (float)(q2 != 0.0 ? q2 : q0);
 }
 
 // rows r0 .. r0 + n - 1 (n <= G) of x normed into the same rows of out (and row `mine` also into out2, if set), by
@@ -115,7 +113,8 @@ __device__ __forceinline__ void norm_rows(const void* x, int x_dtype, const void
     for (int i = 0; i < 8; i++) tot += part[i][threadIdx.x];
     const double den = sqrt(tot / H + eps);
     dr[threadIdx.x][0] = den;
-    dr[threadIdx.x][1] = 1.0 / den;
+    dr[threadIdx.x][1] = 1.0 / den;  // (a row whose d is not positive, normal and finite: r = 0 marks the division)
+    if (!(den >= 0x1p-1022 && den <= 0x1.fffffffffffffp+1023)) dr[threadIdx.x][1] = 0.0;
   }
   __syncthreads();
   for (int c = threadIdx.x * 8; c < H; c += 256 * 8) {
@@ -127,8 +126,13 @@ __device__ __forceinline__ void norm_rows(const void* x, int x_dtype, const void
         const double d = dr[t][0], r = dr[t][1];
         float v[8];
         ld8p(x, x_dtype, (r0 + t) * H + c, v);
+        if (r != 0.0) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = __fmul_rn(div_to_f32(v[j], d, r), g[j]);
+          for (int j = 0; j < 8; j++) v[j] = __fmul_rn(div_to_f32(v[j], d, r), g[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) v[j] = __fmul_rn((float)((double)v[j] / d), g[j]);
+        }
         st8(out, x_dtype, (r0 + t) * H + c, v);
         if (out2 && r0 + t == mine) st8(out2, x_dtype, (r0 + t) * H + c, v);
       }

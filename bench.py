@@ -475,7 +475,8 @@ def main() -> None:
     ap.add_argument("--decode", action="store_true", help="benchmark config 2 (decode batches, Q4_K) instead")
     ap.add_argument("--qwen35", action="store_true", help="with --decode: the qwen35moe shape (E 256, F 512, shared)")
     ap.add_argument("--q4-k-m", action="store_true", help="with --decode: Q4_K gate / up with Q6_K downs")
-    ap.add_argument("--norm", action="store_true", help="with --decode: each layer with its input norm and residual")
+    ap.add_argument("--norm", action="store_true",
+                    help="each layer with its input norm and residual (the default stack, or --decode)")
     ap.add_argument("--config", type=int, choices=[3, 5], help="benchmark config 3 or 5 (one GPU) instead")
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tc"], help="expert path of --decode")
     ap.add_argument("--batches", type=int, nargs="+", default=[1, 4, 16, 64], help="decode batches of --decode")
@@ -521,6 +522,10 @@ def main() -> None:
         block.set_weights(layer, gate=gate.data_ptr(), up=up.data_ptr(), down=down.data_ptr(),
                           router=router.data_ptr(), qtype=QTYPE)
         del gate, up, down, router
+        if args.norm:  # (each layer with its input norm and residual: the reference's MoE layer in its decoder)
+            wn = 1.0 + 0.1 * torch.randn((H,), generator=g, device=dev)
+            block.set_norm(layer, wn.data_ptr(), eps=1e-6, dtype="F32")
+            del wn
     torch.cuda.empty_cache()
     if world > 1:
         from artlite_b200.moe.block import ep_unique_id
@@ -686,7 +691,8 @@ def main() -> None:
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded torch CUDA generator: Q4_0 d=|N(0,0.02)| fp16, nibbles uniform; x bf16 N(0,1))",
-            "config": {"workload": WORKLOAD, "layers": L, "tokens": T * world, "tokens_per_rank": T, "hidden": H,
+            "config": {"workload": WORKLOAD + ("-norm" if args.norm else ""), "layers": L, "tokens": T * world,
+                       "tokens_per_rank": T, "hidden": H,
                        "experts": E, "top_k": K, "expert_ffn": F, "qtype": QTYPE, "path": path,
                        "parallelism": f"ep{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (340 MB of weights streamed per layer)"},
