@@ -125,13 +125,15 @@ int launch_combine(const void* y, int y_dtype, const int32_t* slot, const float*
                     out_dtype, own, sh, res);
 }
 
-// the layer's input norm as its own pass (norm.cuh): four rows a CTA (their loads, sums and reductions interleaved)
-__global__ void __launch_bounds__(256) norm_kernel(const void* x, int x_dtype, const void* w, int w_dtype, double eps,
-                                                   int64_t T, int H, void* out) {
+// the layer's input norm as its own pass (norm.cuh): four rows a CTA (their loads, sums and reductions interleaved),
+// one instance per (x, w) dtype pair (a fixed pair takes fewer registers: 4 CTAs an SM instead of 3)
+template <int XD, int WD>
+__global__ void __launch_bounds__(256) norm_kernel(const void* x, const void* w, double eps, int64_t T, int H,
+                                                   void* out) {
   griddep_wait();
   griddep_launch();
   const int64_t r0 = (int64_t)blockIdx.x * 4;
-  nrm::norm_rows<4>(x, x_dtype, w, w_dtype, eps, H, r0, (int)min64(4, T - r0), out);
+  nrm::norm_rows<4>(x, XD, w, WD, eps, H, r0, (int)min64(4, T - r0), out);
 }
 
 int launch_norm(const void* x, int x_dtype, const void* w, int w_dtype, double eps, int64_t T, int H, void* out,
@@ -139,7 +141,12 @@ int launch_norm(const void* x, int x_dtype, const void* w, int w_dtype, double e
   AL_CHECK(H % 8 == 0, ARTLITE_EUNSUPPORTED, "norm: H %d (a multiple of 8)", H);
   AL_CHECK(w_dtype == ARTLITE_F32 || w_dtype == ARTLITE_BF16, ARTLITE_EINVAL, "norm: weight type %d", w_dtype);
   if (T == 0) return ARTLITE_OK;
-  return launch_pdl(norm_kernel, dim3((unsigned)cdiv(T, 4)), dim3(256), 0, st, x, x_dtype, w, w_dtype, eps, T, H, out);
+  const dim3 grid((unsigned)cdiv(T, 4));
+  const bool xb = x_dtype == ARTLITE_BF16, wb = w_dtype == ARTLITE_BF16;
+  if (xb && !wb) return launch_pdl(norm_kernel<ARTLITE_BF16, ARTLITE_F32>, grid, dim3(256), 0, st, x, w, eps, T, H, out);
+  if (xb && wb) return launch_pdl(norm_kernel<ARTLITE_BF16, ARTLITE_BF16>, grid, dim3(256), 0, st, x, w, eps, T, H, out);
+  if (wb) return launch_pdl(norm_kernel<ARTLITE_F32, ARTLITE_BF16>, grid, dim3(256), 0, st, x, w, eps, T, H, out);
+  return launch_pdl(norm_kernel<ARTLITE_F32, ARTLITE_F32>, grid, dim3(256), 0, st, x, w, eps, T, H, out);
 }
 
 // a grid-stride loop over 16-byte chunks of the output rows (8 values each): row i of xp = token perm[i] / k of x
