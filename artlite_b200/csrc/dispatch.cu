@@ -28,8 +28,12 @@ __device__ __forceinline__ int64_t blk_pairs(const DispatchArgs& a) {
   return a.blk_pairs ? a.blk_pairs : kDispatchBlockPairs;
 }
 
+// (the dispatch kernels are programmatic dependents, each of the kernel before it: every one waits for that kernel's
+// end before it reads or writes anything)
 __global__ void __launch_bounds__(512) dispatch_count(DispatchArgs a) {
   extern __shared__ int32_t hist[];
+  griddep_wait();
+  griddep_launch();
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
   const int64_t p0 = (int64_t)blockIdx.x * blk_pairs(a);
@@ -51,6 +55,8 @@ __global__ void __launch_bounds__(1024) dispatch_scan(DispatchArgs a, int nblk) 
   __shared__ int64_t s64[32];
   __shared__ int32_t s32[32];
   __shared__ int64_t seg[1024];
+  griddep_wait();
+  griddep_launch();
   const int Ep = (a.E + 31) & ~31, nseg = blockDim.x / Ep;
   const int e = threadIdx.x % Ep, sg = threadIdx.x / Ep;
   const int per = (nblk + nseg - 1) / nseg, b0 = min(nblk, sg * per), b1 = min(nblk, b0 + per);
@@ -101,6 +107,8 @@ __global__ void __launch_bounds__(1024) dispatch_scan(DispatchArgs a, int nblk) 
 
 __global__ void __launch_bounds__(256) dispatch_rank(DispatchArgs a) {
   extern __shared__ int32_t sm[];
+  griddep_wait();
+  griddep_launch();
   int32_t* wc = sm;              // [8][E] per-warp counts of the current round
   int32_t* run = sm + 8 * a.E;   // [E] pairs of this block placed so far
   for (int i = threadIdx.x; i < 9 * a.E; i += blockDim.x) sm[i] = 0;
@@ -139,19 +147,11 @@ __global__ void __launch_bounds__(256) dispatch_rank(DispatchArgs a) {
 int launch_dispatch(const DispatchArgs& a, cudaStream_t st) {
   AL_CHECK(a.E >= 1 && a.E <= 1024, ARTLITE_EUNSUPPORTED, "dispatch: E %d (this build: E <= 1024)", a.E);
   const int nblk = a.P ? (int)cdiv(a.P, a.blk_pairs ? a.blk_pairs : kDispatchBlockPairs) : 0;
-  if (nblk) {
-    dispatch_count<<<nblk, 512, a.E * sizeof(int32_t), st>>>(a);
-    AL_LAUNCHED();
-  }
+  if (nblk) AL_TRY(launch_pdl(dispatch_count, dim3(nblk), dim3(512), a.E * sizeof(int32_t), st, a));
   const int Ep = (int)cdiv(a.E, 32) * 32;
   const int nseg = std::max(1, std::min(1024 / Ep, nblk));
-  dispatch_scan<<<1, Ep * nseg, 0, st>>>(a, nblk);
-  AL_LAUNCHED();
-  if (nblk) {
-    const size_t smem = 9 * (size_t)a.E * sizeof(int32_t);
-    dispatch_rank<<<nblk, 256, smem, st>>>(a);
-    AL_LAUNCHED();
-  }
+  AL_TRY(launch_pdl(dispatch_scan, dim3(1), dim3(Ep * nseg), 0, st, a, nblk));
+  if (nblk) AL_TRY(launch_pdl(dispatch_rank, dim3(nblk), dim3(256), 9 * (size_t)a.E * sizeof(int32_t), st, a));
   return ARTLITE_OK;
 }
 
@@ -264,6 +264,8 @@ namespace artlite {
 __global__ void __launch_bounds__(1024) unit_scan_kernel(const int32_t* counts, int E, int unit_rows, int mult,
                                                          int32_t* out) {
   __shared__ int32_t s32[32];
+  griddep_wait();
+  griddep_launch();
   const int e = threadIdx.x;
   const int32_t u = e < E ? (counts[e] + unit_rows - 1) / unit_rows * mult : 0;
   int32_t tot;
@@ -274,9 +276,8 @@ __global__ void __launch_bounds__(1024) unit_scan_kernel(const int32_t* counts, 
 
 int launch_unit_scan(const int32_t* counts, int E, int unit_rows, int mult, int32_t* out, cudaStream_t st) {
   AL_CHECK(E >= 1 && E <= 1024 && unit_rows > 0, ARTLITE_EUNSUPPORTED, "unit scan: E %d", E);
-  unit_scan_kernel<<<1, (unsigned)cdiv(E, 32) * 32, 0, st>>>(counts, E, unit_rows, mult, out);
-  AL_LAUNCHED();
-  return ARTLITE_OK;
+  return launch_pdl(unit_scan_kernel, dim3(1), dim3((unsigned)cdiv(E, 32) * 32), 0, st, counts, E, unit_rows, mult,
+                    out);
 }
 
 }  // namespace artlite

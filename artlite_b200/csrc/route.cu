@@ -29,14 +29,13 @@ int launch_route(const RouteArgs& a, cudaStream_t st) {
   const int warps = 8;
   const unsigned grid = (unsigned)cdiv(a.n, warps);
   const int J = (a.E + 31) / 32;
-  if (J <= 1) route_kernel<1><<<grid, warps * 32, 0, st>>>(a);
-  else if (J <= 2) route_kernel<2><<<grid, warps * 32, 0, st>>>(a);
-  else if (J <= 4) route_kernel<4><<<grid, warps * 32, 0, st>>>(a);
-  else if (J <= 8) route_kernel<8><<<grid, warps * 32, 0, st>>>(a);
-  else if (J <= 16) route_kernel<16><<<grid, warps * 32, 0, st>>>(a);
-  else route_kernel<32><<<grid, warps * 32, 0, st>>>(a);
-  AL_LAUNCHED();
-  return ARTLITE_OK;
+  const dim3 g(grid), b(warps * 32);
+  if (J <= 1) return launch_pdl(route_kernel<1>, g, b, 0, st, a);
+  if (J <= 2) return launch_pdl(route_kernel<2>, g, b, 0, st, a);
+  if (J <= 4) return launch_pdl(route_kernel<4>, g, b, 0, st, a);
+  if (J <= 8) return launch_pdl(route_kernel<8>, g, b, 0, st, a);
+  if (J <= 16) return launch_pdl(route_kernel<16>, g, b, 0, st, a);
+  return launch_pdl(route_kernel<32>, g, b, 0, st, a);
 }
 
 int check_route_args(int64_t n, int per_col, int E, int k) {
